@@ -1,0 +1,354 @@
+#!/usr/bin/env python
+"""Benchmark of the hot path: the attention block of the NF4 QLoRA step, forward + backward.
+
+One step = one pass of the block over one packed batch per GPU: NF4 double-quant dequant of
+W_q/W_k/W_v + q/k/v GEMMs with bias + LoRA r=16 (alpha 32) on q and v + RoPE + packed varlen causal
+GQA attention, then the backward (attention, RoPE, LoRA A/B grads, the projections' input
+gradient), then, on N > 1 GPUs, the NCCL all-reduce of the LoRA gradients (data-parallel by whole
+packed sequences). Shapes: Qwen2.5-1.5B layer (hidden 1536, 12 q / 2 kv heads, head_dim 128).
+Packing: config 3 of the baseline, 16,384 tokens per GPU, row lengths uniform in [64, 4096].
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0). ``value`` is whole-job tokens/s with inputs resident in HBM;
+``e2e`` is the same step with the inputs copied from pinned host memory and the LoRA gradients
+read back inside the timed region; ``roofline`` is the varlen attention kernels (forward +
+backward) timed live with CUDA events inside the timed steps, against the measured bf16 peak.
+``--impl reference`` times the reference's CPU path (the oracle's torch fp32 port of
+solution/nf4.py + attn.py + varlen.py PackedSDPA) on a bounded sample, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "QLoRA step tokens/s at 1/2/4/8 B200; varlen attn fwd+bwd TFLOP/s vs BF16 peak"
+HIDDEN, HQ, HK, D = 1536, 12, 2, 128
+TOKENS = 16384
+WORKLOAD = ("attention block fwd+bwd of one Qwen2.5-1.5B QLoRA layer (NF4 dq q/k/v + bias, "
+            "LoRA r16 q,v, RoPE, varlen causal GQA attention) over config-3 packing")
+
+
+def lengths_for(seed: int, total: int = TOKENS, lo: int = 64, hi: int = 4096) -> list[int]:
+    """Row lengths uniform in [lo, hi], packed greedily to ``total`` tokens (last row truncated)."""
+    rng = np.random.default_rng(seed)
+    out, t = [], 0
+    while t < total:
+        L = int(min(rng.integers(lo, hi + 1), total - t))
+        out.append(L)
+        t += L
+    return out
+
+
+def causal_flops(lengths, n_heads=HQ, head_dim=D) -> float:
+    return 4.0 * head_dim * n_heads * sum(L * (L + 1) // 2 for L in lengths)
+
+
+def peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"bf16_tflops": float(p["bf16_tflops"]), "hbm_gbs": float(p["hbm_gbs"]),
+                "source": "MEASURED_PEAKS.json (measured; bf16 burst)"}
+    except Exception:
+        return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback (earlier pool measurement)"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        with open(self.file.name) as f:
+            rows = [r.strip().split(", ") for r in f if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0):
+    """Times the reference's CPU path (oracle.block, torch fp32) on the first rows of the packing,
+    ``sample_tokens`` tokens (last row truncated). Returns (tokens/s, sample description, threads)."""
+    from decik_b200.nf4_quant import quantize_nf4
+    from oracle import block as ob
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows, t = [], 0
+    for L in lengths:
+        if t >= sample_tokens:
+            break
+        L = min(L, sample_tokens - t)
+        rows.append(L)
+        t += L
+    spans, s = [], 0
+    for L in rows:
+        spans.append((s, L))
+        s += L
+    T = s
+    rng = np.random.default_rng(seed)
+    g = torch.Generator().manual_seed(seed)
+    inputs = dict(x=torch.randn(T, HIDDEN, generator=g), spans=spans, n_heads=HQ, n_kv=HK, scaling=2.0)
+    for name, n_out in (("q", HQ * D), ("k", HK * D), ("v", HK * D)):
+        inputs[f"nf4_{name}"] = quantize_nf4((rng.standard_normal((n_out, HIDDEN)) * 0.02).astype(np.float32))
+        inputs[f"b_{name}"] = torch.randn(n_out, generator=g) * 0.02
+    inputs.update(a_q=torch.randn(16, HIDDEN, generator=g) * 0.02, bb_q=torch.randn(HQ * D, 16, generator=g) * 0.02,
+                  a_v=torch.randn(16, HIDDEN, generator=g) * 0.02, bb_v=torch.randn(HK * D, 16, generator=g) * 0.02)
+    pos = torch.cat([torch.arange(L) for L in rows]).float()
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2).float() / D))
+    fr = torch.outer(pos, inv)
+    emb = torch.cat((fr, fr), -1)
+    inputs["cos"], inputs["sin"] = emb.cos(), emb.sin()
+    grad = torch.randn(T, HQ * D, generator=g)
+    times = []
+    for _ in range(n_steps):
+        t0 = time.perf_counter()
+        ob.block_step(inputs, grad)
+        times.append(time.perf_counter() - t0)
+    desc = f"{len(rows)} rows, {T} tokens (first rows of the packing), fwd+bwd incl. NF4 dequant, fp32"
+    return T / statistics.mean(times), desc, threads, times
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    lengths = lengths_for(1000)
+    sample = args.ref_tokens
+    # warm-up steps (untimed), then K timed steps, each one bounded sample of the workload
+    if args.warmup:
+        cpu_reference_steps(lengths, min(args.warmup, 1), sample)
+    value, desc, threads, times = cpu_reference_steps(lengths, args.steps, sample)
+    line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * statistics.mean(times), 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD + " (bounded CPU sample)", "tokens_per_gpu": TOKENS,
+                       "sample": desc, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    from decik_b200 import ops
+    from decik_b200.block import QLoRAAttentionBlock, rope_cos_sin
+    from decik_b200.solution.varlen import packing_from_lengths
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    block = QLoRAAttentionBlock.random(seed=0, device=dev)          # replicated frozen weights + LoRA
+    lengths = lengths_for(1000 + rank)                                # each rank its own sequences
+    T = sum(lengths)
+    packing = packing_from_lengths(lengths, dev)
+    cos, sin = rope_cos_sin(packing.positions, D)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    x = torch.randn(T, HIDDEN, device=dev, generator=g).requires_grad_(True)
+    dout = torch.randn(T, HQ * D, device=dev, generator=g).to(torch.bfloat16)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    params = block.lora_params()
+    grad_buf = torch.empty(sum(p.numel() for p in params), dtype=torch.float32, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+    def step(xin, din):
+        for p in params:
+            p.grad = None
+        xin.grad = None
+        out = block.forward(xin, packing, cos, sin)
+        out.backward(din)
+        if world > 1:  # data-parallel exchange: one flat all-reduce of the LoRA grads
+            torch.cat([p.grad.reshape(-1) for p in params], out=grad_buf)
+            dist.all_reduce(grad_buf)
+        return out
+
+    for _ in range(args.warmup):
+        step(x, dout)
+    torch.cuda.synchronize()
+
+    def timed(n, fn):
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(n):
+            flush.zero_()                      # L2 flushed between timed steps (not timed)
+            starts[i].record()
+            fn()
+            ends[i].record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        return [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+    timer = ops.OpTimer()
+    ops.install_timer(timer)
+    with ClockSampler(local) as clocks:
+        step_ms = timed(args.steps, lambda: step(x, dout))
+    ops.install_timer(None)
+    op_ms = timer.elapsed_ms()
+    launches = timer.launches
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = world * T * args.steps / (total_ms / 1e3)
+
+    # end to end through the same public API, inputs from pinned host memory, LoRA grads read back
+    x_host = x.detach().cpu().pin_memory()
+    d_host = dout.cpu().pin_memory()
+    g_host = torch.empty(grad_buf.numel(), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x.detach())
+    d_dev = torch.empty_like(dout)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        d_dev.copy_(d_host, non_blocking=True)
+        xin = x_dev.detach().requires_grad_(True)
+        step(xin, d_dev)
+        if world == 1:
+            torch.cat([p.grad.reshape(-1) for p in params], out=grad_buf)
+        g_host.copy_(grad_buf, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms = sum(timed(args.steps, e2e_step))
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+
+    if rank != 0:
+        return
+    pk = peaks()
+    f_fwd = causal_flops(lengths)
+    fwd_ms = statistics.mean(op_ms.get("varlen_attn_fwd", [float("nan")]))
+    bwd_ms = statistics.mean(op_ms.get("varlen_attn_bwd", [float("nan")]))
+    attn_tflops = 3.0 * f_fwd / ((fwd_ms + bwd_ms) / 1e3) / 1e12
+    kernels = {name: {"ms_mean": round(statistics.mean(v), 4), "calls_per_step": len(v) // max(args.steps, 1)}
+               for name, v in op_ms.items()}
+    kernels["varlen_attn_fwd"]["tflops"] = round(f_fwd / (fwd_ms / 1e3) / 1e12, 2)
+    kernels["varlen_attn_bwd"]["tflops"] = round(2 * f_fwd / (bwd_ms / 1e3) / 1e12, 2)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded lengths, N(0,1) activations, random-init NF4/LoRA weights)",
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "rows_rank0": len(lengths),
+                   "lengths": "U[64,4096], numpy default_rng(1000 + rank)", "hidden": HIDDEN,
+                   "heads": f"{HQ}/{HK}", "head_dim": D, "lora": "r16 alpha32 q,v", "nf4": "bs64, double quant bs256",
+                   "l2": "flushed between timed steps (256 MiB write, untimed)", "parallelism": f"dp{world}"},
+        "roofline": {"bound": "tensor", "kernel": "varlen attention fwd+bwd (decik_varlen_attn_fwd/bwd)",
+                     "achieved": round(attn_tflops, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(attn_tflops / pk["bf16_tflops"], 4), "traffic": None,
+                     "flops_per_step": 3.0 * f_fwd, "peak_source": pk["source"]},
+        "attn_tflops": round(attn_tflops, 2),
+        "kernels": kernels,
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": x_host.numel() * 4 + d_host.numel() * 2,
+                "d2h_bytes_per_step": g_host.numel() * 4},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cv, desc, threads, _ = cpu_reference_steps(lengths, 1, args.ref_tokens)
+        line["cpu_baseline"] = {"value": round(cv, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": desc}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ref-tokens", type=int, default=4096, help="tokens of the bounded CPU sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

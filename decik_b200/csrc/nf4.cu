@@ -1,0 +1,172 @@
+// NF4 double-quant dequant, bit-exact with the reference's skc_nf4_dequant_kernel
+// (solution/nf4.py:28-49) and so with bitsandbytes' dequantize_4bit.
+//
+// HBM-bound: per weight 0.5 B of nibbles + 1/blocksize B of absmax (+ fp32 absmax2 every
+// blocksize*blocksize2 weights) are read and 2 B (fp16/bf16) written. Each thread takes 16
+// packed bytes (one 16-byte load, 32 weights) per step of a grid-stride loop sized to the SM
+// count, and writes 64 bytes with 16-byte stores. The 16 / 256-entry code tables sit in shared
+// memory. Products and sums use __fmul_rn / __fadd_rn so that nothing is contracted to an FMA:
+// scale = code2[q] * absmax2 then + offset (two roundings), w = code[nibble] * scale.
+#include "common.cuh"
+
+namespace decik {
+namespace {
+
+template <typename OutT>
+struct Store32;  // writes 32 fp32 weights as OutT
+
+template <>
+struct Store32<float> {
+  static __device__ __forceinline__ void run(float* out, const float (&w)[32]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      reinterpret_cast<float4*>(out)[i] = make_float4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  }
+};
+
+template <typename T>
+struct Store32 {
+  static __device__ __forceinline__ void run(T* out, const float (&w)[32]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 v;
+      v.x = Dt<T>::pack2(w[8 * i + 0], w[8 * i + 1]);
+      v.y = Dt<T>::pack2(w[8 * i + 2], w[8 * i + 3]);
+      v.z = Dt<T>::pack2(w[8 * i + 4], w[8 * i + 5]);
+      v.w = Dt<T>::pack2(w[8 * i + 6], w[8 * i + 7]);
+      reinterpret_cast<uint4*>(out)[i] = v;
+    }
+  }
+};
+
+template <typename OutT>
+__device__ __forceinline__ OutT cvt_out(float x);
+template <> __device__ __forceinline__ float cvt_out<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half cvt_out<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+struct Nf4Args {
+  const uint8_t* packed;
+  const void* absmax;
+  const float* absmax2;
+  const float* code2;
+  const float* offset;
+  const float* code;
+  int64_t n_bytes;
+  int blocksize;
+  int blocksize2;
+};
+
+template <bool NESTED>
+__device__ __forceinline__ float block_scale(const Nf4Args& a, const float* s_code2, float offset,
+                                             int64_t block) {
+  if (NESTED) {
+    const uint8_t q = __ldg(reinterpret_cast<const uint8_t*>(a.absmax) + block);
+    const float s = __fmul_rn(s_code2[q], __ldg(a.absmax2 + block / a.blocksize2));
+    return __fadd_rn(s, offset);
+  }
+  return __ldg(reinterpret_cast<const float*>(a.absmax) + block);
+}
+
+// VEC: 16 bytes per step (needs 16-byte aligned packed and out). Otherwise one byte per step.
+template <typename OutT, bool NESTED, bool VEC>
+__global__ void __launch_bounds__(256) nf4_dequant_kernel(Nf4Args a, OutT* __restrict__ out) {
+  __shared__ float s_code[16];
+  __shared__ float s_code2[256];
+  if (threadIdx.x < 16) s_code[threadIdx.x] = a.code[threadIdx.x];
+  if (NESTED) s_code2[threadIdx.x] = a.code2[threadIdx.x];  // blockDim.x == 256
+  __syncthreads();
+  const float offset = NESTED ? __ldg(a.offset) : 0.f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (VEC) {
+    const int64_t n_chunks = a.n_bytes >> 4;
+    for (int64_t c = tid; c < n_chunks; c += stride) {
+      const uint4 raw = ldg16(a.packed + (c << 4));
+      const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+      float w[32];
+      const int64_t first = (c << 5) / a.blocksize;         // block of weight 32c
+      const int64_t last = ((c << 5) + 31) / a.blocksize;   // block of weight 32c + 31
+      if (first == last) {  // the whole chunk in one absmax block (blocksize >= 32)
+        const float scale = block_scale<NESTED>(a, s_code2, offset, first);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t b = (words[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+          w[2 * j] = __fmul_rn(s_code[b >> 4], scale);
+          w[2 * j + 1] = __fmul_rn(s_code[b & 15u], scale);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int64_t block = (((c << 4) + j) * 2) / a.blocksize;
+          const float scale = block_scale<NESTED>(a, s_code2, offset, block);
+          const uint32_t b = (words[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
+          w[2 * j] = __fmul_rn(s_code[b >> 4], scale);
+          w[2 * j + 1] = __fmul_rn(s_code[b & 15u], scale);
+        }
+      }
+      Store32<OutT>::run(out + (c << 5), w);
+    }
+    // tail bytes (n_bytes % 16) by the first threads
+    const int64_t tail0 = n_chunks << 4;
+    for (int64_t i = tail0 + tid; i < a.n_bytes; i += stride) {
+      const uint32_t b = a.packed[i];
+      const float scale = block_scale<NESTED>(a, s_code2, offset, (i * 2) / a.blocksize);
+      out[2 * i] = cvt_out<OutT>(__fmul_rn(s_code[b >> 4], scale));
+      out[2 * i + 1] = cvt_out<OutT>(__fmul_rn(s_code[b & 15u], scale));
+    }
+  } else {
+    for (int64_t i = tid; i < a.n_bytes; i += stride) {
+      const uint32_t b = a.packed[i];
+      const float scale = block_scale<NESTED>(a, s_code2, offset, (i * 2) / a.blocksize);
+      out[2 * i] = cvt_out<OutT>(__fmul_rn(s_code[b >> 4], scale));
+      out[2 * i + 1] = cvt_out<OutT>(__fmul_rn(s_code[b & 15u], scale));
+    }
+  }
+}
+
+template <typename OutT>
+int launch(const Nf4Args& a, void* out, bool nested, cudaStream_t stream) {
+  const bool vec = aligned16(a.packed) && aligned16(out);
+  const int64_t work = vec ? (a.n_bytes >> 4) + 1 : a.n_bytes;
+  const int64_t want = (work + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
+  const int grid = static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
+  OutT* o = reinterpret_cast<OutT*>(out);
+  if (nested) {
+    if (vec) nf4_dequant_kernel<OutT, true, true><<<grid, 256, 0, stream>>>(a, o);
+    else nf4_dequant_kernel<OutT, true, false><<<grid, 256, 0, stream>>>(a, o);
+  } else {
+    if (vec) nf4_dequant_kernel<OutT, false, true><<<grid, 256, 0, stream>>>(a, o);
+    else nf4_dequant_kernel<OutT, false, false><<<grid, 256, 0, stream>>>(a, o);
+  }
+  return check_launch("nf4_dequant");
+}
+
+}  // namespace
+}  // namespace decik
+
+extern "C" int decik_nf4_dequant(const uint8_t* packed, const void* absmax, const float* absmax2,
+                                 const float* code2, const float* offset, const float* code,
+                                 void* out, int64_t n_bytes, int nested, int blocksize,
+                                 int blocksize2, int out_dtype, void* stream) {
+  using namespace decik;
+  if (n_bytes < 0) return set_error(DECIK_ERR_INVALID, "nf4_dequant: n_bytes < 0");
+  if (n_bytes == 0) return DECIK_OK;
+  if (!packed || !absmax || !code || !out)
+    return set_error(DECIK_ERR_INVALID, "nf4_dequant: null pointer");
+  if (blocksize <= 0 || blocksize % 2 != 0)
+    return set_error(DECIK_ERR_INVALID, "nf4_dequant: blocksize %d must be even and > 0", blocksize);
+  if (nested && (!absmax2 || !code2 || !offset || blocksize2 <= 0))
+    return set_error(DECIK_ERR_INVALID, "nf4_dequant: nested needs absmax2, code2, offset, blocksize2");
+  Nf4Args a{packed, absmax, absmax2, code2, offset, code, n_bytes, blocksize, blocksize2};
+  cudaStream_t s = as_stream(stream);
+  switch (out_dtype) {
+    case DECIK_F16: return launch<__half>(a, out, nested != 0, s);
+    case DECIK_BF16: return launch<__nv_bfloat16>(a, out, nested != 0, s);
+    case DECIK_F32: return launch<float>(a, out, nested != 0, s);
+    default: return set_error(DECIK_ERR_INVALID, "nf4_dequant: out_dtype %d", out_dtype);
+  }
+}

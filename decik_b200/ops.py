@@ -1,0 +1,269 @@
+"""Torch-tensor front end of the C ABI: each function checks its tensors, allocates the outputs
+with the PyTorch caching allocator and enqueues the kernels on the current CUDA stream.
+
+These are the operators the reference-facing modules in ``decik_b200.solution`` call. They run
+only on CUDA tensors; anything else raises (there is no CPU fallback).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import BF16, F16, F32, Tensor3
+
+_DT = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise RuntimeError(f"decik_b200: unsupported dtype {t.dtype}") from None
+
+
+def _cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("decik_b200: tensors must be on a CUDA device (no CPU fallback)")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _p(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ------------------------------------------------------------------------------------------------
+# NF4
+# ------------------------------------------------------------------------------------------------
+def nf4_dequant(packed: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, shape,
+                blocksize: int, absmax2: torch.Tensor | None = None, code2: torch.Tensor | None = None,
+                offset: torch.Tensor | None = None, blocksize2: int = 256,
+                out_dtype: torch.dtype = torch.float16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[N, K] weights from packed NF4 (solution/nf4.py:66-85). ``nested`` iff absmax is uint8."""
+    nested = absmax.dtype == torch.uint8
+    _cuda(packed, absmax, code, absmax2, code2, offset)
+    n_out, n_in = int(shape[0]), int(shape[1])
+    n_bytes = n_out * n_in // 2
+    if packed.numel() < n_bytes:
+        raise RuntimeError("decik_b200 nf4_dequant: packed tensor smaller than shape")
+    if out is None:
+        out = torch.empty((n_out, n_in), dtype=out_dtype, device=packed.device)
+    with _timed("nf4_dequant", 1):
+        rc = _lib.lib().decik_nf4_dequant(
+            _p(packed), _p(absmax), _p(absmax2) if nested else None, _p(code2) if nested else None,
+            _p(offset) if nested else None, _p(code), _p(out), n_bytes, int(nested), int(blocksize),
+            int(blocksize2), _dt(out), _stream(packed))
+    _lib.check(rc, "nf4_dequant")
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+# RoPE
+# ------------------------------------------------------------------------------------------------
+def rope_fwd(q_base: torch.Tensor, q_lora: torch.Tensor | None, k: torch.Tensor, cos: torch.Tensor,
+             sin: torch.Tensor, n_heads: int, n_kv: int):
+    """q_base, q_lora [T, Hq*D], k [T, Hk*D] (contiguous, fp16/bf16), cos/sin fp32 [T, D] ->
+    q [Hq, T, D], k [Hk, T, D] (solution/attn.py:97-111)."""
+    _cuda(q_base, q_lora, k, cos, sin)
+    T = q_base.shape[0]
+    D = cos.shape[-1]
+    for t in (q_base, q_lora, k, cos, sin):
+        if t is not None and not t.is_contiguous():
+            raise RuntimeError("decik_b200 rope_fwd: inputs must be contiguous")
+    q_out = torch.empty((n_heads, T, D), dtype=q_base.dtype, device=q_base.device)
+    k_out = torch.empty((n_kv, T, D), dtype=q_base.dtype, device=q_base.device)
+    with _timed("rope_fwd", 1):
+        rc = _lib.lib().decik_rope_fwd(_p(q_base), _p(q_lora), _p(k), _p(cos), _p(sin), _p(q_out),
+                                       _p(k_out), T, n_heads, n_kv, D, _dt(q_base), _stream(q_base))
+    _lib.check(rc, "rope_fwd")
+    return q_out, k_out
+
+
+def rope_bwd(grad_q: torch.Tensor, grad_k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
+    """grad_q [Hq, T, D], grad_k [Hk, T, D] -> dq [T, Hq*D], dk [T, Hk*D] (solution/attn.py:113-126)."""
+    _cuda(grad_q, grad_k, cos, sin)
+    grad_q = grad_q.contiguous()
+    grad_k = grad_k.contiguous()
+    Hq, T, D = grad_q.shape
+    Hk = grad_k.shape[0]
+    dq = torch.empty((T, Hq * D), dtype=grad_q.dtype, device=grad_q.device)
+    dk = torch.empty((T, Hk * D), dtype=grad_q.dtype, device=grad_q.device)
+    with _timed("rope_bwd", 1):
+        rc = _lib.lib().decik_rope_bwd(_p(grad_q), _p(grad_k), _p(cos.contiguous()), _p(sin.contiguous()),
+                                       _p(dq), _p(dk), T, Hq, Hk, D, _dt(grad_q), _stream(grad_q))
+    _lib.check(rc, "rope_bwd")
+    return dq, dk
+
+
+# ------------------------------------------------------------------------------------------------
+# LoRA dropout helpers
+# ------------------------------------------------------------------------------------------------
+def keep_pack(keep_q: torch.Tensor, keep_v: torch.Tensor):
+    _cuda(keep_q, keep_v)
+    n, w = keep_q.shape
+    kq = keep_q.contiguous().view(torch.uint8)
+    kv = keep_v.contiguous().view(torch.uint8)
+    bq = torch.empty((n, w // 8), dtype=torch.uint8, device=keep_q.device)
+    bv = torch.empty_like(bq)
+    _lib.check(_lib.lib().decik_keep_pack(_p(kq), _p(kv), _p(bq), _p(bv), n, w, _stream(kq)), "keep_pack")
+    return bq, bv
+
+
+def lora_inputs(x: torch.Tensor, bits_q, bits_v, scale_q, scale_v, out_dtype=torch.float16):
+    _cuda(x, bits_q, bits_v, scale_q, scale_v)
+    w = x.shape[-1]
+    x2 = x.reshape(-1, w).contiguous()
+    n = x2.shape[0]
+    xq = torch.empty((n, w), dtype=out_dtype, device=x.device)
+    xv = torch.empty_like(xq)
+    sq = scale_q.reshape(1).to(torch.float32).contiguous()
+    sv = scale_v.reshape(1).to(torch.float32).contiguous()
+    rc = _lib.lib().decik_lora_inputs(_p(x2), _p(bits_q), _p(bits_v), _p(sq), _p(sv), _p(xq), _p(xv),
+                                      n, w, _dt(xq), _stream(x))
+    _lib.check(rc, "lora_inputs")
+    return xq, xv
+
+
+def lora_input_grad(g_q, g_v, bits_q, bits_v, scale_q: float, scale_v: float):
+    _cuda(g_q, g_v, bits_q, bits_v)
+    w = g_q.shape[-1]
+    gq = g_q.reshape(-1, w).contiguous()
+    gv = g_v.reshape(-1, w).to(gq.dtype).contiguous()
+    n = gq.shape[0]
+    out = torch.empty((n, w), dtype=torch.float32, device=g_q.device)
+    rc = _lib.lib().decik_lora_input_grad(_p(gq), _p(gv), _p(bits_q), _p(bits_v), _p(out), n, w,
+                                          float(scale_q), float(scale_v), _dt(gq), _stream(gq))
+    _lib.check(rc, "lora_input_grad")
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+# RMSNorm
+# ------------------------------------------------------------------------------------------------
+def rmsnorm_fwd(x2: torch.Tensor, w: torch.Tensor, eps: float, want_rstd: bool = True):
+    _cuda(x2, w)
+    n, c = x2.shape
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    y = torch.empty((n, c), dtype=torch.float32, device=x2.device)
+    rstd = torch.empty(n, dtype=torch.float32, device=x2.device) if want_rstd else None
+    rc = _lib.lib().decik_rmsnorm_fwd(_p(x2), _p(w.contiguous()), _dt(w), _p(y), _p(rstd), n, c,
+                                      x2.stride(0), y.stride(0), float(eps), _stream(x2))
+    _lib.check(rc, "rmsnorm_fwd")
+    return y, rstd
+
+
+def rmsnorm_bwd(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor, rstd: torch.Tensor):
+    _cuda(dy2, x2, w, rstd)
+    n, c = x2.shape
+    dy2 = dy2.contiguous()
+    x2 = x2.contiguous()
+    dx = torch.empty((n, c), dtype=torch.float32, device=x2.device)
+    rc = _lib.lib().decik_rmsnorm_bwd(_p(dy2), _p(x2), _p(w.contiguous()), _dt(w), _p(rstd), _p(dx), n, c,
+                                      _stream(x2))
+    _lib.check(rc, "rmsnorm_bwd")
+    return dx
+
+
+# ------------------------------------------------------------------------------------------------
+# varlen attention
+# ------------------------------------------------------------------------------------------------
+def _t3(t: torch.Tensor) -> Tensor3:
+    """A [T, H, D] view (last dim contiguous) -> decik_tensor3."""
+    if t.dim() != 3 or t.stride(2) != 1:
+        raise RuntimeError("decik_b200: attention tensors must be [T, H, D] views with D contiguous")
+    return Tensor3(t.data_ptr(), t.stride(0), t.stride(1))
+
+
+def varlen_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: torch.Tensor,
+                    max_len: int, scale: float, out: torch.Tensor | None = None):
+    """q [T, Hq, D], k/v [T, Hk, D] views -> out [T, Hq, D] (contiguous unless given), lse fp32 [Hq, T]."""
+    _cuda(q, k, v, cu_seqlens)
+    T, Hq, D = q.shape
+    Hk = k.shape[1]
+    if cu_seqlens.dtype != torch.int32:
+        raise RuntimeError("decik_b200 varlen_attn_fwd: cu_seqlens must be int32")
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=q.dtype, device=q.device)
+    lse = torch.empty((Hq, T), dtype=torch.float32, device=q.device)
+    with _timed("varlen_attn_fwd", 1):
+        rc = _lib.lib().decik_varlen_attn_fwd(_t3(q), _t3(k), _t3(v), _t3(out), _p(lse), _p(cu_seqlens),
+                                              cu_seqlens.numel() - 1, int(max_len), T, Hq, Hk, D,
+                                              float(scale), _dt(q), _stream(q))
+    _lib.check(rc, "varlen_attn_fwd")
+    return out, lse
+
+
+def varlen_attn_bwd_workspace(n_tok: int, n_heads: int, head_dim: int) -> int:
+    return int(_lib.lib().decik_varlen_attn_bwd_workspace(n_tok, n_heads, head_dim))
+
+
+def varlen_attn_bwd(dout, q, k, v, out, lse, cu_seqlens, max_len: int, scale: float,
+                    dq=None, dk=None, dv=None, workspace: torch.Tensor | None = None):
+    """Returns (dq, dk, dv) shaped and strided like q, k, v (dk/dv GQA-summed)."""
+    _cuda(dout, q, k, v, out, lse, cu_seqlens)
+    T, Hq, D = q.shape
+    Hk = k.shape[1]
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
+    nbytes = varlen_attn_bwd_workspace(T, Hq, D)
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    with _timed("varlen_attn_bwd", 3):
+        rc = _lib.lib().decik_varlen_attn_bwd(_t3(dout), _t3(q), _t3(k), _t3(v), _t3(out), _p(lse), _t3(dq),
+                                              _t3(dk), _t3(dv), _p(cu_seqlens), cu_seqlens.numel() - 1,
+                                              int(max_len), T, Hq, Hk, D, float(scale), _dt(q),
+                                              _p(workspace), _stream(q))
+    _lib.check(rc, "varlen_attn_bwd")
+    return dq, dk, dv
+
+
+# ------------------------------------------------------------------------------------------------
+# instrumentation (off unless a caller installs a recorder): CUDA events around named ops on the
+# stream they launch on, and a count of this library's kernel launches.
+# ------------------------------------------------------------------------------------------------
+class OpTimer:
+    """Records (name, start event, end event) around ops while installed with ``install``."""
+
+    def __init__(self):
+        self.events = []
+        self.launches = 0
+
+    def elapsed_ms(self) -> dict:
+        torch.cuda.synchronize()
+        out: dict = {}
+        for name, a, b in self.events:
+            out.setdefault(name, []).append(a.elapsed_time(b))
+        return out
+
+
+_timer: OpTimer | None = None
+
+
+def install_timer(t: OpTimer | None) -> None:
+    global _timer
+    _timer = t
+
+
+class _timed:
+    def __init__(self, name: str, launches: int):
+        self.name, self.launches = name, launches
+
+    def __enter__(self):
+        if _timer is not None:
+            self.a = torch.cuda.Event(enable_timing=True)
+            self.a.record()
+        return self
+
+    def __exit__(self, *exc):
+        if _timer is not None:
+            b = torch.cuda.Event(enable_timing=True)
+            b.record()
+            _timer.events.append((self.name, self.a, b))
+            _timer.launches += self.launches
+        return False

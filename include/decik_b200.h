@@ -1,0 +1,171 @@
+/*
+ * decik_b200: C ABI of the B200 (sm_100a) kernels for the attention block of decik's NF4 QLoRA
+ * training step.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (cudaStream_t passed as
+ * void*, NULL = the legacy default stream), enqueues its kernels on that stream and returns a
+ * status code. Nothing here allocates device memory: outputs and workspaces are the caller's.
+ * On a non-zero status, decik_last_error() returns a message for the calling thread.
+ *
+ * Layout conventions: "token-major" [T, H*D] means row t holds all heads of token t;
+ * "head-major" [H, T, D] means head h is one contiguous [T, D] block. Strides are in ELEMENTS.
+ * dtype codes: DECIK_F16, DECIK_BF16, DECIK_F32.
+ *
+ * Reference citations are paths inside the tokha-t/decik repository.
+ */
+#ifndef DECIK_B200_H
+#define DECIK_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DECIK_API __attribute__((visibility("default")))
+#else
+#define DECIK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DECIK_OK 0
+#define DECIK_ERR_INVALID 1      /* bad argument: size, alignment, dtype, null pointer */
+#define DECIK_ERR_CUDA 2         /* a CUDA runtime error while launching */
+#define DECIK_ERR_UNSUPPORTED 3  /* a shape or option this build has no kernel for */
+
+#define DECIK_F16 0
+#define DECIK_BF16 1
+#define DECIK_F32 2
+
+/* Message of the last failed call on this thread ("" if none). */
+DECIK_API const char* decik_last_error(void);
+
+/* ABI version of this library (bumped on any signature change). */
+DECIK_API int decik_abi_version(void);
+
+/* ---------------------------------------------------------------------------------------------
+ * NF4 double-quant dequant.
+ * Replaces solution/nf4.py:66-85 (dequantize_nf4) and its kernel skc_nf4_dequant_kernel
+ * (solution/nf4.py:28-49). Bit-exact: for packed byte i, the high nibble is weight 2i and the low
+ * nibble weight 2i+1; block = (2i) / blocksize; with nested=1 the block scale is
+ * code2[absmax_u8[block]] * absmax2[block / blocksize2] then + *offset (two fp32 roundings, no
+ * FMA); each weight is code[nibble] * scale in fp32, rounded to out_dtype (F16, BF16 or F32).
+ *   packed  uint8 [n_bytes]                 (row-major [N_out, K_in] weights, 2 per byte)
+ *   absmax  uint8 [n_blocks] if nested, else fp32 [n_blocks]
+ *   absmax2 fp32 [ceil(n_blocks / blocksize2)] (nested only, else may be NULL)
+ *   code2   fp32 [256] (nested only), offset fp32 [1] device scalar (nested only)
+ *   code    fp32 [16]
+ *   out     [2 * n_bytes] of out_dtype
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int decik_nf4_dequant(const uint8_t* packed, const void* absmax, const float* absmax2,
+                      const float* code2, const float* offset, const float* code, void* out,
+                      int64_t n_bytes, int nested, int blocksize, int blocksize2, int out_dtype,
+                      void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * LoRA add + RoPE + cast, forward. Replaces FusedQKRope.forward / skc_rope_fwd_kernel
+ * (solution/attn.py:28-61, :97-111). Bit-exact (each fp32 product and sum rounded, no FMA):
+ *   q = f32(q_base) + f32(q_lora);  q_out = q * cos + rotate_half(q) * sin
+ *   k_out = k * cos + rotate_half(k) * sin
+ *   q_base, q_lora  [T, n_heads*head_dim] token-major, dtype (q_lora may be NULL: no LoRA term)
+ *   k               [T, n_kv*head_dim] token-major, dtype
+ *   cos, sin        fp32 [T, head_dim]
+ *   q_out           [n_heads, T, head_dim] head-major, dtype;  k_out [n_kv, T, head_dim]
+ * dtype: DECIK_F16 or DECIK_BF16. head_dim % 16 == 0.
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int decik_rope_fwd(const void* q_base, const void* q_lora, const void* k, const float* cos,
+                   const float* sin, void* q_out, void* k_out, int64_t n_tok, int n_heads,
+                   int n_kv, int head_dim, int dtype, void* stream);
+
+/* RoPE backward. Replaces FusedQKRope.backward / skc_rope_bwd_kernel (solution/attn.py:64-90,
+ * :113-126): dq[d] = g[d]*cos[d] + (d < D/2 ? g[d+D/2]*sin[d+D/2] : -(g[d-D/2]*sin[d-D/2])).
+ *   grad_q [n_heads, T, head_dim] head-major, grad_k [n_kv, T, head_dim]  (dtype)
+ *   dq [T, n_heads*head_dim], dk [T, n_kv*head_dim] token-major (dtype)                        */
+DECIK_API int decik_rope_bwd(const void* grad_q, const void* grad_k, const float* cos, const float* sin,
+                   void* dq, void* dk, int64_t n_tok, int n_heads, int n_kv, int head_dim,
+                   int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * LoRA dropout helpers (p > 0 only).
+ * decik_keep_pack replaces skc_keep_pack_kernel / pack_keep (solution/attn.py:130-144, :195-203):
+ *   keep_q, keep_v bool (one byte 0/1) [n_rows, width] -> bits_q, bits_v uint8 [n_rows, width/8],
+ *   bit j of byte c = keep[8c + j]. width % 8 == 0.
+ * decik_lora_inputs replaces skc_lora_inputs_kernel / _lora_inputs (solution/attn.py:154-165,
+ *   :183-192): xq = round(x * (keep_q * scale_q)), xv likewise; x fp32 [n_rows, width];
+ *   scale_q, scale_v fp32 device scalars; xq, xv of out_dtype (F16/BF16).
+ * decik_lora_input_grad replaces skc_lora_input_grad_kernel (solution/attn.py:169-180):
+ *   out = (f32(g_q) * keep_q) * scale_q + (f32(g_v) * keep_v) * scale_v, fp32 [n_rows, width];
+ *   g_q, g_v of in_dtype (F16/BF16).
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int decik_keep_pack(const uint8_t* keep_q, const uint8_t* keep_v, uint8_t* bits_q,
+                    uint8_t* bits_v, int64_t n_rows, int width, void* stream);
+DECIK_API int decik_lora_inputs(const float* x, const uint8_t* bits_q, const uint8_t* bits_v,
+                      const float* scale_q, const float* scale_v, void* xq, void* xv,
+                      int64_t n_rows, int width, int out_dtype, void* stream);
+DECIK_API int decik_lora_input_grad(const void* g_q, const void* g_v, const uint8_t* bits_q,
+                          const uint8_t* bits_v, float* out, int64_t n_rows, int width,
+                          float scale_q, float scale_v, int in_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * RMSNorm (Qwen2RMSNorm), the producer of the LoRA input (norm_link recompute).
+ * Replaces skc_rmsnorm_fwd_kernel / skc_rmsnorm_bwd_kernel (solution/rmsnorm.py:17-45) and
+ * rmsnorm.recompute (:76-80): y = w * (x * rsqrt(mean(x^2) + eps)), fp32 rows.
+ *   x fp32 [n_rows, n_cols] (row stride stride_x), w of w_dtype (F32 or F16) [n_cols],
+ *   y fp32 (row stride stride_y), rstd fp32 [n_rows] (may be NULL).
+ * Backward: dx = rstd * (g - x * rstd^2 * mean(g * x)), g = dy * w. n_cols % 4 == 0, <= 8192.
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int decik_rmsnorm_fwd(const float* x, const void* w, int w_dtype, float* y, float* rstd,
+                      int64_t n_rows, int n_cols, int64_t stride_x, int64_t stride_y, float eps,
+                      void* stream);
+DECIK_API int decik_rmsnorm_bwd(const float* dy, const float* x, const void* w, int w_dtype,
+                      const float* rstd, float* dx, int64_t n_rows, int n_cols, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Packed (padding-free) varlen causal GQA attention.
+ * Replaces VarlenSDPA (solution/varlen.py:134-168), i.e. aten::_efficient_attention_forward /
+ * _backward over cu_seqlens with the 6x GQA expansion (_expand_kv, :124-131) and the
+ * dk/dv group sum (:165-167); same result as PackedSDPA (:85-121). Query head h reads kv head
+ * h / (n_heads / n_kv); row r spans tokens [cu_seqlens[r], cu_seqlens[r+1]); key j is visible to
+ * query i of the same row iff j <= i (top-left causal).
+ *
+ * Tensors are 3-D views [T, H, head_dim] given by (pointer, token stride, head stride) in
+ * elements; head_dim is contiguous. dtype F16 or BF16, head_dim == 128. Strides and pointers must
+ * be 16-byte aligned.
+ *   cu_seqlens int32 [n_rows + 1] (device), max_len = the longest row.
+ *   out [T, n_heads, D]; lse fp32 [n_heads, T] (natural-log logsumexp of the scaled scores).
+ * ------------------------------------------------------------------------------------------- */
+typedef struct {
+  const void* ptr;
+  int64_t tok_stride;
+  int64_t head_stride;
+} decik_tensor3;
+
+typedef struct {
+  void* ptr;
+  int64_t tok_stride;
+  int64_t head_stride;
+} decik_tensor3_mut;
+
+DECIK_API int decik_varlen_attn_fwd(decik_tensor3 q, decik_tensor3 k, decik_tensor3 v, decik_tensor3_mut out,
+                          float* lse, const int32_t* cu_seqlens, int n_rows, int max_len,
+                          int64_t n_tok, int n_heads, int n_kv, int head_dim, float scale,
+                          int dtype, void* stream);
+
+/* Bytes of device workspace decik_varlen_attn_bwd needs for these sizes (fp32 dq accumulator
+ * [T, n_heads, D] and the fp32 rowsum(dO * O) [n_heads, T]). */
+DECIK_API int64_t decik_varlen_attn_bwd_workspace(int64_t n_tok, int n_heads, int head_dim);
+
+/* Backward: dq, dk, dv (dk/dv already summed over each kv head's query heads). Uses the forward's
+ * out and lse (no forward recompute). workspace: decik_varlen_attn_bwd_workspace() bytes,
+ * 256-byte aligned; its contents on entry do not matter. */
+DECIK_API int decik_varlen_attn_bwd(decik_tensor3 dout, decik_tensor3 q, decik_tensor3 k, decik_tensor3 v,
+                          decik_tensor3 out, const float* lse, decik_tensor3_mut dq,
+                          decik_tensor3_mut dk, decik_tensor3_mut dv, const int32_t* cu_seqlens,
+                          int n_rows, int max_len, int64_t n_tok, int n_heads, int n_kv,
+                          int head_dim, float scale, int dtype, void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DECIK_B200_H */

@@ -1,0 +1,297 @@
+"""Parity of the sm_100a kernels (through the C ABI, via decik_b200.ops) with the CPU oracle and
+the reference's golden fixtures. Integer / rounding-defined kernels must be bit-exact; attention
+must meet the bf16 bar in tests/tolerance.py."""
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as o_attn
+from oracle import lora as o_lora
+from oracle import nf4 as o_nf4
+from oracle import rmsnorm as o_norm
+from oracle import rope as o_rope
+from tests.conftest import golden
+from tests.tolerance import assert_close16
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ops():
+    from decik_b200 import ops
+    return ops
+
+
+def _dequant_gpu(st, out_dtype):
+    ops = _ops()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    if st["nested"]:
+        return ops.nf4_dequant(t(st["packed"]), t(st["absmax"]), t(st["code"]), st["shape"], st["blocksize"],
+                               absmax2=t(st["absmax2"]), code2=t(st["code2"]),
+                               offset=torch.tensor([float(st["offset"])], dtype=torch.float32, device=DEV),
+                               blocksize2=st["blocksize2"], out_dtype=out_dtype)
+    return ops.nf4_dequant(t(st["packed"]), t(st["absmax"]), t(st["code"]), st["shape"], st["blocksize"],
+                           out_dtype=out_dtype)
+
+
+def _golden_state(g, tag):
+    nested = bool(g[f"{tag}_nested"])
+    st = dict(packed=g[f"{tag}_packed"], absmax=g[f"{tag}_absmax"], code=g[f"{tag}_code"],
+              shape=tuple(int(v) for v in g[f"{tag}_shape"]), blocksize=64, blocksize2=256, nested=nested)
+    if nested:
+        st.update(absmax2=g[f"{tag}_absmax2"], code2=g[f"{tag}_code2"], offset=np.float32(g[f"{tag}_offset"]))
+    return st
+
+
+# ---------------------------------------------------------------------------------------- NF4
+@pytest.mark.parametrize("tag", ["a", "b", "c"])
+def test_nf4_golden_bit_exact(cuda_lib, tag):
+    g = golden("nf4_golden.npz")
+    out = _dequant_gpu(_golden_state(g, tag), torch.float16).cpu().numpy()
+    assert np.array_equal(out.view(np.uint16), g[f"{tag}_out"].view(np.uint16))
+
+
+@pytest.mark.parametrize("i", [0, 1, 2, 3])
+def test_nf4_reference_shapes_hash(cuda_lib, i):
+    """solution/test_solution.py:10 shapes: (1536,1536), (256,1536) nested/not, (1536,8960)."""
+    from tests.golden.make_golden import random_nf4_state
+
+    g = golden("nf4_golden.npz")
+    shape = tuple(int(v) for v in g[f"hash{i}_shape"])
+    st = random_nf4_state(shape, bool(g[f"hash{i}_nested"]), int(g[f"hash{i}_seed"]))
+    out = _dequant_gpu(st, torch.float16).cpu().numpy()
+    assert hashlib.sha256(out.tobytes()).hexdigest() == str(g[f"hash{i}_sha256"])
+
+
+@pytest.mark.parametrize("shape,nested,bs", [((1536, 1536), True, 64), ((256, 1536), False, 64),
+                                             ((8960, 1536), True, 64), ((96, 64), True, 32),
+                                             ((128, 256), True, 128), ((7, 18), False, 2)])
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
+def test_nf4_vs_oracle_bit_exact(cuda_lib, shape, nested, bs, dtype):
+    rng = np.random.default_rng(hash((shape, nested, bs)) % 2**32)
+    w = (rng.standard_normal(shape) * 0.05).astype(np.float32)
+    st = o_nf4.quantize_nf4(w, blocksize=bs, nested=nested)
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dtype]
+    out = _dequant_gpu(st, tdt).cpu()
+    ref = o_nf4.dequantize_nf4(st, dtype)
+    if dtype == "bf16":
+        assert np.array_equal(out.view(torch.int16).numpy().view(np.uint16), ref)
+    elif dtype == "f16":
+        assert np.array_equal(out.numpy().view(np.uint16), ref.view(np.uint16))
+    else:
+        assert np.array_equal(out.numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def test_nf4_unaligned_views(cuda_lib):
+    """Packed bytes at an odd offset take the scalar path; results are still bit-exact."""
+    ops = _ops()
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((64, 128)) * 0.05).astype(np.float32)
+    st = o_nf4.quantize_nf4(w, nested=False)
+    buf = torch.zeros(st["packed"].size + 1, dtype=torch.uint8, device=DEV)
+    buf[1:] = torch.from_numpy(st["packed"]).to(DEV)
+    out = ops.nf4_dequant(buf[1:], torch.from_numpy(st["absmax"]).to(DEV),
+                          torch.from_numpy(st["code"]).to(DEV), st["shape"], 64).cpu().numpy()
+    assert np.array_equal(out.view(np.uint16), o_nf4.dequantize_nf4(st, "f16").view(np.uint16))
+
+
+# ---------------------------------------------------------------------------------------- RoPE
+def test_rope_golden_bit_exact(cuda_lib):
+    ops = _ops()
+    g = golden("rope_golden.npz")
+    T, HQ, HK, D = (int(v) for v in g["dims"])
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    qo, ko = ops.rope_fwd(t(g["qb"]), t(g["ql"]), t(g["kb"]), t(g["cos"]), t(g["sin"]), HQ, HK)
+    assert np.array_equal(qo.cpu().numpy().view(np.uint16), g["qo"].view(np.uint16))
+    assert np.array_equal(ko.cpu().numpy().view(np.uint16), g["ko"].view(np.uint16))
+    dq, dk = ops.rope_bwd(t(g["gq"]), t(g["gk"]), t(g["cos"]), t(g["sin"]))
+    assert np.array_equal(dq.cpu().numpy().view(np.uint16), g["dq"].view(np.uint16))
+    assert np.array_equal(dk.cpu().numpy().view(np.uint16), g["dk"].view(np.uint16))
+
+
+@pytest.mark.parametrize("T,HQ,HK", [(1, 12, 2), (830, 12, 2), (513, 28, 4)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rope_vs_oracle_bit_exact(cuda_lib, T, HQ, HK, dtype):
+    ops = _ops()
+    D = 128
+    torch.manual_seed(T)
+    qb = (torch.randn(T, HQ * D) * 3).to(dtype)
+    ql = (torch.randn(T, HQ * D) * 0.1).to(dtype)
+    kb = (torch.randn(T, HK * D) * 3).to(dtype)
+    c, s = o_rope.cos_sin(np.arange(T) % 300, D)
+    gq = torch.randn(HQ, T, D).to(dtype)
+    gk = torch.randn(HK, T, D).to(dtype)
+    qo, ko = ops.rope_fwd(qb.to(DEV), ql.to(DEV), kb.to(DEV), torch.from_numpy(c).to(DEV),
+                          torch.from_numpy(s).to(DEV), HQ, HK)
+    dq, dk = ops.rope_bwd(gq.to(DEV), gk.to(DEV), torch.from_numpy(c).to(DEV), torch.from_numpy(s).to(DEV))
+    f = lambda x: x.float().numpy()
+    odt = "bf16" if dtype == torch.bfloat16 else np.float16
+    rq, rk = o_rope.rope_fwd(f(qb), f(ql), f(kb), c, s, HQ, HK, odt)
+    rdq, rdk = o_rope.rope_bwd(f(gq), f(gk), c, s, odt)
+    bits = lambda x: x.cpu().view(torch.int16).numpy().view(np.uint16)
+    ref_bits = lambda r: r if dtype == torch.bfloat16 else r.view(np.uint16)
+    assert np.array_equal(bits(qo), ref_bits(rq)) and np.array_equal(bits(ko), ref_bits(rk))
+    assert np.array_equal(bits(dq), ref_bits(rdq)) and np.array_equal(bits(dk), ref_bits(rdk))
+
+
+# ---------------------------------------------------------------------------------------- LoRA
+def test_lora_kernels_golden_bit_exact(cuda_lib):
+    ops = _ops()
+    g = golden("lora_golden.npz")
+    T, H, R, HV = (int(v) for v in g["dims"])
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    bq, bv = ops.keep_pack(t(g["keep_q"].reshape(T, H)), t(g["keep_v"].reshape(T, H)))
+    assert np.array_equal(bq.cpu().numpy(), g["bits_q"]) and np.array_equal(bv.cpu().numpy(), g["bits_v"])
+    scale = torch.tensor(float(g["scale"]), device=DEV)
+    xq, xv = ops.lora_inputs(t(g["x"].reshape(T, H)), bq, bv, scale, scale)
+    assert np.array_equal(xq.cpu().numpy().view(np.uint16), g["xq16"].view(np.uint16))
+    assert np.array_equal(xv.cpu().numpy().view(np.uint16), g["xv16"].view(np.uint16))
+    s = 1.0 / (1.0 - float(g["p"]))
+    gin = ops.lora_input_grad(t(g["giq"]), t(g["giv"]), bq, bv, s, s)
+    assert np.array_equal(gin.cpu().numpy().view(np.uint32), g["gin"].view(np.uint32))
+
+
+def test_lora_inputs_bf16_vs_oracle(cuda_lib):
+    ops = _ops()
+    rng = np.random.default_rng(1)
+    T, W = 77, 1536
+    x = rng.standard_normal((T, W)).astype(np.float32)
+    kq = rng.random((T, W)) > 0.1
+    kv = rng.random((T, W)) > 0.1
+    bq, bv = o_lora.keep_pack(kq), o_lora.keep_pack(kv)
+    sc = np.float32(1 / 0.9)
+    xq, xv = ops.lora_inputs(torch.from_numpy(x).to(DEV), torch.from_numpy(bq).to(DEV),
+                             torch.from_numpy(bv).to(DEV), torch.tensor(sc, device=DEV),
+                             torch.tensor(sc, device=DEV), out_dtype=torch.bfloat16)
+    rq, rv = o_lora.lora_inputs(x, bq, bv, sc, sc, out_dtype="bf16")
+    assert np.array_equal(xq.cpu().view(torch.int16).numpy().view(np.uint16), rq)
+    assert np.array_equal(xv.cpu().view(torch.int16).numpy().view(np.uint16), rv)
+
+
+# ---------------------------------------------------------------------------------------- RMSNorm
+def test_rmsnorm_vs_oracle(cuda_lib):
+    ops = _ops()
+    g = golden("lora_golden.npz")
+    T, H = int(g["dims"][0]), int(g["dims"][1])
+    x = torch.from_numpy(g["h"].reshape(T, H)).to(DEV)
+    w = torch.from_numpy(g["w"]).to(DEV)
+    y, rstd = ops.rmsnorm_fwd(x, w, float(g["eps"]))
+    np.testing.assert_allclose(y.cpu().numpy(), g["norm_y"].reshape(T, H), rtol=1e-5, atol=1e-5)
+    dx = ops.rmsnorm_bwd(torch.from_numpy(g["norm_gy"].reshape(T, H)).to(DEV), x, w, rstd)
+    np.testing.assert_allclose(dx.cpu().numpy(), g["norm_dx"].reshape(T, H), rtol=1e-4, atol=1e-5)
+    y2, _ = ops.rmsnorm_fwd(x, w, float(g["eps"]))
+    assert torch.equal(y, y2)  # the recompute is bit-identical
+
+
+# ---------------------------------------------------------------------------------------- attention
+def _attn_case(lengths, HQ, HK, dtype, seed=0, layout="token"):
+    torch.manual_seed(seed)
+    D = 128
+    T = int(sum(lengths))
+    spans, start = [], 0
+    for L in lengths:
+        spans.append((start, int(L)))
+        start += int(L)
+    cu = torch.tensor([s for s, _ in spans] + [T], dtype=torch.int32, device=DEV)
+    if layout == "token":
+        q = torch.randn(T, HQ, D).to(dtype).to(DEV)
+        k = torch.randn(T, HK, D).to(dtype).to(DEV)
+        v = torch.randn(T, HK, D).to(dtype).to(DEV)
+    else:  # the reference's layouts: q, k head-major, v token-major (solution/attn.py:408-412)
+        q = torch.randn(HQ, T, D).to(dtype).to(DEV).transpose(0, 1)
+        k = torch.randn(HK, T, D).to(dtype).to(DEV).transpose(0, 1)
+        v = torch.randn(T, HK, D).to(dtype).to(DEV)
+    do = torch.randn(T, HQ, D).to(dtype).to(DEV)
+    return spans, cu, q, k, v, do
+
+
+def _np(t):
+    return t.float().cpu().numpy()
+
+
+CASES = [
+    ([37, 128, 211, 454], 12, 2),                # config 1 lengths
+    ([401, 77, 512, 3], 12, 2),                  # solution/test_solution.py:76 spans
+    ([37, 5, 20, 1], 12, 2),                     # dev/test_cpu_sdpa.py:24 spans
+    ([1], 12, 2),                                # a single token
+    ([129, 64, 65, 127, 191], 28, 4),            # 7B heads, lengths around tile edges
+    ([1000], 4, 4),                              # no GQA, one long row
+]
+
+
+@pytest.mark.parametrize("lengths,HQ,HK", CASES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_varlen_attention_fwd_bwd_vs_oracle(cuda_lib, lengths, HQ, HK, dtype):
+    ops = _ops()
+    spans, cu, q, k, v, do = _attn_case(lengths, HQ, HK, dtype, layout="ref")
+    scale = 128 ** -0.5
+    out, lse = ops.varlen_attn_fwd(q, k, v, cu, max(lengths), scale)
+    ro, rl = o_attn.forward(_np(q), _np(k), _np(v), spans, scale)
+    assert_close16(_np(out), ro, "out")
+    np.testing.assert_allclose(lse.cpu().numpy(), rl, rtol=0, atol=2e-3)
+    dq, dk, dv = ops.varlen_attn_bwd(do, q, k, v, out, lse, cu, max(lengths), scale)
+    assert dq.stride() == q.stride() and dk.stride() == k.stride() and dv.stride() == v.stride()
+    rdq, rdk, rdv = o_attn.backward(_np(do), _np(q), _np(k), _np(v), spans, scale)
+    assert_close16(_np(dq), rdq, "dq")
+    assert_close16(_np(dk), rdk, "dk")
+    assert_close16(_np(dv), rdv, "dv")
+
+
+def test_varlen_attention_golden_reference_packed_sdpa(cuda_lib):
+    """The reference's own PackedSDPA outputs and grads (tests/golden/sdpa_golden.npz)."""
+    ops = _ops()
+    g = golden("sdpa_golden.npz")
+    HQ, HK, D = (int(v) for v in g["dims"])
+    spans = [tuple(int(x) for x in s) for s in g["spans"]]
+    T = sum(L for _, L in spans)
+    cu = torch.tensor([s for s, _ in spans] + [T], dtype=torch.int32, device=DEV)
+    q = torch.from_numpy(g["q"]).to(DEV).transpose(0, 1)      # [T, H, D] view of head-major
+    k = torch.from_numpy(g["k"]).to(DEV).transpose(0, 1)
+    v = torch.from_numpy(g["v"]).to(DEV)
+    do = torch.from_numpy(g["g"][0] if g["g"].ndim == 4 else g["g"]).to(DEV)
+    out, lse = ops.varlen_attn_fwd(q, k, v, cu, max(L for _, L in spans), D ** -0.5)
+    assert_close16(_np(out), g["out"], "out")
+    dq, dk, dv = ops.varlen_attn_bwd(do, q, k, v, out, lse, cu, max(L for _, L in spans), D ** -0.5)
+    assert_close16(_np(dq).transpose(1, 0, 2), g["dq"], "dq")
+    assert_close16(_np(dk).transpose(1, 0, 2), g["dk"], "dk")
+    assert_close16(_np(dv), g["dv"], "dv")
+
+
+def test_varlen_attention_deterministic_forward(cuda_lib):
+    ops = _ops()
+    spans, cu, q, k, v, do = _attn_case([300, 700, 5], 12, 2, torch.bfloat16, seed=4)
+    a, la = ops.varlen_attn_fwd(q, k, v, cu, 700, 0.088)
+    b, lb = ops.varlen_attn_fwd(q, k, v, cu, 700, 0.088)
+    assert torch.equal(a, b) and torch.equal(la, lb)
+
+
+def test_varlen_attention_large_properties(cuda_lib):
+    """Config-3 sized packing (16,384 tokens, L ~ U[64, 4096]): checked on sampled rows against the
+    oracle, and for size-independent properties (rows do not interact; finite outputs)."""
+    ops = _ops()
+    rng = np.random.default_rng(0)
+    lengths, total = [], 0
+    while total < 16384:
+        L = int(min(rng.integers(64, 4097), 16384 - total))
+        lengths.append(L)
+        total += L
+    spans, cu, q, k, v, do = _attn_case(lengths, 12, 2, torch.bfloat16, seed=1)
+    scale = 128 ** -0.5
+    out, lse = ops.varlen_attn_fwd(q, k, v, cu, max(lengths), scale)
+    dq, dk, dv = ops.varlen_attn_bwd(do, q, k, v, out, lse, cu, max(lengths), scale)
+    for t in (out, dq, dk, dv, lse):
+        assert torch.isfinite(t).all()
+    # the shortest row, checked alone against the oracle (rows must not see each other)
+    i = int(np.argmin(lengths))
+    s, L = spans[i]
+    sl = slice(s, s + L)
+    ro, _ = o_attn.forward(_np(q[sl]), _np(k[sl]), _np(v[sl]), [(0, L)], scale)
+    assert_close16(_np(out[sl]), ro, "out row")
+    rdq, rdk, rdv = o_attn.backward(_np(do[sl]), _np(q[sl]), _np(k[sl]), _np(v[sl]), [(0, L)], scale)
+    assert_close16(_np(dq[sl]), rdq, "dq row")
+    assert_close16(_np(dk[sl]), rdk, "dk row")
+    assert_close16(_np(dv[sl]), rdv, "dv row")
