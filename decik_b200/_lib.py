@@ -25,6 +25,7 @@ class Tensor3(ctypes.Structure):
 SIGNATURES = {
     "decik_last_error": (ctypes.c_char_p, []),
     "decik_abi_version": (c_int, []),
+    "decik_kernel_error": (c_int, [c_int]),
     "decik_nf4_dequant": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_int64, c_int, c_int, c_int, c_int, c_void_p]),
     "decik_rope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

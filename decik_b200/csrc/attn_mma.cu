@@ -4,10 +4,7 @@
 // fully-masked causal tiles never visited, logsumexp written by the forward so the backward does
 // not recompute it.
 //
-// Forward: CTA = 128 query rows of one row x one query head, 8 warps x 16 rows; K/V tiles of 64
-// keys double-buffered with cp.async; online softmax in the exp2 domain with quad-shuffle row
-// max/sum; only key blocks at or below the diagonal are loaded. Query blocks are launched
-// heaviest-first (highest block index first).
+// The forward runs on tcgen05 (attn_fwd_sm100.cu); this file holds the backward and the C entries.
 // Backward: CTA = 64 keys of one row x one kv head, 4 warps x 16 keys; it loops over the query
 // heads of its group and the query blocks at or below the diagonal, so dK/dV of the kv head are
 // summed in registers (no GQA reduce pass). S^T and dP^T are computed key-major so P^T and dS^T
@@ -26,184 +23,6 @@ using ptx::smem_u32;
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) { return Dt<T>::pack2(lo, hi); }
-
-// ------------------------------------------------------------------------------------------------
-// forward
-// ------------------------------------------------------------------------------------------------
-constexpr int FBM = 128, FBN = 64, FTHREADS = 256;
-constexpr int kFwdSmem = (FBM + 4 * FBN) * kRowBytes;  // Q + 2 stages x (K + V) = 96 KB
-
-struct FwdParams {
-  Tensor3 q, k, v;
-  Tensor3Mut o;
-  float* lse;
-  const int32_t* cu;
-  int64_t n_tok;
-  int n_heads, groups, n_mblocks;
-  float scale_log2;
-};
-
-template <typename T>
-__global__ void __launch_bounds__(FTHREADS, 1) attn_fwd_kernel(FwdParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int m_block = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);
-  const int row = blockIdx.y, h = blockIdx.z;
-  const int start = p.cu[row];
-  const int L = p.cu[row + 1] - start;
-  const int m0 = m_block * FBM;
-  if (m0 >= L) return;
-  const int kvh = h / p.groups;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t4 = lane & 3;
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sKV = sQ + FBM * kRowBytes;
-  const int64_t tok_end = static_cast<int64_t>(start) + L;
-
-  load_tile<FBM, FTHREADS>(sQ, p.q, start + m0, tok_end, h, tid);
-  const int kv_end = min(m0 + FBM, L);
-  const int n_nb = (kv_end + FBN - 1) / FBN;
-  load_tile<FBN, FTHREADS>(sKV, p.k, start, tok_end, kvh, tid);
-  load_tile<FBN, FTHREADS>(sKV + FBN * kRowBytes, p.v, start, tok_end, kvh, tid);
-  ptx::cp_async_commit();
-
-  uint32_t qf[8][4];
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_r[2] = {-INFINITY, -INFINITY};
-  float l_r[2] = {0.f, 0.f};
-  const int q_row0 = m0 + warp * 16 + g;  // query index in the row of accumulator rows g, g+8
-
-  for (int nb = 0; nb < n_nb; ++nb) {
-    if (nb + 1 < n_nb) {
-      const uint32_t st = sKV + ((nb + 1) & 1) * (2 * FBN * kRowBytes);
-      load_tile<FBN, FTHREADS>(st, p.k, start + (nb + 1) * FBN, tok_end, kvh, tid);
-      load_tile<FBN, FTHREADS>(st + FBN * kRowBytes, p.v, start + (nb + 1) * FBN, tok_end, kvh, tid);
-      ptx::cp_async_commit();
-      ptx::cp_async_wait<1>();
-    } else {
-      ptx::cp_async_wait<0>();
-    }
-    __syncthreads();
-    if (nb == 0) {
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        ldsm_x4(sQ + 2 * swz(warp * 16 + (lane & 15), kk * 2 + (lane >> 4)), qf[kk][0], qf[kk][1],
-                qf[kk][2], qf[kk][3]);
-    }
-    const uint32_t sK = sKV + (nb & 1) * (2 * FBN * kRowBytes);
-    const uint32_t sV = sK + FBN * kRowBytes;
-    float s[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-#pragma unroll
-      for (int np = 0; np < 4; ++np) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(sK + 2 * swz(np * 16 + (lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1)),
-                b0, b1, b2, b3);
-        ptx::mma16816<T>(s[2 * np], qf[kk], b0, b1);
-        ptx::mma16816<T>(s[2 * np + 1], qf[kk], b2, b3);
-      }
-    }
-    // scale, mask (diagonal block or the row end), online softmax
-    const bool need_mask = (nb + 1) * FBN > m0 || (nb + 1) * FBN > L;
-    float mx[2] = {m_r[0], m_r[1]};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float x = s[j][e] * p.scale_log2;
-        if (need_mask) {
-          const int kv = nb * FBN + j * 8 + 2 * t4 + (e & 1);
-          const int qi = q_row0 + ((e >> 1) << 3);
-          if (kv > qi || kv >= L) x = -INFINITY;
-        }
-        s[j][e] = x;
-        mx[e >> 1] = fmaxf(mx[e >> 1], x);
-      }
-    }
-    float alpha[2], rs[2] = {0.f, 0.f};
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
-      const float mu = mx[i] == -INFINITY ? 0.f : mx[i];
-      alpha[i] = ptx::ex2(m_r[i] - mu);
-      m_r[i] = mx[i];
-      mx[i] = mu;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float pe = ptx::ex2(s[j][e] - mx[e >> 1]);
-        s[j][e] = pe;
-        rs[e >> 1] += pe;
-      }
-    }
-    l_r[0] = l_r[0] * alpha[0] + rs[0];
-    l_r[1] = l_r[1] * alpha[1] + rs[1];
-#pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      o[dt][0] *= alpha[0];
-      o[dt][1] *= alpha[0];
-      o[dt][2] *= alpha[1];
-      o[dt][3] *= alpha[1];
-    }
-    // O += P V
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t a[4] = {pack2<T>(s[2 * kk][0], s[2 * kk][1]), pack2<T>(s[2 * kk][2], s[2 * kk][3]),
-                             pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]),
-                             pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3])};
-#pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(sV + 2 * swz(kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), dp * 2 + (lane >> 4)),
-                  b0, b1, b2, b3);
-        ptx::mma16816<T>(o[2 * dp], a, b0, b1);
-        ptx::mma16816<T>(o[2 * dp + 1], a, b2, b3);
-      }
-    }
-    __syncthreads();  // every warp is done with this stage before it is refilled
-  }
-
-  // epilogue: normalise, stage the tile in shared memory, 16-byte coalesced stores
-  float inv[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    l_r[i] += __shfl_xor_sync(0xffffffffu, l_r[i], 1);
-    l_r[i] += __shfl_xor_sync(0xffffffffu, l_r[i], 2);
-    inv[i] = l_r[i] > 0.f ? 1.f / l_r[i] : 0.f;
-  }
-  uint8_t* sO = smem;
-#pragma unroll
-  for (int dt = 0; dt < 16; ++dt) {
-    const int r = warp * 16 + g;
-    *reinterpret_cast<uint32_t*>(sO + 2 * (swz(r, dt) + 2 * t4)) =
-        pack2<T>(o[dt][0] * inv[0], o[dt][1] * inv[0]);
-    *reinterpret_cast<uint32_t*>(sO + 2 * (swz(r + 8, dt) + 2 * t4)) =
-        pack2<T>(o[dt][2] * inv[1], o[dt][3] * inv[1]);
-  }
-  if (t4 == 0) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int qi = q_row0 + i * 8;
-      if (qi < L) p.lse[static_cast<int64_t>(h) * p.n_tok + start + qi] = (m_r[i] + __log2f(l_r[i])) * kLn2;
-    }
-  }
-  __syncthreads();
-  char* og = static_cast<char*>(p.o.ptr);
-  for (int i = tid; i < FBM * 16; i += FTHREADS) {
-    const int r = i >> 4, c = i & 15;
-    if (m0 + r < L) {
-      const int64_t off = (static_cast<int64_t>(start) + m0 + r) * p.o.tok + static_cast<int64_t>(h) * p.o.head + c * 8;
-      *reinterpret_cast<uint4*>(og + 2 * off) = *reinterpret_cast<const uint4*>(sO + 2 * swz(r, c));
-    }
-  }
-}
 
 // ------------------------------------------------------------------------------------------------
 // backward
@@ -476,41 +295,30 @@ bool ok3(const void* p, int64_t tok, int64_t head) {
 using namespace decik;
 using namespace decik::attn;
 
+namespace decik {
+namespace attn {
+int fwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor3& v, const decik_tensor3_mut& out,
+              float* lse, const int32_t* cu, int n_rows, int max_len, int64_t n_tok, int n_heads, int n_kv,
+              float scale, int dtype, cudaStream_t stream);
+}
+}  // namespace decik
+
 extern "C" int decik_varlen_attn_fwd(decik_tensor3 q, decik_tensor3 k, decik_tensor3 v,
                                      decik_tensor3_mut out, float* lse, const int32_t* cu_seqlens,
                                      int n_rows, int max_len, int64_t n_tok, int n_heads, int n_kv,
                                      int head_dim, float scale, int dtype, void* stream) {
   if (n_rows == 0 || n_tok == 0 || max_len == 0) return DECIK_OK;
   if (head_dim != D) return set_error(DECIK_ERR_UNSUPPORTED, "varlen_attn_fwd: head_dim %d (only 128)", head_dim);
-  if (n_rows < 0 || max_len < 0 || n_tok < 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv)
+  if (n_rows < 0 || max_len < 0 || n_tok < 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv ||
+      n_tok > INT32_MAX - 256)
     return set_error(DECIK_ERR_INVALID, "varlen_attn_fwd: bad sizes (rows %d, heads %d/%d)", n_rows, n_heads, n_kv);
   if (!ok3(q.ptr, q.tok_stride, q.head_stride) || !ok3(k.ptr, k.tok_stride, k.head_stride) ||
       !ok3(v.ptr, v.tok_stride, v.head_stride) || !ok3(out.ptr, out.tok_stride, out.head_stride))
     return set_error(DECIK_ERR_INVALID, "varlen_attn_fwd: tensors need 16-byte aligned pointers and strides");
   if (!lse || !cu_seqlens) return set_error(DECIK_ERR_INVALID, "varlen_attn_fwd: null lse / cu_seqlens");
-  FwdParams p;
-  p.q = {q.ptr, q.tok_stride, q.head_stride};
-  p.k = {k.ptr, k.tok_stride, k.head_stride};
-  p.v = {v.ptr, v.tok_stride, v.head_stride};
-  p.o = {out.ptr, out.tok_stride, out.head_stride};
-  p.lse = lse;
-  p.cu = cu_seqlens;
-  p.n_tok = n_tok;
-  p.n_heads = n_heads;
-  p.groups = n_heads / n_kv;
-  p.n_mblocks = (max_len + FBM - 1) / FBM;
-  p.scale_log2 = scale * kLog2e;
-  dim3 grid(p.n_mblocks, n_rows, n_heads);
-  return DECIK_DISPATCH_16(dtype, [&] {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(attn_fwd_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-      cudaFuncSetAttribute(attn_fwd_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-      attr = true;
-    }
-    attn_fwd_kernel<T><<<grid, FTHREADS, kFwdSmem, as_stream(stream)>>>(p);
-    return check_launch("varlen_attn_fwd");
-  });
+  if (dtype != DECIK_F16 && dtype != DECIK_BF16) return set_error(DECIK_ERR_INVALID, "varlen_attn_fwd: dtype");
+  return fwd_sm100(q, k, v, out, lse, cu_seqlens, n_rows, max_len, n_tok, n_heads, n_kv, scale, dtype,
+                   as_stream(stream));
 }
 
 extern "C" int64_t decik_varlen_attn_bwd_workspace(int64_t n_tok, int n_heads, int head_dim) {

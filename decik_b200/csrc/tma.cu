@@ -1,0 +1,87 @@
+// Host side of the sm_100a kernels: TMA tensor maps for [T, H, 128] 16-bit views, and the device
+// error word that bounded waits write when they give up.
+#include <cudaTypedefs.h>
+
+#include "attn_common.cuh"
+
+namespace decik {
+
+// Set by kernels whose bounded waits gave up (first code wins); read and cleared by
+// decik_kernel_error().
+static __device__ int g_kernel_error = 0;
+
+namespace attn {
+
+int* attn_error_word() {
+  static int* ptr = nullptr;
+  static int dev_cached = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (ptr == nullptr || dev != dev_cached) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_kernel_error) != cudaSuccess) return nullptr;
+    ptr = static_cast<int*>(p);
+    dev_cached = dev;
+  }
+  return ptr;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// A 3-D tiled map over a [T, H, 128] 16-bit view (head_dim contiguous) whose box is one 128-row x
+// 64-element half tile with the 128-byte swizzle (the UMMA K-major / MN-major canonical layout).
+// The two outer dimensions are ordered by increasing stride: order 0 = (d, token, head),
+// order 1 = (d, head, token); the kernel passes its coordinates in that order.
+int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
+                  int n_heads, int dtype, int* order) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return set_error(DECIK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const bool tok_inner = tok_stride <= head_stride || n_heads == 1;
+  *order = tok_inner ? 0 : 1;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3], estr[3] = {1, 1, 1};
+  dims[0] = 128;
+  if (tok_inner) {
+    dims[1] = static_cast<cuuint64_t>(n_tok);
+    dims[2] = static_cast<cuuint64_t>(n_heads);
+    strides[0] = static_cast<cuuint64_t>(tok_stride) * 2;
+    strides[1] = static_cast<cuuint64_t>(n_heads == 1 ? tok_stride * n_tok : head_stride) * 2;
+    box[0] = 64; box[1] = 128; box[2] = 1;
+  } else {
+    dims[1] = static_cast<cuuint64_t>(n_heads);
+    dims[2] = static_cast<cuuint64_t>(n_tok);
+    strides[0] = static_cast<cuuint64_t>(head_stride) * 2;
+    strides[1] = static_cast<cuuint64_t>(tok_stride) * 2;
+    box[0] = 64; box[1] = 1; box[2] = 128;
+  }
+  const CUtensorMapDataType dt = dtype == DECIK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(DECIK_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): tok_stride %lld head_stride %lld",
+                     static_cast<int>(r), (long long)tok_stride, (long long)head_stride);
+  return DECIK_OK;
+}
+
+}  // namespace attn
+}  // namespace decik
+
+extern "C" int decik_kernel_error(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, decik::g_kernel_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(decik::g_kernel_error, &zero, sizeof(int));
+  }
+  return v;
+}

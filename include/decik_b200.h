@@ -43,6 +43,11 @@ DECIK_API const char* decik_last_error(void);
 /* ABI version of this library (bumped on any signature change). */
 DECIK_API int decik_abi_version(void);
 
+/* Error code recorded on the current device by a kernel whose bounded wait gave up (0 = none;
+ * -1 if it could not be read). Synchronizes with the device. reset != 0 clears it. Kernels that
+ * wait on mbarriers never spin forever: they record a code here and return. */
+DECIK_API int decik_kernel_error(int reset);
+
 /* ---------------------------------------------------------------------------------------------
  * NF4 double-quant dequant.
  * Replaces solution/nf4.py:66-85 (dequantize_nf4) and its kernel skc_nf4_dequant_kernel

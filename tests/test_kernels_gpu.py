@@ -215,6 +215,7 @@ def _np(t):
 
 CASES = [
     ([37, 128, 211, 454], 12, 2),                # config 1 lengths
+    ([300, 1000, 3], 28, 4),                     # 7B heads: odd group size 7
     ([401, 77, 512, 3], 12, 2),                  # solution/test_solution.py:76 spans
     ([37, 5, 20, 1], 12, 2),                     # dev/test_cpu_sdpa.py:24 spans
     ([1], 12, 2),                                # a single token
@@ -239,6 +240,7 @@ def test_varlen_attention_fwd_bwd_vs_oracle(cuda_lib, lengths, HQ, HK, dtype):
     assert_close16(_np(dq), rdq, "dq")
     assert_close16(_np(dk), rdk, "dk")
     assert_close16(_np(dv), rdv, "dv")
+    assert cuda_lib.decik_kernel_error(1) == 0
 
 
 def test_varlen_attention_golden_reference_packed_sdpa(cuda_lib):
@@ -267,6 +269,7 @@ def test_varlen_attention_deterministic_forward(cuda_lib):
     a, la = ops.varlen_attn_fwd(q, k, v, cu, 700, 0.088)
     b, lb = ops.varlen_attn_fwd(q, k, v, cu, 700, 0.088)
     assert torch.equal(a, b) and torch.equal(la, lb)
+    assert cuda_lib.decik_kernel_error(1) == 0
 
 
 def test_varlen_attention_large_properties(cuda_lib):
