@@ -26,7 +26,7 @@ namespace decik {
 namespace attn {
 
 int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
-                  int n_heads, int dtype, int* order);
+                  int n_heads, int dtype, int* order, int box_rows);
 int* attn_error_word();
 
 namespace {
@@ -339,9 +339,9 @@ int fwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor
               float* lse, const int32_t* cu, int n_rows, int max_len, int64_t n_tok, int n_heads, int n_kv,
               float scale, int dtype, cudaStream_t stream) {
   Params p;
-  int rc = make_tile_map(&p.tq, q.ptr, q.tok_stride, q.head_stride, n_tok, n_heads, dtype, &p.order_q);
-  if (!rc) rc = make_tile_map(&p.tk, k.ptr, k.tok_stride, k.head_stride, n_tok, n_kv, dtype, &p.order_k);
-  if (!rc) rc = make_tile_map(&p.tv, v.ptr, v.tok_stride, v.head_stride, n_tok, n_kv, dtype, &p.order_v);
+  int rc = make_tile_map(&p.tq, q.ptr, q.tok_stride, q.head_stride, n_tok, n_heads, dtype, &p.order_q, BM);
+  if (!rc) rc = make_tile_map(&p.tk, k.ptr, k.tok_stride, k.head_stride, n_tok, n_kv, dtype, &p.order_k, BN);
+  if (!rc) rc = make_tile_map(&p.tv, v.ptr, v.tok_stride, v.head_stride, n_tok, n_kv, dtype, &p.order_v, BN);
   if (rc) return rc;
   p.o = out.ptr;
   p.o_tok = out.tok_stride;

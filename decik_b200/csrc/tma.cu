@@ -38,12 +38,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// A 3-D tiled map over a [T, H, 128] 16-bit view (head_dim contiguous) whose box is one 128-row x
-// 64-element half tile with the 128-byte swizzle (the UMMA K-major / MN-major canonical layout).
+// A 3-D tiled map over a [T, H, 128] 16-bit view (head_dim contiguous) whose box is one
+// box_rows x 64-element half tile with the 128-byte swizzle (the UMMA K-major / MN-major canonical layout).
 // The two outer dimensions are ordered by increasing stride: order 0 = (d, token, head),
 // order 1 = (d, head, token); the kernel passes its coordinates in that order.
 int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
-                  int n_heads, int dtype, int* order) {
+                  int n_heads, int dtype, int* order, int box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return set_error(DECIK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const bool tok_inner = tok_stride <= head_stride || n_heads == 1;
@@ -56,13 +56,13 @@ int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t
     dims[2] = static_cast<cuuint64_t>(n_heads);
     strides[0] = static_cast<cuuint64_t>(tok_stride) * 2;
     strides[1] = static_cast<cuuint64_t>(n_heads == 1 ? tok_stride * n_tok : head_stride) * 2;
-    box[0] = 64; box[1] = 128; box[2] = 1;
+    box[0] = 64; box[1] = static_cast<cuuint32_t>(box_rows); box[2] = 1;
   } else {
     dims[1] = static_cast<cuuint64_t>(n_heads);
     dims[2] = static_cast<cuuint64_t>(n_tok);
     strides[0] = static_cast<cuuint64_t>(head_stride) * 2;
     strides[1] = static_cast<cuuint64_t>(tok_stride) * 2;
-    box[0] = 64; box[1] = 1; box[2] = 128;
+    box[0] = 64; box[1] = 1; box[2] = static_cast<cuuint32_t>(box_rows);
   }
   const CUtensorMapDataType dt = dtype == DECIK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
