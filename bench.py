@@ -69,56 +69,70 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled every 5 ms through NVML (read-only
+    queries) in a background thread while the timed region runs; nvidia-smi at 200 ms as a
+    fallback when NVML is unavailable."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.file = None
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples, self.max_mhz, self.reasons = [], None, set()
+        self.thread = None
+        self.stop = False
+        self.error = None
+
+    def _nvml_index(self) -> int:
+        try:
+            return int(torch.cuda._get_nvml_device_index(self.cuda_index))
+        except Exception:
+            return self.cuda_index
+
+    def _run(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self._nvml_index())
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            masks = [(name, getattr(nv, attr)) for name, attr in self.REASONS if hasattr(nv, attr)]
+            while not self.stop:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                active = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, m in masks:
+                    if active & m:
+                        self.reasons.add(name)
+                time.sleep(0.005)
+            nv.nvmlShutdown()
+        except Exception as e:  # NVML missing: one nvidia-smi reading instead
+            self.error = repr(e)
+            try:
+                out = subprocess.run(["nvidia-smi", "--query-gpu=clocks.sm,clocks.max.sm", "--format=csv,noheader,nounits",
+                                      "-i", str(self._nvml_index())], capture_output=True, text=True, timeout=10).stdout
+                cur, mx = out.strip().split(", ")[:2]
+                self.samples.append(float(cur))
+                self.max_mhz = float(mx)
+            except Exception:
+                pass
 
     def __enter__(self):
-        try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.index), "-lms", "200"], stdout=self.file,
-                                         stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        import threading
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop = True
+        self.thread.join(timeout=10)
         return False
 
     def summary(self) -> dict:
-        if self.proc is None or self.file is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.file.flush()
-        with open(self.file.name) as f:
-            rows = [r.strip().split(", ") for r in f if r.strip()]
-        os.unlink(self.file.name)
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml" if not self.error else "nvidia-smi"}
 
 
 def dist_setup():

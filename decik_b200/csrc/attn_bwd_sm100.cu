@@ -170,13 +170,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const int h = it_head(it), m0 = it_m0(it);
-      // lse (log2 domain) and delta of the 64 queries: plain loads by the warp, then the arrive
+      // -lse (log2 domain) and -delta of the 64 queries: plain loads by the warp, then the arrive
       float* st = stat + s * 2 * BM;
       for (int i = lane; i < BM; i += 32) {
         const int qi = m0 + i;
         const int64_t idx = static_cast<int64_t>(h) * p.n_tok + start + qi;
-        st[i] = qi < L ? p.lse[idx] * kLog2e : INFINITY;
-        st[BM + i] = qi < L ? p.delta[idx] : 0.f;
+        st[i] = qi < L ? -p.lse[idx] * kLog2e : -INFINITY;
+        st[BM + i] = qi < L ? -p.delta[idx] : 0.f;
       }
       __syncwarp();
       if (lane == 0) {
@@ -259,26 +259,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(bar(B_SFREE));
-      const float* lse2 = stat + s * 2 * BM;
-      const float* dlt = lse2 + BM;
-      const bool need_mask = m0 < n0 + BN || m0 + BM > L || n0 + BN > L;
+      const float4* nl4 = reinterpret_cast<const float4*>(stat + s * 2 * BM);   // -lse * log2e
+      const float4* nd4 = reinterpret_cast<const float4*>(stat + s * 2 * BM + BM);  // -delta
+      // visible query columns of this key: qc >= key - m0 (causal) and qc < L - m0 (row end)
+      const int qlo = key - m0;
+      const int qhi = key < L ? min(BM, L - m0) : 0;
+      const bool masked = qlo > 0 || qhi < BM;
+      const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
       uint32_t pp[32], dd[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        float pr[2], dr[2];
+      for (int c = 0; c < 16; ++c) {  // 4 query columns per step, as two packed pairs
+        const float4 nl = nl4[c], nd = nd4[c];
+        float e[4];
+        f2split(ffma2(f2(__uint_as_float(sv[4 * c]), __uint_as_float(sv[4 * c + 1])), sc2, f2(nl.x, nl.y)), e[0], e[1]);
+        f2split(ffma2(f2(__uint_as_float(sv[4 * c + 2]), __uint_as_float(sv[4 * c + 3])), sc2, f2(nl.z, nl.w)), e[2], e[3]);
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int qc = 2 * c + e;
-          float pe = ptx::ex2(__uint_as_float(sv[qc]) * p.scale_log2 - lse2[qc]);
-          if (need_mask) {
-            const int qi = m0 + qc;
-            if (key > qi || key >= L || qi >= L) pe = 0.f;
-          }
-          pr[e] = pe;
-          dr[e] = pe * (__uint_as_float(dp[qc]) - dlt[qc]);
+        for (int i = 0; i < 4; ++i) e[i] = ptx::ex2(e[i]);
+        if (masked) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (4 * c + i < qlo || 4 * c + i >= qhi) e[i] = 0.f;
         }
-        pp[c] = pk2<T>(pr[0], pr[1]);
-        dd[c] = pk2<T>(dr[0], dr[1]);
+        const uint64_t p01 = f2(e[0], e[1]), p23 = f2(e[2], e[3]);
+        const uint64_t g01 = fmul2(p01, fadd2(f2(__uint_as_float(dp[4 * c]), __uint_as_float(dp[4 * c + 1])), f2(nd.x, nd.y)));
+        const uint64_t g23 = fmul2(p23, fadd2(f2(__uint_as_float(dp[4 * c + 2]), __uint_as_float(dp[4 * c + 3])), f2(nd.z, nd.w)));
+        float g[4];
+        f2split(g01, g[0], g[1]);
+        f2split(g23, g[2], g[3]);
+        pp[2 * c] = pk2<T>(e[0], e[1]);
+        pp[2 * c + 1] = pk2<T>(e[2], e[3]);
+        dd[2 * c] = pk2<T>(g[0], g[1]);
+        dd[2 * c + 1] = pk2<T>(g[2], g[3]);
       }
       // P^T / dS^T TMEM slots are free once the previous dV / dK MMAs completed
       if (it > 0) ok = mbar_wait(bar(B_PFREE), (it - 1) & 1, p.err, 603);

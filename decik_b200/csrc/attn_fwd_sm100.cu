@@ -226,28 +226,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
       ok = mbar_wait(bar(B_SF + tile), j & 1, p.err, 301 + tile);
       if (!ok) break;
       tc_fence_after();
-      const bool need_mask = (j + 1) * BN > m0 || (j + 1) * BN > L;
-      // pass 1: row max of the scaled, masked scores
+      // keys past min(query, row end) are masked; only the diagonal / last block has any
+      const int lim = min(qi, L - 1) - j * BN;  // last visible column of this row in this block
+      const bool masked = lim < BN - 1;
+      // pass 1: row max of the raw scores (scale > 0 commutes with max), 64 columns at a time
       float mx = -INFINITY;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint32_t a[32], b[32];
-        tmem_ld32(tS + h * 64, a);
-        tmem_ld32(tS + h * 64 + 32, b);
+        uint32_t sv[64];
+        tmem_ld32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_ld_wait();
+        if (masked) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          float xa = __uint_as_float(a[c]) * p.scale_log2;
-          float xb = __uint_as_float(b[c]) * p.scale_log2;
-          if (need_mask) {
-            const int ka = j * BN + h * 64 + c, kb = ka + 32;
-            if (ka > qi || ka >= L) xa = -INFINITY;
-            if (kb > qi || kb >= L) xb = -INFINITY;
-          }
-          mx = fmaxf(mx, fmaxf(xa, xb));
+          for (int c = 0; c < 64; ++c)
+            if (64 * h + c > lim) sv[c] = __float_as_uint(-INFINITY);
         }
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
       }
-      const float m_new = fmaxf(m_run, mx);
+      const float m_new = fmaxf(m_run, mx * p.scale_log2);
       const bool resc = m_new > m_run + 8.f;
       float alpha = 1.f;
       if (resc) {
@@ -267,36 +265,38 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
         }
         tmem_st_wait();
       }
-      // pass 2: P = exp2(x - m_run) as 16-bit pairs into the first 64 columns of S
-      float sum = 0.f;
+      // pass 2: P = exp2(s * scale*log2e - m_run), packed FMA for the arguments and packed adds for
+      // the sum; P (16-bit pairs) overwrites the first 64 columns of S
+      const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
+      const uint64_t nm2 = f2(-m_run, -m_run);
+      uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint32_t a[32], b[32], pk[32];
-        tmem_ld32(tS + h * 64, a);
-        tmem_ld32(tS + h * 64 + 32, b);
+        uint32_t sv[64], pk[32];
+        tmem_ld32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_ld_wait();
+        if (masked) {
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          float x0 = __uint_as_float(a[2 * c]) * p.scale_log2;
-          float x1 = __uint_as_float(a[2 * c + 1]) * p.scale_log2;
-          float y0 = __uint_as_float(b[2 * c]) * p.scale_log2;
-          float y1 = __uint_as_float(b[2 * c + 1]) * p.scale_log2;
-          if (need_mask) {
-            const int k0 = j * BN + h * 64 + 2 * c;
-            if (k0 > qi || k0 >= L) x0 = -INFINITY;
-            if (k0 + 1 > qi || k0 + 1 >= L) x1 = -INFINITY;
-            if (k0 + 32 > qi || k0 + 32 >= L) y0 = -INFINITY;
-            if (k0 + 33 > qi || k0 + 33 >= L) y1 = -INFINITY;
-          }
-          const float e0 = ptx::ex2(x0 - m_run), e1 = ptx::ex2(x1 - m_run);
-          const float f0 = ptx::ex2(y0 - m_run), f1 = ptx::ex2(y1 - m_run);
-          sum += (e0 + e1) + (f0 + f1);
-          pk[c] = pk2<T>(e0, e1);
-          pk[16 + c] = pk2<T>(f0, f1);
+          for (int c = 0; c < 64; ++c)
+            if (64 * h + c > lim) sv[c] = __float_as_uint(-INFINITY);
         }
-        tmem_st32(tS + h * 32, pk);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          float x0, x1;
+          f2split(ffma2(f2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])), sc2, nm2), x0, x1);
+          const float e0 = ptx::ex2(x0), e1 = ptx::ex2(x1);
+          acc[c & 3] = fadd2(acc[c & 3], f2(e0, e1));
+          pk[c] = pk2<T>(e0, e1);
+        }
+        tmem_st32(tS + 32 * h, pk);
       }
-      l += sum;
+      float s0, s1, s2, s3, s4, s5, s6, s7;
+      f2split(acc[0], s0, s1);
+      f2split(acc[1], s2, s3);
+      f2split(acc[2], s4, s5);
+      f2split(acc[3], s6, s7);
+      l += ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar(B_PR + tile));
