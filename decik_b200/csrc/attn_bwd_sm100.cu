@@ -42,13 +42,14 @@ constexpr int KTILE = 2 * KHALF;
 constexpr int QHALF = BM * 128;  // [64 rows x 64] half: 8 KB
 constexpr int QTILE = 2 * QHALF;
 constexpr int NTHREADS = 320;
+constexpr int NST = 4;  // Q / dO / stats stages in flight
 // shared memory map (offsets from a 1024-aligned base)
 constexpr int OFF_K = 0, OFF_V = KTILE, OFF_Q = 2 * KTILE;   // Q[s] at OFF_Q + s * 2 * QTILE, dO after it
-constexpr int OFF_DS = OFF_Q + 4 * QTILE;                    // dS^T [128 keys x 64 q], 16 KB
-constexpr int OFF_STAT = OFF_DS + KHALF;                     // [2 stages][lse2 64 | delta 64] fp32
-constexpr int OFF_BAR = OFF_STAT + 2 * 2 * BM * 4;
-enum { B_KV = 0, B_QF = 1, B_QE = 3, B_SF = 5, B_SFREE = 6, B_PR = 7, B_PFREE = 8, B_DQF = 9, B_DQFREE = 10,
-       B_DONE = 11, N_BAR = 12 };
+constexpr int OFF_DS = OFF_Q + NST * 2 * QTILE;              // dS^T [128 keys x 64 q], 16 KB
+constexpr int OFF_STAT = OFF_DS + KHALF;                     // [NST][-lse*log2e 64 | -delta 64] fp32
+constexpr int OFF_BAR = OFF_STAT + NST * 2 * BM * 4;
+enum { B_KV = 0, B_QF = 1, B_QE = B_QF + NST, B_SF = B_QE + NST, B_SFREE, B_PR, B_PFREE, B_DQF, B_DQFREE, B_DONE,
+       N_BAR };
 constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
 constexpr int kSmem = OFF_TMEM + 16 + 1024;
 constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_P = 192, T_DS = 224, T_DV = 256, T_DK = 384;
@@ -76,27 +77,24 @@ __device__ __forceinline__ void load_half(uint32_t dst, const CUtensorMap* map, 
   else tma_load_3d(dst, map, bar, c, head, tok);
 }
 
-// A [128 x 128] (K-major, 16 KB halves) times B [64 x 128]^T (K-major, 8 KB halves)
-__device__ __forceinline__ void issue_nt(uint32_t d, uint32_t a, uint32_t b, uint32_t idesc) {
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t ka = (kk >> 2) * KHALF + (kk & 3) * 32;
-    const uint32_t kb = (kk >> 2) * QHALF + (kk & 3) * 32;
-    umma_ss(d, smem_desc_sw128(a + ka, 16, 1024), smem_desc_sw128(b + kb, 16, 1024), idesc, kk > 0);
-  }
-}
-// D [128 x 128] (+)= A (TMEM, 16-bit, [128 x 64]) * B [64 q x 128 d] (MN-major, 8 KB halves)
-__device__ __forceinline__ void issue_tn(uint32_t d, uint32_t a_tmem, uint32_t b, uint32_t idesc, bool acc) {
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk)
-    umma_ts(d, a_tmem + kk * 8, smem_desc_sw128(b + kk * 2048, QHALF, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
-}
-// dQ^T [128 d x 64 q] = K^T (MN-major view of the K tile) * dS^T (MN-major [128 keys x 64 q])
-__device__ __forceinline__ void issue_dq(uint32_t d, uint32_t k, uint32_t ds, uint32_t idesc) {
+// Descriptors are built once; a k-step advances the 14-bit start-address field (bytes >> 4), which
+// never carries out of the field for shared-memory addresses.
+// S^T / dP^T: A [128 x 128] (K-major, 16 KB halves) times B [64 x 128]^T (K-major, 8 KB halves)
+__device__ __forceinline__ void issue_nt(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    umma_ss(d, smem_desc_sw128(k + kk * 2048, KHALF, 1024), smem_desc_sw128(ds + kk * 2048, KHALF, 1024), idesc,
-            kk > 0);
+    umma_ss(d, da + (((kk >> 2) * KHALF + (kk & 3) * 32) >> 4), db + (((kk >> 2) * QHALF + (kk & 3) * 32) >> 4),
+            idesc, kk > 0);
+}
+// dV / dK: D [128 x 128] (+)= A (TMEM, 16-bit, [128 x 64]) * B [64 q x 128 d] (MN-major, 8 KB halves)
+__device__ __forceinline__ void issue_tn(uint32_t d, uint32_t a_tmem, uint64_t db, uint32_t idesc, bool acc) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) umma_ts(d, a_tmem + kk * 8, db + kk * (2048 >> 4), idesc, (acc || kk > 0) ? 1u : 0u);
+}
+// dQ^T [128 d x 64 q] = K^T (MN-major view of the K tile) * dS^T (MN-major [128 keys x 64 q])
+__device__ __forceinline__ void issue_dq(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) umma_ss(d, da + kk * (2048 >> 4), db + kk * (2048 >> 4), idesc, kk > 0);
 }
 
 template <typename T>
@@ -126,8 +124,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B_KV), 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(B_QF + s), 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(bar(B_QF + s), 2);  // the TMA arrival (with its bytes) + the stats arrival
       mbar_init(bar(B_QE + s), 1);
     }
     mbar_init(bar(B_SF), 1);
@@ -165,12 +163,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
     }
     bool ok = true;
     for (int it = 0; it < n_iter; ++it) {
-      const int s = it & 1;
-      if (it >= 2) ok = mbar_wait(bar(B_QE + s), ((it - 2) >> 1) & 1, p.err, 401);
+      const int s = it % NST;
+      if (it >= NST) ok = mbar_wait(bar(B_QE + s), ((it - NST) / NST) & 1, p.err, 401);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const int h = it_head(it), m0 = it_m0(it);
-      // -lse (log2 domain) and -delta of the 64 queries: plain loads by the warp, then the arrive
+      if (lane == 0) {  // Q and dO tiles first: their latency overlaps the stats loads below
+        const uint32_t q = sb + OFF_Q + s * 2 * QTILE;
+        mbar_expect_tx(bar(B_QF + s), 2 * QTILE);
+        for (int c = 0; c < 2; ++c) {
+          load_half(q + c * QHALF, &p.tq, bar(B_QF + s), p.order_q, 64 * c, start + m0, h);
+          load_half(q + QTILE + c * QHALF, &p.tdo, bar(B_QF + s), p.order_do, 64 * c, start + m0, h);
+        }
+      }
+      // -lse (log2 domain) and -delta of the 64 queries: plain loads by the warp, then the 2nd arrival
       float* st = stat + s * 2 * BM;
       for (int i = lane; i < BM; i += 32) {
         const int qi = m0 + i;
@@ -179,18 +185,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
         st[BM + i] = qi < L ? -p.delta[idx] : 0.f;
       }
       __syncwarp();
-      if (lane == 0) {
-        const uint32_t q = sb + OFF_Q + s * 2 * QTILE;
-        mbar_expect_tx(bar(B_QF + s), 2 * QTILE);
-        for (int c = 0; c < 2; ++c) {
-          load_half(q + c * QHALF, &p.tq, bar(B_QF + s), p.order_q, 64 * c, start + m0, h);
-          load_half(q + QTILE + c * QHALF, &p.tdo, bar(B_QF + s), p.order_do, 64 * c, start + m0, h);
-        }
-      }
+      if (lane == 0) mbar_arrive(bar(B_QF + s));
       issued = it + 1;
     }
     if (lane == 0) {
-      for (int it = max(0, issued - 2); it < issued; ++it) mbar_wait(bar(B_QF + (it & 1)), (it >> 1) & 1, p.err, 402);
+      for (int it = max(0, issued - NST); it < issued; ++it)
+        mbar_wait(bar(B_QF + it % NST), (it / NST) & 1, p.err, 402);
       mbar_wait(bar(B_KV), 0, p.err, 403);
     }
   } else if (warp == 9) {
@@ -200,39 +200,41 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       const uint32_t id_nt = idesc_f16(ab, BN, BM, 0, 0);   // S^T, dP^T
       const uint32_t id_tn = idesc_f16(ab, BN, 128, 0, 1);  // dV, dK
       const uint32_t id_dq = idesc_f16(ab, 128, BM, 1, 1);  // dQ^T
-      const uint32_t sK = sb + OFF_K, sV = sb + OFF_V, sDS = sb + OFF_DS;
+      const uint64_t dK = smem_desc_sw128(sb + OFF_K, 16, 1024), dV = smem_desc_sw128(sb + OFF_V, 16, 1024);
+      const uint64_t dKt = smem_desc_sw128(sb + OFF_K, KHALF, 1024), dDS = smem_desc_sw128(sb + OFF_DS, KHALF, 1024);
+      const uint64_t dQk = smem_desc_sw128(sb + OFF_Q, 16, 1024);      // stage 0 Q, K-major
+      const uint64_t dQm = smem_desc_sw128(sb + OFF_Q, QHALF, 1024);   // stage 0 Q, MN-major
+      constexpr uint64_t kStage = (2 * QTILE) >> 4, kDO = QTILE >> 4;  // stage stride, Q -> dO offset
       bool ok = mbar_wait(bar(B_KV), 0, p.err, 501) && mbar_wait(bar(B_QF), 0, p.err, 502);
       if (ok) {
         tc_fence_after();
-        issue_nt(tmem + T_S, sK, sb + OFF_Q, id_nt);
-        issue_nt(tmem + T_DP, sV, sb + OFF_Q + QTILE, id_nt);
+        issue_nt(tmem + T_S, dK, dQk, id_nt);
+        issue_nt(tmem + T_DP, dV, dQk + kDO, id_nt);
         umma_commit(bar(B_SF));
       }
       for (int it = 0; it < n_iter && ok; ++it) {
-        const int s = it & 1;
-        const uint32_t q = sb + OFF_Q + s * 2 * QTILE;
+        const int s = it % NST;
         // next iteration's S^T / dP^T as soon as the softmax has copied this one out
         if (it + 1 < n_iter) {
-          const int s1 = (it + 1) & 1;
-          ok = mbar_wait(bar(B_SFREE), it & 1, p.err, 503) && mbar_wait(bar(B_QF + s1), ((it + 1) >> 1) & 1, p.err, 504);
+          const int s1 = (it + 1) % NST;
+          ok = mbar_wait(bar(B_SFREE), it & 1, p.err, 503) && mbar_wait(bar(B_QF + s1), ((it + 1) / NST) & 1, p.err, 504);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t q1 = sb + OFF_Q + s1 * 2 * QTILE;
-          issue_nt(tmem + T_S, sK, q1, id_nt);
-          issue_nt(tmem + T_DP, sV, q1 + QTILE, id_nt);
+          issue_nt(tmem + T_S, dK, dQk + s1 * kStage, id_nt);
+          issue_nt(tmem + T_DP, dV, dQk + s1 * kStage + kDO, id_nt);
           umma_commit(bar(B_SF));
         }
         ok = mbar_wait(bar(B_PR), it & 1, p.err, 505);
         if (!ok) break;
         tc_fence_after();
-        issue_tn(tmem + T_DV, tmem + T_P, q + QTILE, id_tn, it > 0);  // dV += P^T dO
-        issue_tn(tmem + T_DK, tmem + T_DS, q, id_tn, it > 0);         // dK += dS^T Q
+        issue_tn(tmem + T_DV, tmem + T_P, dQm + s * kStage + kDO, id_tn, it > 0);  // dV += P^T dO
+        issue_tn(tmem + T_DK, tmem + T_DS, dQm + s * kStage, id_tn, it > 0);        // dK += dS^T Q
         umma_commit(bar(B_PFREE));
         umma_commit(bar(B_QE + s));
         if (it > 0) ok = mbar_wait(bar(B_DQFREE), (it - 1) & 1, p.err, 506);
         if (!ok) break;
         tc_fence_after();
-        issue_dq(tmem + T_DQ, sK, sDS, id_dq);
+        issue_dq(tmem + T_DQ, dKt, dDS, id_dq);
         umma_commit(bar(B_DQF));
       }
       umma_commit(bar(B_DONE));
@@ -246,9 +248,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
     uint8_t* ds_row = smem + OFF_DS + r * 128;
     bool ok = true;
     for (int it = 0; it < n_iter; ++it) {
-      const int s = it & 1;
+      const int s = it % NST;
       const int m0 = it_m0(it);
-      ok = mbar_wait(bar(B_SF), it & 1, p.err, 601) && mbar_wait(bar(B_QF + s), (it >> 1) & 1, p.err, 602);
+      ok = mbar_wait(bar(B_SF), it & 1, p.err, 601) && mbar_wait(bar(B_QF + s), (it / NST) & 1, p.err, 602);
       if (!ok) break;
       tc_fence_after();
       uint32_t sv[64], dp[64];
@@ -352,12 +354,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       tc_fence_before();
       mbar_arrive(bar(B_DQFREE));
       const int h = it_head(it), m0 = it_m0(it);
-      float* base = p.dq_acc + ((static_cast<int64_t>(start) + m0) * p.n_heads + h) * D + d;
+      float* ptr = p.dq_acc + ((static_cast<int64_t>(start) + m0) * p.n_heads + h) * D + d;
       const int64_t step = static_cast<int64_t>(p.n_heads) * D;
       const int nq = min(BM, L - m0);
+      // 8 rows per pass, shifting the row values down: a short loop keeps the code (and the
+      // instruction-cache footprint next to the softmax warps) small
+#pragma unroll 1
+      for (int c = 0; c < nq; c += 8) {
 #pragma unroll
-      for (int c = 0; c < BM; ++c)
-        if (c < nq) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(base + c * step), "f"(__uint_as_float(v[c])) : "memory");
+        for (int i = 0; i < 8; ++i) {
+          if (c + i < nq) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(ptr), "f"(__uint_as_float(v[i])) : "memory");
+          ptr += step;
+        }
+#pragma unroll
+        for (int i = 0; i < 56; ++i) v[i] = v[i + 8];
+      }
     }
   }
   tc_fence_before();

@@ -9,7 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 
-#include "../../include/decik_b200.h"
+#include "decik_b200.h"
 
 namespace decik {
 
