@@ -47,6 +47,9 @@ SIGNATURES = {
     "decik_varlen_attn_bwd": (c_int, [Tensor3, Tensor3, Tensor3, Tensor3, Tensor3, c_void_p, Tensor3, Tensor3,
                                       Tensor3, c_void_p, c_int, c_int, c_int64, c_int, c_int, c_int, c_float,
                                       c_int, c_void_p, c_void_p]),
+    "decik_varlen_attn_bwd_noalloc": (c_int, [Tensor3, Tensor3, Tensor3, Tensor3, Tensor3, c_void_p, Tensor3,
+                                              Tensor3, Tensor3, c_void_p, c_int, c_int, c_int64, c_int, c_int, c_int,
+                                              c_float, c_int, c_void_p]),
 }
 
 _lib = None

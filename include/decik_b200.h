@@ -169,6 +169,25 @@ DECIK_API int decik_varlen_attn_bwd(decik_tensor3 dout, decik_tensor3 q, decik_t
                           int n_rows, int max_len, int64_t n_tok, int n_heads, int n_kv,
                           int head_dim, float scale, int dtype, void* workspace, void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * The same backward for callers that cannot allocate device memory. No counterpart in the
+ * reference (its backward runs inside PyTorch, which allocates freely).
+ *
+ * Arguments and results are those of decik_varlen_attn_bwd without the workspace: the scratch is
+ * a static device array inside this library, sized for n_tok * n_heads <= 16384 (about 8.5 MB,
+ * held on every GPU that loads the library until the process exits). Larger inputs return
+ * DECIK_ERR_INVALID with a message. It is meant for callers whose device memory is owned by a
+ * host framework's pool that forbids raw allocations, or that run where an allocation could
+ * block or fail. The first call on a device looks up the array's address (make it before any
+ * stream capture); every call reuses the same array, so calls whose kernels overlap on the GPU
+ * race with each other. Nothing is allocated or freed.
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int decik_varlen_attn_bwd_noalloc(decik_tensor3 dout, decik_tensor3 q, decik_tensor3 k, decik_tensor3 v,
+                          decik_tensor3 out, const float* lse, decik_tensor3_mut dq,
+                          decik_tensor3_mut dk, decik_tensor3_mut dv, const int32_t* cu_seqlens,
+                          int n_rows, int max_len, int64_t n_tok, int n_heads, int n_kv,
+                          int head_dim, float scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
