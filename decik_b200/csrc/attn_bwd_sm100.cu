@@ -12,12 +12,14 @@
 //   dV  += P^T dO     [128 keys x 128 d]   TS (A = P^T in TMEM), M=128 N=128 K=64
 //   dK  += dS^T Q     [128 x 128]          TS
 //   dQ^T = K^T dS^T   [128 d x 64 q]       SS, both operands MN-major
-//   dQ WG: dQ^T (thread = one d) added to the fp32 dq accumulator, coalesced across the warp
+//   dQ WG: dQ^T (thread = one d) staged in shared memory; a TMA reduce-add adds the [64 x 128]
+//          fp32 tile into the dq accumulator
 // TMEM (512 cols): S^T [0,64) dP^T [64,128) dQ^T [128,192) P^T [192,224) dS^T [224,256)
 //                  dV [256,384) dK [384,512).
 // The softmax WG copies S^T / dP^T to registers and releases them at once, so the MMA warp issues
 // the next iteration's S^T / dP^T while this iteration's softmax runs.
-// 10 warps: 0-3 softmax + dK/dV epilogue (thread = key row), 4-7 dQ (thread = d), 8 TMA, 9 MMA.
+// 14 warps: 0-7 softmax in two column halves + dK/dV epilogue (thread = key row), 8-11 dQ (thread =
+// d), 12 TMA, 13 MMA (event-driven issue: it polls the barriers of its three kinds of work).
 // Every mbarrier wait is bounded (error word + wind-down).
 #include <cudaTypedefs.h>
 
@@ -29,6 +31,7 @@ namespace attn {
 
 int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
                   int n_heads, int dtype, int* order, int box_rows);
+int make_f32_rows_map(CUtensorMap* map, float* ptr, int64_t n_tok, int n_heads, int box_rows);
 int* attn_error_word();
 
 namespace {
@@ -41,12 +44,13 @@ constexpr int KHALF = BN * 128;  // [128 rows x 64] 16-bit half: 16 KB
 constexpr int KTILE = 2 * KHALF;
 constexpr int QHALF = BM * 128;  // [64 rows x 64] half: 8 KB
 constexpr int QTILE = 2 * QHALF;
-constexpr int NTHREADS = 320;
-constexpr int NST = 4;  // Q / dO / stats stages in flight
+constexpr int NTHREADS = 448;  // 14 warps
+constexpr int NST = 3;  // Q / dO / stats stages in flight
 // shared memory map (offsets from a 1024-aligned base)
 constexpr int OFF_K = 0, OFF_V = KTILE, OFF_Q = 2 * KTILE;   // Q[s] at OFF_Q + s * 2 * QTILE, dO after it
 constexpr int OFF_DS = OFF_Q + NST * 2 * QTILE;              // dS^T [128 keys x 64 q], 16 KB
-constexpr int OFF_STAT = OFF_DS + KHALF;                     // [NST][-lse*log2e 64 | -delta 64] fp32
+constexpr int OFF_DQS = OFF_DS + KHALF;                      // dQ staging [64 q][128 d] fp32, 32 KB
+constexpr int OFF_STAT = OFF_DQS + BM * 128 * 4;             // [NST][-lse*log2e 64 | -delta 64] fp32
 constexpr int OFF_BAR = OFF_STAT + NST * 2 * BM * 4;
 enum { B_KV = 0, B_QF = 1, B_QE = B_QF + NST, B_SF = B_QE + NST, B_SFREE, B_PR, B_PFREE, B_DQF, B_DQFREE, B_DONE,
        N_BAR };
@@ -55,7 +59,7 @@ constexpr int kSmem = OFF_TMEM + 16 + 1024;
 constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_P = 192, T_DS = 224, T_DV = 256, T_DK = 384;
 
 struct Params {
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   void* dk;
   int64_t dk_tok, dk_head;
   void* dv;
@@ -129,15 +133,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       mbar_init(bar(B_QE + s), 1);
     }
     mbar_init(bar(B_SF), 1);
-    mbar_init(bar(B_SFREE), 128);
-    mbar_init(bar(B_PR), 128);
+    mbar_init(bar(B_SFREE), 256);
+    mbar_init(bar(B_PR), 256);
     mbar_init(bar(B_PFREE), 1);
     mbar_init(bar(B_DQF), 1);
     mbar_init(bar(B_DQFREE), 128);
     mbar_init(bar(B_DONE), 1);
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == 13) {
     tmem_alloc(sb + OFF_TMEM, 512);
     tmem_relinquish();
   }
@@ -147,7 +151,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM);
   float* stat = reinterpret_cast<float*>(smem + OFF_STAT);
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ---------------------------------------------------------------- TMA producer
     int issued = 0;
     if (lane == 0) {
@@ -155,6 +159,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       prefetch_tmap(&p.tk);
       prefetch_tmap(&p.tv);
       prefetch_tmap(&p.tdo);
+      prefetch_tmap(&p.tdq);
       mbar_expect_tx(bar(B_KV), 2 * KTILE);
       for (int c = 0; c < 2; ++c) {
         load_half(sb + OFF_K + c * KHALF, &p.tk, bar(B_KV), p.order_k, 64 * c, start + n0, kvh);
@@ -193,8 +198,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
         mbar_wait(bar(B_QF + it % NST), (it / NST) & 1, p.err, 402);
       mbar_wait(bar(B_KV), 0, p.err, 403);
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ---------------------------------------------------------------- MMA issue (one thread)
+    // Event-driven: the thread polls the barriers its three kinds of work depend on and issues
+    // whichever is ready, so no wait holds back work that could already run.
     if (lane == 0) {
       constexpr int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t id_nt = idesc_f16(ab, BN, BM, 0, 0);   // S^T, dP^T
@@ -212,39 +219,57 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
         issue_nt(tmem + T_DP, dV, dQk + kDO, id_nt);
         umma_commit(bar(B_SF));
       }
-      for (int it = 0; it < n_iter && ok; ++it) {
-        const int s = it % NST;
-        // next iteration's S^T / dP^T as soon as the softmax has copied this one out
-        if (it + 1 < n_iter) {
-          const int s1 = (it + 1) % NST;
-          ok = mbar_wait(bar(B_SFREE), it & 1, p.err, 503) && mbar_wait(bar(B_QF + s1), ((it + 1) / NST) & 1, p.err, 504);
-          if (!ok) break;
+      int nS = 1, nV = 0, nQ = 0;  // next iteration whose S^T/dP^T, dV/dK, dQ^T is to be issued
+      long long t_last = cycles();
+      while (ok && nQ < n_iter) {
+        bool progress = false;
+        // S^T / dP^T of the next iteration: the softmax copied the previous one out, Q/dO landed
+        if (nS < n_iter && mbar_test(bar(B_SFREE), (nS - 1) & 1) &&
+            mbar_test(bar(B_QF + nS % NST), (nS / NST) & 1)) {
           tc_fence_after();
-          issue_nt(tmem + T_S, dK, dQk + s1 * kStage, id_nt);
-          issue_nt(tmem + T_DP, dV, dQk + s1 * kStage + kDO, id_nt);
+          issue_nt(tmem + T_S, dK, dQk + (nS % NST) * kStage, id_nt);
+          issue_nt(tmem + T_DP, dV, dQk + (nS % NST) * kStage + kDO, id_nt);
           umma_commit(bar(B_SF));
+          ++nS;
+          progress = true;
         }
-        ok = mbar_wait(bar(B_PR), it & 1, p.err, 505);
-        if (!ok) break;
-        tc_fence_after();
-        issue_tn(tmem + T_DV, tmem + T_P, dQm + s * kStage + kDO, id_tn, it > 0);  // dV += P^T dO
-        issue_tn(tmem + T_DK, tmem + T_DS, dQm + s * kStage, id_tn, it > 0);        // dK += dS^T Q
-        umma_commit(bar(B_PFREE));
-        umma_commit(bar(B_QE + s));
-        if (it > 0) ok = mbar_wait(bar(B_DQFREE), (it - 1) & 1, p.err, 506);
-        if (!ok) break;
-        tc_fence_after();
-        issue_dq(tmem + T_DQ, dKt, dDS, id_dq);
-        umma_commit(bar(B_DQF));
+        // dV += P^T dO, dK += dS^T Q once the softmax wrote P^T / dS^T
+        if (nV < nS && mbar_test(bar(B_PR), nV & 1)) {
+          tc_fence_after();
+          const int s = nV % NST;
+          issue_tn(tmem + T_DV, tmem + T_P, dQm + s * kStage + kDO, id_tn, nV > 0);
+          issue_tn(tmem + T_DK, tmem + T_DS, dQm + s * kStage, id_tn, nV > 0);
+          umma_commit(bar(B_PFREE));
+          umma_commit(bar(B_QE + s));
+          ++nV;
+          progress = true;
+        }
+        // dQ^T once dS^T is in shared memory and the dQ warps read the previous dQ^T out
+        if (nQ < nV && (nQ == 0 || mbar_test(bar(B_DQFREE), (nQ - 1) & 1))) {
+          tc_fence_after();
+          issue_dq(tmem + T_DQ, dKt, dDS, id_dq);
+          umma_commit(bar(B_DQF));
+          ++nQ;
+          progress = true;
+        }
+        if (progress) {
+          t_last = cycles();
+        } else if (cycles() - t_last > kWaitLimitCycles) {
+          report(p.err, 503);
+          ok = false;
+        }
       }
       umma_commit(bar(B_DONE));
       mbar_wait(bar(B_DONE), 0, p.err, 507);
     }
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ---------------------------------------------------------------- softmax (thread = key row)
-    const int r = warp * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    // warpgroup `half` handles query columns [32 * half, 32 * half + 32) of every key row
+    const int half = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int key = n0 + r;
+    const int c0 = 32 * half;
     uint8_t* ds_row = smem + OFF_DS + r * 128;
     bool ok = true;
     for (int it = 0; it < n_iter; ++it) {
@@ -253,24 +278,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       ok = mbar_wait(bar(B_SF), it & 1, p.err, 601) && mbar_wait(bar(B_QF + s), (it / NST) & 1, p.err, 602);
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[64], dp[64];
-      tmem_ld32(tmem + lane_off + T_S, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld32(tmem + lane_off + T_S + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-      tmem_ld32(tmem + lane_off + T_DP, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-      tmem_ld32(tmem + lane_off + T_DP + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
+      uint32_t sv[32], dp[32];
+      tmem_ld32(tmem + lane_off + T_S + c0, sv);
+      tmem_ld32(tmem + lane_off + T_DP + c0, dp);
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(bar(B_SFREE));
-      const float4* nl4 = reinterpret_cast<const float4*>(stat + s * 2 * BM);   // -lse * log2e
-      const float4* nd4 = reinterpret_cast<const float4*>(stat + s * 2 * BM + BM);  // -delta
+      const float4* nl4 = reinterpret_cast<const float4*>(stat + s * 2 * BM + c0);       // -lse * log2e
+      const float4* nd4 = reinterpret_cast<const float4*>(stat + s * 2 * BM + BM + c0);  // -delta
       // visible query columns of this key: qc >= key - m0 (causal) and qc < L - m0 (row end)
-      const int qlo = key - m0;
-      const int qhi = key < L ? min(BM, L - m0) : 0;
-      const bool masked = qlo > 0 || qhi < BM;
+      const int qlo = key - m0 - c0;
+      const int qhi = (key < L ? min(BM, L - m0) : 0) - c0;
+      const bool masked = qlo > 0 || qhi < 32;
       const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
-      uint32_t pp[32], dd[32];
+      uint32_t pp[16], dd[16];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 4 query columns per step, as two packed pairs
+      for (int c = 0; c < 8; ++c) {  // 4 query columns per step, as two packed pairs
         const float4 nl = nl4[c], nd = nd4[c];
         float e[4];
         f2split(ffma2(f2(__uint_as_float(sv[4 * c]), __uint_as_float(sv[4 * c + 1])), sc2, f2(nl.x, nl.y)), e[0], e[1]);
@@ -297,55 +320,54 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       if (it > 0) ok = mbar_wait(bar(B_PFREE), (it - 1) & 1, p.err, 603);
       if (!ok) break;
       tc_fence_after();
-      tmem_st32(tmem + lane_off + T_P, pp);
-      tmem_st32(tmem + lane_off + T_DS, dd);
+      tmem_st16(tmem + lane_off + T_P + c0 / 2, pp);
+      tmem_st16(tmem + lane_off + T_DS + c0 / 2, dd);
       // dS^T smem tile is free once the previous dQ^T MMA completed
       if (it > 0) ok = mbar_wait(bar(B_DQF), (it - 1) & 1, p.err, 604);
       if (!ok) break;
 #pragma unroll
-      for (int c = 0; c < 8; ++c)  // 16-byte chunk c of this key's 64 queries, 128B-swizzled
-        *reinterpret_cast<uint4*>(ds_row + ((c ^ (r & 7)) << 4)) =
+      for (int c = 0; c < 4; ++c) {  // 16-byte chunk (c0 / 8 + c) of this key's 64 queries, 128B-swizzled
+        const int chunk = c0 / 8 + c;
+        *reinterpret_cast<uint4*>(ds_row + ((chunk ^ (r & 7)) << 4)) =
             make_uint4(dd[4 * c], dd[4 * c + 1], dd[4 * c + 2], dd[4 * c + 3]);
+      }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar(B_PR));
     }
-    // epilogue: dV and dK (x scale) rows of this key
+    // epilogue: warpgroup 0 writes the dV rows, warpgroup 1 the dK rows (x scale)
     if (ok && mbar_wait(bar(B_DONE), 0, p.err, 605)) {
       tc_fence_after();
       const bool valid = key < L;
       const int64_t tok = static_cast<int64_t>(start) + key;
-      T* dvp = static_cast<T*>(p.dv) + tok * p.dv_tok + static_cast<int64_t>(kvh) * p.dv_head;
-      T* dkp = static_cast<T*>(p.dk) + tok * p.dk_tok + static_cast<int64_t>(kvh) * p.dk_head;
+      const uint32_t base = tmem + lane_off + (half ? T_DK : T_DV);
+      const float mul = half ? p.scale : 1.f;
+      T* dst = half ? static_cast<T*>(p.dk) + tok * p.dk_tok + static_cast<int64_t>(kvh) * p.dk_head
+                    : static_cast<T*>(p.dv) + tok * p.dv_tok + static_cast<int64_t>(kvh) * p.dv_head;
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t base = tmem + lane_off + (which ? T_DK : T_DV);
-        const float mul = which ? p.scale : 1.f;
-        T* dst = which ? dkp : dvp;
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        tmem_ld32(base + 32 * c4, o);
+        tmem_ld_wait();
+        uint32_t w[16];
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t o[32];
-          tmem_ld32(base + 32 * c4, o);
-          tmem_ld_wait();
-          uint32_t w[16];
+        for (int i = 0; i < 16; ++i)
+          w[i] = pk2<T>(__uint_as_float(o[2 * i]) * mul, __uint_as_float(o[2 * i + 1]) * mul);
+        if (valid) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pk2<T>(__uint_as_float(o[2 * i]) * mul, __uint_as_float(o[2 * i + 1]) * mul);
-          if (valid) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              reinterpret_cast<uint4*>(dst + 32 * c4)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-          }
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4*>(dst + 32 * c4)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
     }
-  } else if (warp < 8) {
+  } else if (warp < 12) {
     // ---------------------------------------------------------------- dQ (thread = one of the 128 dims)
     const int d = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     for (int it = 0; it < n_iter; ++it) {
-      if (!mbar_wait(bar(B_DQF), it & 1, p.err, 701)) break;
+      const bool got = mbar_wait(bar(B_DQF), it & 1, p.err, 701);
+      if (!named_bar_and(1, 128, got)) break;  // the 4 warps leave together (they share named barriers)
       tc_fence_after();
       uint32_t v[64];
       tmem_ld32(tmem + lane_off + T_DQ, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
@@ -353,27 +375,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(bar(B_DQFREE));
+      // stage dQ^T as [64 q][128 d] fp32 and let the TMA engine add the tile into the fp32
+      // accumulator: no per-thread global reductions compete with the softmax warps' traffic
       const int h = it_head(it), m0 = it_m0(it);
-      float* ptr = p.dq_acc + ((static_cast<int64_t>(start) + m0) * p.n_heads + h) * D + d;
-      const int64_t step = static_cast<int64_t>(p.n_heads) * D;
-      const int nq = min(BM, L - m0);
-      // 8 rows per pass, shifting the row values down: a short loop keeps the code (and the
-      // instruction-cache footprint next to the softmax warps) small
-#pragma unroll 1
-      for (int c = 0; c < nq; c += 8) {
+      if (d == 0 && it > 0) bulk_wait_read0();  // the previous tile has been read out of the staging buffer
+      named_bar(1, 128);
+      float* stg = reinterpret_cast<float*>(smem + OFF_DQS);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (c + i < nq) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(ptr), "f"(__uint_as_float(v[i])) : "memory");
-          ptr += step;
-        }
-#pragma unroll
-        for (int i = 0; i < 56; ++i) v[i] = v[i + 8];
+      for (int c = 0; c < BM; ++c) stg[c * 128 + d] = __uint_as_float(v[c]);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      named_bar(1, 128);
+      if (d == 0) {
+        tma_reduce_add_3d(&p.tdq, sb + OFF_DQS, 0, h, start + m0);
+        bulk_commit();
       }
     }
+    if (d == 0) bulk_wait0();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -390,6 +411,7 @@ int bwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor
   if (!rc) rc = make_tile_map(&p.tdo, dout.ptr, dout.tok_stride, dout.head_stride, n_tok, n_heads, dtype, &p.order_do, BM);
   if (!rc) rc = make_tile_map(&p.tk, k.ptr, k.tok_stride, k.head_stride, n_tok, n_kv, dtype, &p.order_k, BN);
   if (!rc) rc = make_tile_map(&p.tv, v.ptr, v.tok_stride, v.head_stride, n_tok, n_kv, dtype, &p.order_v, BN);
+  if (!rc) rc = make_f32_rows_map(&p.tdq, dq_acc, n_tok, n_heads, BM);
   if (rc) return rc;
   p.dk = dk.ptr;
   p.dk_tok = dk.tok_stride;
