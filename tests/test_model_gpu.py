@@ -1,0 +1,139 @@
+"""End to end through the reference's patch surface: a tiny Qwen2 (head_dim 128) with NF4 q/k/v/o
+and LoRA on q and v, trained one step on a right-padded batch, with ``decik_b200.solution.apply()``
+(padding-free packing, patched Qwen2Attention.forward / sdpa / RMSNorm / Linear4bit on the sm_100a
+kernels) against the same model on the original transformers code. Mirrors the reference's
+dev/test_cpu_attn.py section 2 (loss and LoRA gradients vs the unpatched path, and every new path
+taken once per layer)."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from tests.qlora_stubs import Linear4bit, LoraLayer
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(device, dtype, lora_dropout):
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    torch.manual_seed(0)
+    cfg = Qwen2Config(vocab_size=300, hidden_size=512, intermediate_size=256, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, max_position_embeddings=512,
+                      tie_word_embeddings=False, rope_theta=1e6)
+    cfg._attn_implementation = "sdpa"
+    model = Qwen2ForCausalLM(cfg).to(device)
+    for layer in model.model.layers:
+        a = layer.self_attn
+        a.q_proj = LoraLayer(Linear4bit(a.q_proj, dtype, device), 16, 32, lora_dropout, device)
+        a.k_proj = Linear4bit(a.k_proj, dtype, device)
+        a.v_proj = LoraLayer(Linear4bit(a.v_proj, dtype, device), 16, 32, lora_dropout, device)
+        a.o_proj = Linear4bit(a.o_proj, dtype, device)
+    for name, p in model.named_parameters():
+        p.requires_grad_("lora_" in name)
+    model.train()
+    return model
+
+
+def _batch(device, lengths, vocab=300):
+    g = torch.Generator().manual_seed(1)
+    B, S = len(lengths), max(lengths)
+    ids = torch.randint(0, vocab, (B, S), generator=g)
+    am = torch.zeros(B, S, dtype=torch.long)
+    lab = torch.full((B, S), -100)
+    for i, L in enumerate(lengths):
+        am[i, :L] = 1
+        lab[i, L // 3:L] = ids[i, L // 3:L]
+    return ids.to(device), am.to(device), lab.to(device)
+
+
+def _step(model, batch, state, dtype):
+    """One training step. The loss is taken on the real tokens as the reference's fused head does
+    (solution/head.py:147-171, shifted labels gathered at packing.index when the decoder ran
+    packed, at the mask's positions otherwise); the head itself is not part of this path."""
+    ids, am, lab = batch
+    model.zero_grad(set_to_none=True)
+    torch.manual_seed(5)
+    state.request, state.packing = True, None
+    try:
+        with torch.autocast("cuda", dtype=dtype):
+            hidden = model.model(input_ids=ids, attention_mask=am, use_cache=False).last_hidden_state
+            packing = state.packing
+            flat = hidden.reshape(-1, hidden.shape[-1])
+            if packing is not None:
+                positions = packing.index
+            else:
+                positions = am.reshape(-1).nonzero().squeeze(1)
+                flat = flat.index_select(0, positions)
+            targets = F.pad(lab, (0, 1), value=-100)[..., 1:].reshape(-1).index_select(0, positions)
+            logits = model.lm_head(flat).float()
+    finally:
+        state.request, state.packing = False, None
+    loss = F.cross_entropy(logits, targets, ignore_index=-100, reduction="sum") / (targets != -100).sum()
+    loss.backward()
+    grads = {n: p.grad.detach().float().clone() for n, p in model.named_parameters() if p.grad is not None}
+    return loss.detach().float(), grads, packing is not None
+
+
+@pytest.fixture()
+def patched_classes():
+    """Saves and restores every class attribute apply() patches."""
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+    from transformers.models.qwen2 import modeling_qwen2 as mq
+
+    saved = [(mq.Qwen2Model, "forward", mq.Qwen2Model.forward),
+             (mq.Qwen2Attention, "forward", mq.Qwen2Attention.forward),
+             (mq.Qwen2RMSNorm, "forward", mq.Qwen2RMSNorm.forward),
+             (torch.nn.Dropout, "forward", torch.nn.Dropout.forward),
+             (Linear4bit, "forward", Linear4bit.forward)]
+    sdpa = ALL_ATTENTION_FUNCTIONS["sdpa"]
+    yield
+    for cls, name, fn in saved:
+        setattr(cls, name, fn)
+    ALL_ATTENTION_FUNCTIONS["sdpa"] = sdpa
+
+
+@pytest.mark.parametrize("lengths,lora_dropout", [([17, 6, 11], 0.0), ([300, 129, 64, 1], 0.0),
+                                                  ([40, 33, 7], 0.1)])
+def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora_dropout):
+    """With LoRA dropout the packed path draws its keep-masks with the base's op on the base's
+    [B, S, H] shape (solution/varlen.py:42-63), so the same seed gives the same masks."""
+    from decik_b200 import solution
+    from decik_b200.solution import _state, attn, varlen
+
+    dtype = torch.bfloat16
+    base = _model("cuda", dtype, lora_dropout)
+    batch = _batch("cuda", lengths)
+    l0, g0, packed0 = _step(base, batch, _state.STATE, dtype)   # original transformers + stub modules
+    assert not packed0
+
+    model = _model("cuda", dtype, lora_dropout)    # same seeds: identical weights
+    solution.apply(linear4bit_cls=Linear4bit, lora_classes=(LoraLayer,))
+    calls = {"rope": 0, "varlen": 0, "pair": 0}
+    orig = {n: getattr(c, "forward") for n, c in (("rope", attn.FusedQKRope), ("varlen", varlen.VarlenSDPA),
+                                                  ("pair", attn.LoRAPairFromNorm))}
+
+    def counting(name):
+        def fwd(ctx, *a):
+            calls[name] += 1
+            return orig[name](ctx, *a)
+        return staticmethod(fwd)
+
+    try:
+        for n, c in (("rope", attn.FusedQKRope), ("varlen", varlen.VarlenSDPA), ("pair", attn.LoRAPairFromNorm)):
+            c.forward = counting(n)
+        l1, g1, packed1 = _step(model, batch, _state.STATE, dtype)
+    finally:
+        for n, c in (("rope", attn.FusedQKRope), ("varlen", varlen.VarlenSDPA), ("pair", attn.LoRAPairFromNorm)):
+            c.forward = orig[n]
+    assert packed1
+    n_layers = len(model.model.layers)
+    assert calls == {"rope": n_layers, "varlen": n_layers, "pair": n_layers}, calls
+    print(f"loss {l0.item():.6f} -> {l1.item():.6f}")
+    assert abs(l1.item() - l0.item()) / abs(l0.item()) < 2e-3, (l1.item(), l0.item())
+    assert set(g1) == set(g0)
+    for name in g0:
+        rel = (g1[name] - g0[name]).norm() / g0[name].norm().clamp(min=1e-12)
+        print(f"{name}: rel-L2 {rel.item():.3e}")
+        assert rel < 2e-2, f"{name}: rel-L2 {rel.item():.3e}"
+    assert cuda_lib.decik_kernel_error(1) == 0
