@@ -216,6 +216,7 @@ def run_reference(args, world, rank):
 def run_ours(args, world, rank, local):
     from decik_b200 import ops
     from decik_b200.block import QLoRAAttentionBlock, rope_cos_sin
+    from decik_b200.dp import GradBucket
     from decik_b200.solution.varlen import packing_from_lengths
 
     dev = torch.device("cuda", local)
@@ -229,20 +230,16 @@ def run_ours(args, world, rank, local):
     x = torch.randn(T, HIDDEN, device=dev, generator=g).requires_grad_(True)
     dout = torch.randn(T, HQ * D, device=dev, generator=g).to(torch.bfloat16)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
-    params = block.lora_params()
-    grad_buf = torch.empty(sum(p.numel() for p in params), dtype=torch.float32, device=dev)
+    bucket = GradBucket(block.lora_params())                         # LoRA grads: views of one fp32 buffer
     if world > 1:
         import torch.distributed as dist
 
     def step(xin, din):
-        for p in params:
-            p.grad = None
+        bucket.zero_()
         xin.grad = None
         out = block.forward(xin, packing, cos, sin)
         out.backward(din)
-        if world > 1:  # data-parallel exchange: one flat all-reduce of the LoRA grads
-            torch.cat([p.grad.reshape(-1) for p in params], out=grad_buf)
-            dist.all_reduce(grad_buf)
+        bucket.all_reduce()   # data-parallel exchange: one flat NCCL all-reduce (no-op at N=1)
         return out
 
     for _ in range(args.warmup):
@@ -282,7 +279,7 @@ def run_ours(args, world, rank, local):
     # end to end through the same public API, inputs from pinned host memory, LoRA grads read back
     x_host = x.detach().cpu().pin_memory()
     d_host = dout.cpu().pin_memory()
-    g_host = torch.empty(grad_buf.numel(), dtype=torch.float32).pin_memory()
+    g_host = torch.empty(bucket.flat.numel(), dtype=torch.float32).pin_memory()
     x_dev = torch.empty_like(x.detach())
     d_dev = torch.empty_like(dout)
 
@@ -291,9 +288,7 @@ def run_ours(args, world, rank, local):
         d_dev.copy_(d_host, non_blocking=True)
         xin = x_dev.detach().requires_grad_(True)
         step(xin, d_dev)
-        if world == 1:
-            torch.cat([p.grad.reshape(-1) for p in params], out=grad_buf)
-        g_host.copy_(grad_buf, non_blocking=True)
+        g_host.copy_(bucket.flat, non_blocking=True)
 
     for _ in range(2):
         e2e_step()
