@@ -44,6 +44,14 @@ SIGNATURES = {
     "decik_varlen_attn_fwd": (c_int, [Tensor3, Tensor3, Tensor3, Tensor3, c_void_p, c_void_p, c_int, c_int,
                                       c_int64, c_int, c_int, c_int, c_float, c_int, c_void_p]),
     "decik_varlen_attn_bwd_workspace": (c_int64, [c_int64, c_int, c_int]),
+    "decik_lora_frag_bytes": (c_int64, [c_int, c_int]),
+    "decik_lora_pack": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                                c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "decik_qkv_epilogue_fwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_float, c_void_p,
+                                       c_void_p, Tensor3, Tensor3, Tensor3, c_void_p, c_int64, c_int, c_int,
+                                       c_int, c_int, c_void_p]),
+    "decik_qkv_epilogue_bwd": (c_int, [Tensor3, Tensor3, c_void_p, c_void_p, c_void_p, c_float, c_void_p,
+                                       c_int64, c_int64, c_int, c_int, c_int, c_int, c_void_p]),
     "decik_varlen_attn_bwd": (c_int, [Tensor3, Tensor3, Tensor3, Tensor3, Tensor3, c_void_p, Tensor3, Tensor3,
                                       Tensor3, c_void_p, c_int, c_int, c_int64, c_int, c_int, c_int, c_float,
                                       c_int, c_void_p, c_void_p]),

@@ -1,6 +1,8 @@
 """The attention block of one decoder layer of the QLoRA step, as a plain object: the forward and
-backward the patched Qwen2Attention.forward runs (solution/attn.py:387-418, without o_proj),
-composed from the reference-facing autograd Functions of ``decik_b200.solution``.
+backward the patched Qwen2Attention.forward runs (solution/attn.py:387-418, without o_proj).
+By default one fused autograd node (``FusedAttentionBlock``: one projection GEMM, the sm_100a
+epilogues and attention kernels); ``fused=False`` composes the reference-facing autograd
+Functions of ``decik_b200.solution`` one by one instead.
 
     block = QLoRAAttentionBlock.random(hidden=1536, n_heads=12, n_kv=2, device="cuda")
     out = block.forward(x, packing)          # [T, n_heads * 128]
@@ -19,7 +21,7 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
-from .solution.attn import FusedQKRope
+from .solution.attn import FusedAttentionBlock, FusedQKRope
 from .solution.nf4 import NF4Linear
 from .solution.varlen import Packing, VarlenSDPA
 
@@ -68,11 +70,16 @@ class QLoRAAttentionBlock:
     def __init__(self, nf4_states: dict, biases: dict, lora: dict, n_heads: int, n_kv: int,
                  head_dim: int = 128, scaling: float = 2.0, dtype=torch.bfloat16, device="cuda"):
         self.n_heads, self.n_kv, self.head_dim = n_heads, n_kv, head_dim
+        self.nf4_states = nf4_states  # the host-side arrays, for checks against the CPU oracle
         self.scaling, self.dtype, self.device = scaling, dtype, device
         self.weights = {n: quant_state_from_arrays(nf4_states[n], device, dtype) for n in ("q", "k", "v")}
         self.bias = {n: biases[n].to(device=device, dtype=torch.float32) for n in ("q", "k", "v")}
         self.lora = {n: lora[n].to(device=device, dtype=torch.float32).requires_grad_(True)
                      for n in ("a_q", "b_q", "a_v", "b_v")}
+        rank = self.lora["a_q"].shape[0]
+        # frozen biases of the fused projection, zero for the two lora_A output groups
+        self.bias_cat = torch.cat([self.bias["q"], self.bias["k"], self.bias["v"],
+                                   torch.zeros(2 * rank, device=device)]).to(dtype)
 
     @classmethod
     def random(cls, hidden=1536, n_heads=12, n_kv=2, head_dim=128, rank=16, alpha=32, seed=0,
@@ -98,10 +105,35 @@ class QLoRAAttentionBlock:
     def lora_params(self):
         return [self.lora[n] for n in ("a_q", "b_q", "a_v", "b_v")]
 
-    def forward(self, x: torch.Tensor, packing: Packing, cos: torch.Tensor, sin: torch.Tensor):
-        """x fp32 [T, hidden] (the normed hidden states) -> attention output [T, n_heads*D] (dtype)."""
+    def dequant_cat(self) -> torch.Tensor:
+        """This step's W_q, W_k, W_v (NF4 -> dtype, bit-exact) as the first rows of a fresh
+        [(Hq+2Hk)*D + 2r, hidden] matrix; the fused forward fills the last 2r rows with A_q, A_v."""
+        from .solution.nf4 import dequantize_nf4
+
+        rows = [self.weights[n][1].shape[0] for n in ("q", "k", "v")]
+        rank = self.lora["a_q"].shape[0]
+        hidden = self.weights["q"][1].shape[1]
+        w = torch.empty((sum(rows) + 2 * rank, hidden), dtype=self.dtype, device=self.device)
+        r0 = 0
+        for n, nr in zip(("q", "k", "v"), rows):
+            packed, qs = self.weights[n]
+            dequantize_nf4(packed, qs, self.dtype, out=w[r0:r0 + nr])
+            r0 += nr
+        return w
+
+    def forward(self, x: torch.Tensor, packing: Packing, cos: torch.Tensor, sin: torch.Tensor,
+                fused: bool = True):
+        """x fp32 [T, hidden] (the normed hidden states) -> attention output [T, n_heads*D] (dtype).
+        ``fused``: one projection GEMM + the sm_100a epilogues (FusedAttentionBlock); otherwise the
+        reference's chain of autograd Functions (NF4Linear x3, LoRA, FusedQKRope, VarlenSDPA)."""
         dt = self.dtype
         T = x.shape[0]
+        if fused:
+            a_q, b_q, a_v, b_v = self.lora_params()
+            out = FusedAttentionBlock.apply(x, a_q, b_q, a_v, b_v, self.dequant_cat(), self.bias_cat, cos, sin,
+                                            packing.cu_seqlens(x.device), packing.max_len, self.n_heads,
+                                            self.n_kv, self.scaling, self.head_dim ** -0.5)
+            return out.view(T, self.n_heads * self.head_dim)
         x16 = x.to(dt)
         (pq, sq), (pk, sk), (pv, sv) = self.weights["q"], self.weights["k"], self.weights["v"]
         q_base = NF4Linear.apply(x16, pq, self.bias["q"].to(dt), sq)

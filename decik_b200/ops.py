@@ -52,6 +52,8 @@ def nf4_dequant(packed: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, 
         raise RuntimeError("decik_b200 nf4_dequant: packed tensor smaller than shape")
     if out is None:
         out = torch.empty((n_out, n_in), dtype=out_dtype, device=packed.device)
+    elif not (out.is_contiguous() and out.numel() == n_out * n_in and out.dtype == out_dtype):
+        raise RuntimeError("decik_b200 nf4_dequant: out must be contiguous [N, K] of out_dtype")
     with _timed("nf4_dequant", 1):
         rc = _lib.lib().decik_nf4_dequant(
             _p(packed), _p(absmax), _p(absmax2) if nested else None, _p(code2) if nested else None,
@@ -221,6 +223,82 @@ def varlen_attn_bwd(dout, q, k, v, out, lse, cu_seqlens, max_len: int, scale: fl
                                               _p(workspace), _stream(q))
     _lib.check(rc, "varlen_attn_bwd")
     return dq, dk, dv
+
+
+# ------------------------------------------------------------------------------------------------
+# projection epilogues (around one fused q|k|v|LoRA-down GEMM)
+# ------------------------------------------------------------------------------------------------
+LORA_RANK = 16
+
+
+def _t3any(t: torch.Tensor) -> Tensor3:
+    """Any 3-D [T, H, D] view with D contiguous (strides in elements)."""
+    if t.dim() != 3 or t.stride(2) != 1:
+        raise RuntimeError("decik_b200: expected a [T, H, D] view with D contiguous")
+    return Tensor3(t.data_ptr(), t.stride(0), t.stride(1))
+
+
+def lora_pack(a_q: torch.Tensor, a_v: torch.Tensor, b_q: torch.Tensor, b_v: torch.Tensor, dtype: torch.dtype,
+              a_out: torch.Tensor | None = None) -> torch.Tensor:
+    """One step's LoRA operands: A_q, A_v rounded to ``dtype`` into the rows of ``a_out`` [32, hidden]
+    (a row slice of the projection weight; optional) and the lora_B fragments both projection
+    epilogues read (a uint8 buffer; keep it from forward to backward)."""
+    _cuda(a_q, a_v, b_q, b_v, a_out)
+    for t in (a_q, a_v, b_q, b_v):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise RuntimeError("decik_b200 lora_pack: LoRA weights must be contiguous fp32")
+    rank, hidden = a_q.shape
+    D = 128
+    n_heads, n_kv = b_q.shape[0] // D, b_v.shape[0] // D
+    frag = torch.empty(int(_lib.lib().decik_lora_frag_bytes(n_heads, n_kv)), dtype=torch.uint8, device=a_q.device)
+    if a_out is not None and (a_out.dtype != dtype or a_out.stride(1) != 1 or tuple(a_out.shape) != (2 * rank, hidden)):
+        raise RuntimeError("decik_b200 lora_pack: a_out must be [2r, hidden] rows of dtype")
+    with _timed("lora_pack", 1):
+        rc = _lib.lib().decik_lora_pack(_p(a_q), _p(a_v), _p(a_out), a_out.stride(0) if a_out is not None else 0,
+                                        hidden, _p(b_q), _p(b_v), _p(frag), n_heads, n_kv, D, rank,
+                                        _DT[dtype], _stream(a_q))
+    _lib.check(rc, "lora_pack")
+    return frag
+
+
+def qkv_epilogue_fwd(y: torch.Tensor, u: torch.Tensor | None, frag: torch.Tensor | None, scaling: float,
+                     cos: torch.Tensor, sin: torch.Tensor, n_heads: int, n_kv: int, want_u: bool = False):
+    """From y [T, >= (Hq+2Hk)*D] (q_base | k | v_base) and u [T, >= 32] (u_q | u_v): q [Hq, T, D]
+    and k [Hk, T, D] head-major with RoPE, v [T, Hk, D], and (want_u) a compact u copy [T, 32]."""
+    _cuda(y, u, frag, cos, sin)
+    T = y.shape[0]
+    D = cos.shape[-1]
+    if y.stride(1) != 1 or (u is not None and u.stride(1) != 1):
+        raise RuntimeError("decik_b200 qkv_epilogue_fwd: y and u need contiguous rows")
+    q = torch.empty((n_heads, T, D), dtype=y.dtype, device=y.device)
+    k = torch.empty((n_kv, T, D), dtype=y.dtype, device=y.device)
+    v = torch.empty((T, n_kv, D), dtype=y.dtype, device=y.device)
+    lora = frag is not None
+    u_out = torch.empty((T, 2 * LORA_RANK), dtype=y.dtype, device=y.device) if (lora and want_u) else None
+    with _timed("qkv_epilogue_fwd", 1):
+        rc = _lib.lib().decik_qkv_epilogue_fwd(
+            _p(y), y.stride(0), _p(u) if lora else None, u.stride(0) if lora else 0, _p(frag),
+            float(scaling), _p(cos), _p(sin), _t3any(q.transpose(0, 1)), _t3any(k.transpose(0, 1)), _t3any(v),
+            _p(u_out), T, n_heads, n_kv, D, _dt(y), _stream(y))
+    _lib.check(rc, "qkv_epilogue_fwd")
+    return q, k, v, u_out
+
+
+def qkv_epilogue_bwd(grad_q: torch.Tensor, grad_k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                     frag: torch.Tensor | None, scaling: float, dy: torch.Tensor, n_heads: int,
+                     n_kv: int) -> torch.Tensor:
+    """grad_q/grad_k: [T, H, D] views. dy [T, ld] must hold dv in its v columns; fills the rest."""
+    _cuda(grad_q, grad_k, cos, sin, frag, dy)
+    T = dy.shape[0]
+    D = cos.shape[-1]
+    if dy.stride(1) != 1:
+        raise RuntimeError("decik_b200 qkv_epilogue_bwd: dy needs contiguous rows")
+    with _timed("qkv_epilogue_bwd", 1):
+        rc = _lib.lib().decik_qkv_epilogue_bwd(
+            _t3any(grad_q), _t3any(grad_k), _p(cos), _p(sin), _p(frag), float(scaling), _p(dy), dy.stride(0),
+            T, n_heads, n_kv, D, _dt(dy), _stream(dy))
+    _lib.check(rc, "qkv_epilogue_bwd")
+    return dy
 
 
 # ------------------------------------------------------------------------------------------------

@@ -37,6 +37,65 @@ class FusedQKRope(torch.autograd.Function):
         return dq, dq.clone(), dk, None, None, None, None
 
 
+class FusedAttentionBlock(torch.autograd.Function):
+    """x -> packed causal GQA attention output [T, Hq, D] in one autograd node, for q/v LoRA
+    without dropout. The arithmetic of the reference's chain (solution/attn.py:395-416: three
+    NF4Linear, LoRAPairFromNorm, FusedQKRope, VarlenSDPA), regrouped so each pass over the tokens
+    does as much as it can:
+
+    forward   y = x16 [W_q; W_k; W_v; A_q; A_v]^T + [b; 0]   one GEMM (the three base projections
+              and both lora_A products share x16); decik_qkv_epilogue_fwd (LoRA-up, v add, RoPE,
+              head-major q/k); decik_varlen_attn_fwd.
+    backward  decik_varlen_attn_bwd with dv written straight into dy; decik_qkv_epilogue_bwd
+              (RoPE^T, du); dX = dy . W_cat (one GEMM, fp32 out: the three NF4Linear input
+              gradients and both LoRA input gradients); dA = du^T x16; dB = scaling . g^T u.
+
+    ``w_cat`` [(Hq+2Hk)*D + 2r, H] holds this step's dequantised W_q, W_k, W_v in its first rows;
+    decik_lora_pack writes A_q, A_v (as dt) into the last 2r rows and the lora_B fragments of both
+    epilogues in the same launch. The matrix is kept for backward, where the reference dequantises
+    again (solution/nf4.py:99-104)."""
+
+    @staticmethod
+    def forward(ctx, x, a_q, b_q, a_v, b_v, w_cat, bias_cat, cos, sin, cu_seqlens, max_len, n_heads,
+                n_kv, scaling, scale):
+        dt = w_cat.dtype
+        D = cos.shape[-1]
+        r = a_q.shape[0]
+        n_proj = (n_heads + 2 * n_kv) * D
+        frag = ops.lora_pack(a_q, a_v, b_q, b_v, dt, a_out=w_cat[n_proj:])
+        x16 = x.to(dt)
+        y = F.linear(x16, w_cat, bias_cat)
+        q, k, v, u = ops.qkv_epilogue_fwd(y, y[:, n_proj:], frag, scaling, cos, sin, n_heads, n_kv, want_u=True)
+        del y
+        out, lse = ops.varlen_attn_fwd(q.transpose(0, 1), k.transpose(0, 1), v, cu_seqlens, max_len, scale)
+        ctx.save_for_backward(x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu_seqlens)
+        ctx.meta = (int(max_len), n_heads, n_kv, float(scaling), float(scale), r)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu = ctx.saved_tensors
+        max_len, n_heads, n_kv, scaling, scale, r = ctx.meta
+        T, D = x16.shape[0], cos.shape[-1]
+        n_q, n_kvd = n_heads * D, n_kv * D
+        n_proj = n_q + 2 * n_kvd
+        dt = x16.dtype
+        dy = torch.empty((T, n_proj + 2 * r), dtype=dt, device=x16.device)
+        dq = torch.empty((T, n_heads, D), dtype=dt, device=x16.device)
+        dk = torch.empty((T, n_kv, D), dtype=dt, device=x16.device)
+        dv = dy[:, n_q + n_kvd:n_proj].view(T, n_kv, D)
+        g = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
+        ops.varlen_attn_bwd(g, q.transpose(0, 1), k.transpose(0, 1), v, out, lse, cu, max_len, scale,
+                            dq=dq, dk=dk, dv=dv)
+        ops.qkv_epilogue_bwd(dq, dk, cos, sin, frag, scaling, dy, n_heads, n_kv)
+        dx = torch.mm(dy, w_cat, out_dtype=torch.float32)
+        da = torch.mm(dy[:, n_proj:].t(), x16, out_dtype=torch.float32)
+        db = torch.mm(dy[:, :n_proj].t(), u, out_dtype=torch.float32)
+        d_bq = db[:n_q, :r] * scaling
+        d_bv = db[n_q + n_kvd:, r:] * scaling
+        return (dx, da[:r], d_bq, da[r:], d_bv) + (None,) * 10
+
+
 def pack_keep(keep_q, keep_v):
     """Two bool keep-masks [T, W] (W % 8 == 0) -> bit-packed uint8 [T, W / 8] each."""
     return ops.keep_pack(keep_q, keep_v)

@@ -33,8 +33,9 @@ def supported(quant_state, n_in=None):
         return False
 
 
-def dequantize_nf4(packed, quant_state, dtype=torch.float16):
-    """[N, K] weights of a bitsandbytes nf4 tensor (packed uint8 + QuantState), solution/nf4.py:66-85."""
+def dequantize_nf4(packed, quant_state, dtype=torch.float16, out=None):
+    """[N, K] weights of a bitsandbytes nf4 tensor (packed uint8 + QuantState), solution/nf4.py:66-85.
+    ``out`` (optional, contiguous [N, K] of ``dtype``) receives them, e.g. rows of a larger matrix."""
     qs = quant_state
     code = qs.code if qs.code.device == packed.device else qs.code.to(packed.device)
     if qs.nested:
@@ -44,8 +45,8 @@ def dequantize_nf4(packed, quant_state, dtype=torch.float16):
         return ops.nf4_dequant(packed, qs.absmax, code, qs.shape, qs.blocksize,
                                absmax2=qs.state2.absmax, code2=qs.state2.code,
                                offset=offset.reshape(1).to(device=packed.device, dtype=torch.float32),
-                               blocksize2=qs.state2.blocksize, out_dtype=dtype)
-    return ops.nf4_dequant(packed, qs.absmax, code, qs.shape, qs.blocksize, out_dtype=dtype)
+                               blocksize2=qs.state2.blocksize, out_dtype=dtype, out=out)
+    return ops.nf4_dequant(packed, qs.absmax, code, qs.shape, qs.blocksize, out_dtype=dtype, out=out)
 
 
 class NF4Linear(torch.autograd.Function):

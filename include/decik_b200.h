@@ -111,6 +111,59 @@ DECIK_API int decik_lora_input_grad(const void* g_q, const void* g_v, const uint
                           const uint8_t* bits_v, float* out, int64_t n_rows, int width,
                           float scale_q, float scale_v, int in_dtype, void* stream);
 
+/* [T, H, D] views: (pointer, token stride, head stride) in elements; D contiguous. */
+typedef struct {
+  const void* ptr;
+  int64_t tok_stride;
+  int64_t head_stride;
+} decik_tensor3;
+
+typedef struct {
+  void* ptr;
+  int64_t tok_stride;
+  int64_t head_stride;
+} decik_tensor3_mut;
+
+/* ---------------------------------------------------------------------------------------------
+ * Projection epilogues: the per-token work between one fused q|k|v|LoRA-down GEMM and attention.
+ * No single reference counterpart: together they replace what the reference's patched
+ * Qwen2Attention.forward (solution/attn.py:395-411) does between its three NF4Linear calls
+ * (solution/nf4.py:93-97), LoRAPairFromNorm (solution/attn.py:217-228) and FusedQKRope
+ * (solution/attn.py:97-111), and the matching backward (solution/attn.py:113-126, :235-273).
+ * head_dim == 128, LoRA rank == 16, dtype F16 or BF16 (dt below).
+ *
+ * decik_lora_pack prepares one step's LoRA operands: A_q, A_v (fp32 [16, hidden]) rounded to dt
+ * into rows 0..15 and 16..31 of a_out (row stride lda; may be NULL to skip), and the lora_B
+ * weights b_q (fp32 [Hq*D, 16]) and b_v (fp32 [Hk*D, 16]) rounded to dt (as peft's b.to(dt)) in
+ * the mma fragment order both epilogues read, into frag (decik_lora_frag_bytes() bytes, 16-byte
+ * aligned). Keep frag from the forward for the backward of the same step.
+ *
+ * Forward: y [T, ldy] of dt holds q_base | k | v_base in columns [0, Hq*D), [Hq*D, (Hq+Hk)*D),
+ * [(Hq+Hk)*D, (Hq+2Hk)*D) (biases already added); u [T, ldu] of dt holds u_q = x16 A16_q^T in
+ * columns [0, 16) and u_v in [16, 32) (u may point into y). frag = NULL: no LoRA term.
+ *   q = rope(f32(q_base) + f32(dt(dt(u_q B16_q^T) * scaling)))   (RoPE exactly as decik_rope_fwd)
+ *   k = rope(k);   v = dt(f32(v_base) + f32(dt(dt(u_v B16_v^T) * scaling)))
+ * q, k, v are [T, H, D] views (8-byte aligned, strides % 4 == 0; head-major q, k for attention).
+ * y and cos/sin 16-byte aligned, ldy % 8 == 0. u_out (may be NULL): a compact [T, 32] copy of u.
+ *
+ * Backward: grad_q, grad_k are the gradients of q and k ([T, H, D] views, 16-byte aligned,
+ * strides % 8 == 0). dy [T, ldy] of dt must hold dv in its v columns on entry; this writes
+ * rope^T(grad_q) and rope^T(grad_k) (exactly as decik_rope_bwd) into the q and k columns and,
+ * with frag, du_q = dt(dt(rope^T(grad_q) * scaling) B16_q) and du_v = dt(dt(dv * scaling) B16_v)
+ * into columns [(Hq+2Hk)*D, +32). Then dX = dy . [W_q; W_k; W_v; A_q; A_v] is one GEMM.
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int64_t decik_lora_frag_bytes(int n_heads, int n_kv);
+DECIK_API int decik_lora_pack(const float* a_q, const float* a_v, void* a_out, int64_t lda, int hidden,
+                    const float* b_q, const float* b_v, void* frag, int n_heads, int n_kv,
+                    int head_dim, int rank, int dtype, void* stream);
+DECIK_API int decik_qkv_epilogue_fwd(const void* y, int64_t ldy, const void* u, int64_t ldu,
+                           const void* frag, float scaling, const float* cos, const float* sin,
+                           decik_tensor3_mut q, decik_tensor3_mut k, decik_tensor3_mut v, void* u_out,
+                           int64_t n_tok, int n_heads, int n_kv, int head_dim, int dtype, void* stream);
+DECIK_API int decik_qkv_epilogue_bwd(decik_tensor3 grad_q, decik_tensor3 grad_k, const float* cos,
+                           const float* sin, const void* frag, float scaling, void* dy, int64_t ldy,
+                           int64_t n_tok, int n_heads, int n_kv, int head_dim, int dtype, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * RMSNorm (Qwen2RMSNorm), the producer of the LoRA input (norm_link recompute).
  * Replaces skc_rmsnorm_fwd_kernel / skc_rmsnorm_bwd_kernel (solution/rmsnorm.py:17-45) and
@@ -139,18 +192,6 @@ DECIK_API int decik_rmsnorm_bwd(const float* dy, const float* x, const void* w, 
  *   cu_seqlens int32 [n_rows + 1] (device), max_len = the longest row.
  *   out [T, n_heads, D]; lse fp32 [n_heads, T] (natural-log logsumexp of the scaled scores).
  * ------------------------------------------------------------------------------------------- */
-typedef struct {
-  const void* ptr;
-  int64_t tok_stride;
-  int64_t head_stride;
-} decik_tensor3;
-
-typedef struct {
-  void* ptr;
-  int64_t tok_stride;
-  int64_t head_stride;
-} decik_tensor3_mut;
-
 DECIK_API int decik_varlen_attn_fwd(decik_tensor3 q, decik_tensor3 k, decik_tensor3 v, decik_tensor3_mut out,
                           float* lse, const int32_t* cu_seqlens, int n_rows, int max_len,
                           int64_t n_tok, int n_heads, int n_kv, int head_dim, float scale,
