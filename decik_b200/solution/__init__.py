@@ -6,7 +6,8 @@
 - ``SKC_RMSNORM``     Qwen2RMSNorm -> sm_100a RMSNorm, recorded as the LoRA input link (rmsnorm.py)
 - ``SKC_VARLEN``      padding-free decoder + varlen attention (varlen.py); ``SKC_VARLEN_ATTN``
 - ``SKC_ATTN``        Qwen2Attention forward: LoRA + RoPE + varlen attention (attn.py);
-                      ``SKC_LORA_RECOMPUTE``
+                      ``SKC_LORA_RECOMPUTE``; ``SKC_FUSED_BLOCK`` (this build's addition: LoRA
+                      without dropout runs as one fused projection + attention node)
 The reference's MLP, head, embedding and warm-up patches are outside this build's scope.
 Patches whose third-party library is not installed (bitsandbytes, peft) are skipped with a
 warning; an eligible input never falls back to a CPU or per-row path.
@@ -37,4 +38,5 @@ def apply(linear4bit_cls=None, lora_classes=None):
         _try(varlen.patch, "Qwen2Model", varlen_attention=_enabled("VARLEN_ATTN"))
         if _enabled("ATTN"):
             _try(attn.patch, "Qwen2Attention", recompute_lora=_enabled("LORA_RECOMPUTE"),
-                 linear4bit_cls=linear4bit_cls, lora_classes=lora_classes)
+                 linear4bit_cls=linear4bit_cls, lora_classes=lora_classes,
+                 fused_block=_enabled("FUSED_BLOCK"))

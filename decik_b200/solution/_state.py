@@ -12,6 +12,9 @@ class _State:
         # (output, input, weight, eps) of the last RMSNorm on the packed path: the q/v LoRA
         # branch rebuilds its input from the norm's input in backward (solution/attn.py:238)
         self.norm_link = None
+        # whether the packed attention runs on the varlen kernels (varlen.patch's switch); the fused
+        # attention block calls them directly, so it follows the same switch
+        self.varlen_attention = False
 
 
 STATE = _State()

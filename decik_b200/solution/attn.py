@@ -242,9 +242,59 @@ def _lora_delta(layer, name, x):
     return layer.lora_B[name](layer.lora_A[name](layer.lora_dropout[name](x))) * layer.scaling[name]
 
 
-def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None):
+def _nf4_parts(module, n_in, dtype):
+    """(packed weight, QuantState, bias or None) of an NF4 linear the fused block can dequantise."""
+    from .nf4 import supported
+
+    weight = getattr(module, "weight", None)
+    qs = getattr(weight, "quant_state", None)
+    bias = getattr(module, "bias", None)
+    if (weight is None or not on_gpu(weight) or weight.dtype != torch.uint8 or weight.requires_grad
+            or getattr(module, "compute_dtype", None) != dtype or not supported(qs, n_in)
+            or (bias is not None and (bias.requires_grad or not on_gpu(bias)))):
+        return None
+    return weight.data, qs, bias
+
+
+def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim):
+    """The attention output [1, T, Hq*D] through FusedAttentionBlock, or None when this layer does not
+    qualify: both LoRA branches without dropout, rank 16 and one scaling; q, k, v NF4 linears of the
+    compute dtype; the varlen attention switched on; head_dim 128."""
+    from .nf4 import dequantize_nf4
+
+    pq, pv = _lora_parts(self.q_proj, q_name), _lora_parts(self.v_proj, v_name)
+    if not (STATE.varlen_attention and head_dim == 128 and pq is not None and pv is not None
+            and pq[3] == 0.0 and pv[3] == 0.0 and pq[2] == pv[2]
+            and pq[0].shape[0] == 16 and pv[0].shape[0] == 16
+            and (not self.training or getattr(self, "attention_dropout", 0.0) == 0.0)):
+        return None
+    hidden = x.shape[-1]
+    parts = [_nf4_parts(m, hidden, dtype) for m in (self.q_proj.base_layer, self.k_proj, self.v_proj.base_layer)]
+    if any(p is None for p in parts):
+        return None
+    rows = [int(p[1].shape[0]) for p in parts]
+    if rows != [n_heads * head_dim, n_kv * head_dim, n_kv * head_dim]:
+        return None
+    n_tok = x.shape[1]
+    w_cat = torch.empty((sum(rows) + 32, hidden), dtype=dtype, device=x.device)
+    biases, r0 = [], 0
+    for (packed, qs, bias), nr in zip(parts, rows):
+        dequantize_nf4(packed, qs, dtype, out=w_cat[r0:r0 + nr])
+        biases.append(bias.float() if bias is not None else torch.zeros(nr, device=x.device))
+        r0 += nr
+    bias_cat = torch.cat(biases + [torch.zeros(32, device=x.device)]).to(dtype)
+    out = FusedAttentionBlock.apply(x.reshape(n_tok, hidden), pq[0], pq[1], pv[0], pv[1], w_cat, bias_cat,
+                                    cos.reshape(n_tok, -1), sin.reshape(n_tok, -1),
+                                    packing.cu_seqlens(x.device), packing.max_len, n_heads, n_kv, pq[2],
+                                    self.scaling)
+    return out.reshape(1, n_tok, -1)
+
+
+def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None, fused_block=True):
     """Patch Qwen2Attention.forward (solution/attn.py:349-421). ``linear4bit_cls`` and
-    ``lora_classes`` default to bitsandbytes' Linear4bit and peft's LoRA layers."""
+    ``lora_classes`` default to bitsandbytes' Linear4bit and peft's LoRA layers. With
+    ``fused_block`` a qualifying layer (LoRA without dropout) runs as one FusedAttentionBlock;
+    the others keep the reference's chain of autograd Functions."""
     from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
     from transformers.models.qwen2 import modeling_qwen2
 
@@ -289,6 +339,10 @@ def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None):
         n_heads = self.config.num_attention_heads
         n_kv = self.config.num_key_value_heads
         x = hidden_states
+        if fused_block:
+            out = _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim)
+            if out is not None:
+                return self.o_proj(out), None
         link = STATE.norm_link
         parts_q = parts_v = None
         if (recompute_lora and link is not None and link[0] is x

@@ -203,6 +203,7 @@ def patch(varlen_attention=True):
 
     forward._skc = True
     model_cls.forward = forward
+    STATE.varlen_attention = bool(varlen_attention)
 
     sdpa = ALL_ATTENTION_FUNCTIONS["sdpa"]
 
