@@ -11,11 +11,12 @@ namespace {
 // ------------------------------------------------------------------------------------------------
 // backward
 // ------------------------------------------------------------------------------------------------
-// delta[h, t] = sum_d dO * O (fp32) and dq_acc = 0. One warp per (token, head), 4 dims per lane.
+// delta[h, t] = sum_d dO * O (fp32), dq_acc = 0 and, when dK / dV are reduced in fp32, their
+// accumulators = 0. One warp per (token, head), 4 dims per lane.
 template <typename T>
 __global__ void __launch_bounds__(256)
 attn_bwd_prep_kernel(Tensor3 dout, Tensor3 out, float* __restrict__ delta, float* __restrict__ dq_acc,
-                     int64_t n_tok, int n_heads) {
+                     float* __restrict__ dk_acc, float* __restrict__ dv_acc, int64_t n_tok, int n_heads, int n_kv) {
   const int lane = threadIdx.x & 31;
   const int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (item >= n_tok * n_heads) return;
@@ -28,24 +29,44 @@ attn_bwd_prep_kernel(Tensor3 dout, Tensor3 out, float* __restrict__ delta, float
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if (lane == 0) delta[static_cast<int64_t>(h) * n_tok + tok] = acc;
-  reinterpret_cast<float4*>(dq_acc + (tok * n_heads + h) * D)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  reinterpret_cast<float4*>(dq_acc + (tok * n_heads + h) * D)[lane] = z;
+  if (dk_acc != nullptr && h < n_kv) {
+    reinterpret_cast<float4*>(dk_acc + (tok * n_kv + h) * D)[lane] = z;
+    reinterpret_cast<float4*>(dv_acc + (tok * n_kv + h) * D)[lane] = z;
+  }
 }
 
-// dq = dq_acc * scale, cast, into dq's strided layout. One thread per 8 dims.
+// dq = scale * dq_acc and, with fp32 dK / dV accumulators, dk = scale * dk_acc and dv = dv_acc,
+// cast into the callers' strided layouts. One thread per 8 dims.
 template <typename T>
 __global__ void __launch_bounds__(256)
-attn_bwd_post_kernel(const float* __restrict__ dq_acc, Tensor3Mut dq, int64_t n_tok, int n_heads, float scale) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n_tok * n_heads * (D / 8)) return;
+attn_bwd_post_kernel(const float* __restrict__ dq_acc, Tensor3Mut dq, const float* __restrict__ dk_acc, Tensor3Mut dk,
+                     const float* __restrict__ dv_acc, Tensor3Mut dv, int64_t n_tok, int n_heads, int n_kv, float scale) {
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nq = n_tok * n_heads * (D / 8);
+  const int64_t nkv = dk_acc != nullptr ? n_tok * n_kv * (D / 8) : 0;
+  const float* src;
+  Tensor3Mut dst;
+  int heads;
+  float mul;
+  if (i < nq) {
+    src = dq_acc; dst = dq; heads = n_heads; mul = scale;
+  } else if (i < nq + nkv) {
+    i -= nq; src = dk_acc; dst = dk; heads = n_kv; mul = scale;
+  } else if (i < nq + 2 * nkv) {
+    i -= nq + nkv; src = dv_acc; dst = dv; heads = n_kv; mul = 1.f;
+  } else {
+    return;
+  }
   const int c = static_cast<int>(i % (D / 8));
   const int64_t th = i / (D / 8);
-  const int h = static_cast<int>(th % n_heads);
-  const int64_t tok = th / n_heads;
-  const float4 a = reinterpret_cast<const float4*>(dq_acc + th * D + c * 8)[0];
-  const float4 b = reinterpret_cast<const float4*>(dq_acc + th * D + c * 8)[1];
-  const float f[8] = {a.x * scale, a.y * scale, a.z * scale, a.w * scale,
-                      b.x * scale, b.y * scale, b.z * scale, b.w * scale};
-  stg16(static_cast<T*>(dq.ptr) + tok * dq.tok + h * dq.head + c * 8, pack8<T>(f));
+  const int h = static_cast<int>(th % heads);
+  const int64_t tok = th / heads;
+  const float4 a = reinterpret_cast<const float4*>(src + th * D + c * 8)[0];
+  const float4 b = reinterpret_cast<const float4*>(src + th * D + c * 8)[1];
+  const float f[8] = {a.x * mul, a.y * mul, a.z * mul, a.w * mul, b.x * mul, b.y * mul, b.z * mul, b.w * mul};
+  stg16(static_cast<T*>(dst.ptr) + tok * dst.tok + h * dst.head + c * 8, pack8<T>(f));
 }
 
 bool ok3(const void* p, int64_t tok, int64_t head) {
@@ -66,8 +87,9 @@ int fwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor
               float scale, int dtype, cudaStream_t stream);
 int bwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor3& v, const decik_tensor3& dout,
               const decik_tensor3_mut& dk, const decik_tensor3_mut& dv, const float* lse, const float* delta,
-              float* dq_acc, const int32_t* cu, int n_rows, int max_len, int64_t n_tok, int n_heads, int n_kv,
-              float scale, int dtype, cudaStream_t stream);
+              float* dq_acc, float* dk_acc, float* dv_acc, int n_split, const int32_t* cu, int n_rows,
+              int max_len, int64_t n_tok, int n_heads, int n_kv, float scale, int dtype, cudaStream_t stream);
+int bwd_sm100_splits(int64_t n_tok, int n_rows, int n_heads, int n_kv);
 }
 }  // namespace decik
 
@@ -89,19 +111,27 @@ extern "C" int decik_varlen_attn_fwd(decik_tensor3 q, decik_tensor3 k, decik_ten
                    as_stream(stream));
 }
 
-extern "C" int64_t decik_varlen_attn_bwd_workspace(int64_t n_tok, int n_heads, int head_dim) {
-  const int64_t dq = n_tok * n_heads * head_dim * 4;
-  const int64_t delta = n_tok * n_heads * 4;
-  return ((dq + 255) / 256) * 256 + ((delta + 255) / 256) * 256;
+namespace {
+int64_t up256(int64_t b) { return ((b + 255) / 256) * 256; }
+}  // namespace
+
+namespace decik {
+namespace attn {
+
+// Workspace bytes: the fp32 dq accumulator and delta; with `kv_acc`, also fp32 dK / dV
+// accumulators, sized for n_kv = n_heads (the largest a caller can have).
+int64_t bwd_workspace_bytes(int64_t n_tok, int n_heads, bool kv_acc) {
+  const int64_t acc = up256(n_tok * n_heads * D * 4);
+  return acc + up256(n_tok * n_heads * 4) + (kv_acc ? 2 * acc : 0);
 }
 
-extern "C" int decik_varlen_attn_bwd(decik_tensor3 dout, decik_tensor3 q, decik_tensor3 k,
-                                     decik_tensor3 v, decik_tensor3 out, const float* lse,
-                                     decik_tensor3_mut dq, decik_tensor3_mut dk,
-                                     decik_tensor3_mut dv, const int32_t* cu_seqlens, int n_rows,
-                                     int max_len, int64_t n_tok, int n_heads, int n_kv,
-                                     int head_dim, float scale, int dtype, void* workspace,
-                                     void* stream) {
+// The backward with a workspace of bwd_workspace_bytes(n_tok, n_heads, allow_split) bytes.
+int varlen_attn_bwd_impl(const decik_tensor3& dout, const decik_tensor3& q, const decik_tensor3& k,
+                         const decik_tensor3& v, const decik_tensor3& out, const float* lse,
+                         const decik_tensor3_mut& dq, const decik_tensor3_mut& dk, const decik_tensor3_mut& dv,
+                         const int32_t* cu_seqlens, int n_rows, int max_len, int64_t n_tok, int n_heads,
+                         int n_kv, int head_dim, float scale, int dtype, void* workspace, bool allow_split,
+                         cudaStream_t s) {
   if (n_rows == 0 || n_tok == 0 || max_len == 0) return DECIK_OK;
   if (head_dim != D) return set_error(DECIK_ERR_UNSUPPORTED, "varlen_attn_bwd: head_dim %d (only 128)", head_dim);
   if (n_rows < 0 || max_len < 0 || n_tok < 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv ||
@@ -115,22 +145,48 @@ extern "C" int decik_varlen_attn_bwd(decik_tensor3 dout, decik_tensor3 q, decik_
     return set_error(DECIK_ERR_INVALID, "varlen_attn_bwd: tensors need 16-byte aligned pointers and strides");
   if (!lse || !cu_seqlens || !workspace || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return set_error(DECIK_ERR_INVALID, "varlen_attn_bwd: null lse/cu_seqlens or workspace not 256-byte aligned");
-  float* dq_acc = static_cast<float*>(workspace);
-  float* delta = reinterpret_cast<float*>(static_cast<char*>(workspace) + ((n_tok * n_heads * D * 4 + 255) / 256) * 256);
-  cudaStream_t s = as_stream(stream);
+  const int n_split = allow_split ? bwd_sm100_splits(n_tok, n_rows, n_heads, n_kv) : 1;
+  char* ws = static_cast<char*>(workspace);
+  const int64_t acc = up256(n_tok * n_heads * D * 4);
+  float* dq_acc = reinterpret_cast<float*>(ws);
+  float* delta = reinterpret_cast<float*>(ws + acc);
+  float* dk_acc = n_split > 1 ? reinterpret_cast<float*>(ws + acc + up256(n_tok * n_heads * 4)) : nullptr;
+  float* dv_acc = n_split > 1 ? reinterpret_cast<float*>(ws + 2 * acc + up256(n_tok * n_heads * 4)) : nullptr;
   return DECIK_DISPATCH_16(dtype, [&] {
     const int64_t items = n_tok * n_heads;
     attn_bwd_prep_kernel<T><<<static_cast<unsigned>((items + 7) / 8), 256, 0, s>>>(
         Tensor3{dout.ptr, dout.tok_stride, dout.head_stride}, Tensor3{out.ptr, out.tok_stride, out.head_stride},
-        delta, dq_acc, n_tok, n_heads);
+        delta, dq_acc, dk_acc, dv_acc, n_tok, n_heads, n_kv);
     int rc = check_launch("varlen_attn_bwd prep");
     if (rc) return rc;
-    rc = bwd_sm100(q, k, v, dout, dk, dv, lse, delta, dq_acc, cu_seqlens, n_rows, max_len, n_tok, n_heads, n_kv,
-                   scale, dtype, s);
+    rc = bwd_sm100(q, k, v, dout, dk, dv, lse, delta, dq_acc, dk_acc, dv_acc, n_split, cu_seqlens, n_rows,
+                   max_len, n_tok, n_heads, n_kv, scale, dtype, s);
     if (rc) return rc;
-    const int64_t n8 = n_tok * n_heads * (D / 8);
+    const int64_t n8 = n_tok * (n_heads + (n_split > 1 ? 2 * n_kv : 0)) * (D / 8);
     attn_bwd_post_kernel<T><<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, s>>>(
-        dq_acc, Tensor3Mut{dq.ptr, dq.tok_stride, dq.head_stride}, n_tok, n_heads, scale);
+        dq_acc, Tensor3Mut{dq.ptr, dq.tok_stride, dq.head_stride}, dk_acc,
+        Tensor3Mut{dk.ptr, dk.tok_stride, dk.head_stride}, dv_acc, Tensor3Mut{dv.ptr, dv.tok_stride, dv.head_stride},
+        n_tok, n_heads, n_kv, scale);
     return check_launch("varlen_attn_bwd post");
   });
+}
+
+}  // namespace attn
+}  // namespace decik
+
+extern "C" int64_t decik_varlen_attn_bwd_workspace(int64_t n_tok, int n_heads, int head_dim) {
+  (void)head_dim;
+  return decik::attn::bwd_workspace_bytes(n_tok, n_heads, true);
+}
+
+extern "C" int decik_varlen_attn_bwd(decik_tensor3 dout, decik_tensor3 q, decik_tensor3 k,
+                                     decik_tensor3 v, decik_tensor3 out, const float* lse,
+                                     decik_tensor3_mut dq, decik_tensor3_mut dk,
+                                     decik_tensor3_mut dv, const int32_t* cu_seqlens, int n_rows,
+                                     int max_len, int64_t n_tok, int n_heads, int n_kv,
+                                     int head_dim, float scale, int dtype, void* workspace,
+                                     void* stream) {
+  return decik::attn::varlen_attn_bwd_impl(dout, q, k, v, out, lse, dq, dk, dv, cu_seqlens, n_rows, max_len, n_tok,
+                                           n_heads, n_kv, head_dim, scale, dtype, workspace, true,
+                                           decik::as_stream(stream));
 }

@@ -27,6 +27,17 @@ namespace {
 constexpr int64_t kNoAllocTokenHeads = 16384;
 constexpr int64_t kNoAllocScratchBytes =
     ((kNoAllocTokenHeads * attn::D * 4 + 255) / 256) * 256 + ((kNoAllocTokenHeads * 4 + 255) / 256) * 256;
+}  // namespace
+namespace attn {
+int64_t bwd_workspace_bytes(int64_t n_tok, int n_heads, bool kv_acc);
+int varlen_attn_bwd_impl(const decik_tensor3& dout, const decik_tensor3& q, const decik_tensor3& k,
+                         const decik_tensor3& v, const decik_tensor3& out, const float* lse,
+                         const decik_tensor3_mut& dq, const decik_tensor3_mut& dk, const decik_tensor3_mut& dv,
+                         const int32_t* cu_seqlens, int n_rows, int max_len, int64_t n_tok, int n_heads,
+                         int n_kv, int head_dim, float scale, int dtype, void* workspace, bool allow_split,
+                         cudaStream_t s);
+}  // namespace attn
+namespace {
 
 static __device__ __align__(256) unsigned char g_bwd_scratch[kNoAllocScratchBytes];
 
@@ -70,11 +81,12 @@ extern "C" int decik_varlen_attn_bwd_noalloc(decik_tensor3 dout, decik_tensor3 q
                      "varlen_attn_bwd_noalloc: %lld tokens x %d heads exceeds the static scratch "
                      "(%lld token-heads); use decik_varlen_attn_bwd with a workspace",
                      (long long)n_tok, n_heads, (long long)kNoAllocTokenHeads);
-  if (decik_varlen_attn_bwd_workspace(n_tok, n_heads, head_dim) > kNoAllocScratchBytes)
+  if (attn::bwd_workspace_bytes(n_tok, n_heads, false) > kNoAllocScratchBytes)
     return set_error(DECIK_ERR_INVALID, "varlen_attn_bwd_noalloc: workspace larger than the static scratch");
   void* scratch = nullptr;
   const int rc = scratch_address(&scratch);
   if (rc) return rc;
-  return decik_varlen_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, cu_seqlens, n_rows, max_len, n_tok, n_heads,
-                               n_kv, head_dim, scale, dtype, scratch, stream);
+  // one head subset per key block: dK / dV stay on chip, so the scratch holds only dq and delta
+  return attn::varlen_attn_bwd_impl(dout, q, k, v, out, lse, dq, dk, dv, cu_seqlens, n_rows, max_len, n_tok, n_heads,
+                                    n_kv, head_dim, scale, dtype, scratch, false, as_stream(stream));
 }

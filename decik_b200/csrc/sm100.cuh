@@ -97,6 +97,7 @@ __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, uint32
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void named_bar(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -164,6 +165,13 @@ template <int N>
 __device__ __forceinline__ void reg_alloc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
 template <int N>
 __device__ __forceinline__ void reg_dealloc() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+// moves the warpgroup from `From` registers per thread (its launch count) to `To`
+template <int From, int To>
+__device__ __forceinline__ void reg_set() {
+  static_assert(To % 8 == 0 && To >= 24 && To <= 256, "setmaxnreg count");
+  if constexpr (To > From) reg_alloc<To>();
+  else if constexpr (To < From) reg_dealloc<To>();
+}
 
 // the mbarrier arrives once every tcgen05 op this thread issued so far has completed
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -273,6 +281,31 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
+}
+
+// 2^x of two values on the FMA and integer pipes, leaving the MUFU/conversion pipe to the 16-bit
+// packs. Cody-Waite style reduction: adding 1.5 * 2^23 rounds x to the nearest integer j (its low
+// mantissa bits), f = x - j lies in [-1/2, 1/2]; 2^f comes from a cubic fitted here to 2^f on that
+// interval with relative weights (iterated weighted least squares; max relative error 7.5e-5 in
+// fp32 Horner form); 2^j is added to the exponent field: (bits of x + 1.5 * 2^23) << 23 = j << 23.
+// x is clamped to -126 first, so -inf gives a denormal-sized result instead of NaN (callers that
+// need exact zeros mask them).
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  float a, b;
+  f2split(x, a, b);
+  x = f2(fmaxf(a, -126.f), fmaxf(b, -126.f));
+  const uint64_t magic = f2(12582912.f, 12582912.f);
+  const uint64_t t = fadd2(x, magic);
+  const uint64_t j = fadd2(t, f2(-12582912.f, -12582912.f));
+  const uint64_t f = fadd2(x, fmul2(j, f2(-1.f, -1.f)));
+  uint64_t p = ffma2(f2(0.05517132207751274f, 0.05517132207751274f), f, f2(0.24261054396629333f, 0.24261054396629333f));
+  p = ffma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
+  p = ffma2(p, f, f2(0.9999281167984009f, 0.9999281167984009f));
+  float pa, pb, ta, tb;
+  f2split(p, pa, pb);
+  f2split(t, ta, tb);
+  return f2(__uint_as_float(__float_as_uint(pa) + (__float_as_uint(ta) << 23)),
+            __uint_as_float(__float_as_uint(pb) + (__float_as_uint(tb) << 23)));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

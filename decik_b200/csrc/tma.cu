@@ -75,15 +75,17 @@ int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t
 
 // A 3-D map over an fp32 [T, H, 128] tensor (dims ordered d, head, token; head stride 512 B) whose
 // box is box_rows tokens x one head x 128 dims, no swizzle: the target of the dq tile reductions.
-int make_f32_rows_map(CUtensorMap* map, float* ptr, int64_t n_tok, int n_heads, int box_rows) {
+// fp32 [n_tok, n_heads, 128] accumulator (dq, dk, dv) for TMA reduce-add of [box_rows x 16] chunks
+// staged with the 64-byte swizzle (16 fp32 = 64 bytes per row).
+int make_f32_chunk_map(CUtensorMap* map, float* ptr, int64_t n_tok, int n_heads, int box_rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return set_error(DECIK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(n_heads), static_cast<cuuint64_t>(n_tok)};
   cuuint64_t strides[2] = {128 * 4, static_cast<cuuint64_t>(n_heads) * 128 * 4};
-  cuuint32_t box[3] = {128, 1, static_cast<cuuint32_t>(box_rows)}, estr[3] = {1, 1, 1};
+  cuuint32_t box[3] = {16, 1, static_cast<cuuint32_t>(box_rows)}, estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(DECIK_ERR_INVALID, "cuTensorMapEncodeTiled (fp32 rows) failed (%d)", static_cast<int>(r));
+                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(DECIK_ERR_INVALID, "cuTensorMapEncodeTiled (fp32 chunks) failed (%d)", static_cast<int>(r));
   return DECIK_OK;
 }
 

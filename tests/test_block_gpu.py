@@ -73,16 +73,14 @@ def test_block_matches_oracle(cuda_lib, fused, dtype):
 
 def test_fused_block_ragged_and_repeatable(cuda_lib):
     """Token counts that are not multiples of the 16-token tiles and a one-token row. Two runs give
-    the same forward and the same v-side gradients bit for bit; the query-side gradients go through
-    the attention backward's dQ reduce-add, whose order across key blocks is not fixed, so they
-    agree to rounding."""
+    the same forward bit for bit; the gradients go through the attention backward's fp32 reduce-adds
+    (dQ always, dK / dV when a key block's query heads are split over several CTAs), whose order is
+    not fixed, so they agree to rounding."""
     case = _case(torch.bfloat16, lengths=[1, 300, 17, 2, 129], seed=3)
     a = _run(*case, fused=True)
     b = _run(*case, fused=True)
-    out_a, dx_a, daq_a, dbq_a, dav_a, dbv_a = a
-    out_b, dx_b, daq_b, dbq_b, dav_b, dbv_b = b
-    assert torch.equal(out_a, out_b) and torch.equal(dav_a, dav_b) and torch.equal(dbv_a, dbv_b)
-    for t, u in ((dx_a, dx_b), (daq_a, daq_b), (dbq_a, dbq_b)):
+    assert torch.equal(a[0], b[0])
+    for t, u in zip(a[1:], b[1:]):
         assert (t - u).norm() <= 1e-3 * u.norm()
     ref = _oracle(*case)
     for name, g, e in zip(("out", "dx", "dA_q", "dB_q", "dA_v", "dB_v"), a, ref):
