@@ -374,7 +374,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       if (!ok) continue;
       tc_fence_after();
       const float* st = stat + s * 2 * BM;
-      const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
 #pragma unroll 1
       for (int h2 = 0; h2 < 2 && ok; ++h2) {
         const int c0 = 64 * wg + 32 * h2;  // query column of this pass
@@ -389,25 +388,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
         const int qhi = (key < L ? min(BM, L - m0) : 0) - c0;
         const bool masked = qlo > 0 || qhi < 32;
         uint32_t pp[16], dd[16];
+        const float sc = p.scale_log2;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {  // 4 query columns per step, as two packed pairs
+        for (int c = 0; c < 8; ++c) {  // 4 query columns per step
           const float4 nl = nl4[c], nd = nd4[c];
-          float e[4];
-          f2split(ffma2(f2(__uint_as_float(sv[4 * c]), __uint_as_float(sv[4 * c + 1])), sc2, f2(nl.x, nl.y)), e[0], e[1]);
-          f2split(ffma2(f2(__uint_as_float(sv[4 * c + 2]), __uint_as_float(sv[4 * c + 3])), sc2, f2(nl.z, nl.w)), e[2], e[3]);
+          const float nls[4] = {nl.x, nl.y, nl.z, nl.w}, nds[4] = {nd.x, nd.y, nd.z, nd.w};
+          float e[4], g[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) e[i] = ptx::ex2(e[i]);
+          for (int i = 0; i < 4; ++i) e[i] = ptx::ex2(fmaf(__uint_as_float(sv[4 * c + i]), sc, nls[i]));
           if (masked) {
 #pragma unroll
             for (int i = 0; i < 4; ++i)
               if (4 * c + i < qlo || 4 * c + i >= qhi) e[i] = 0.f;
           }
-          const uint64_t p01 = f2(e[0], e[1]), p23 = f2(e[2], e[3]);
-          const uint64_t g01 = fmul2(p01, fadd2(f2(__uint_as_float(dp[4 * c]), __uint_as_float(dp[4 * c + 1])), f2(nd.x, nd.y)));
-          const uint64_t g23 = fmul2(p23, fadd2(f2(__uint_as_float(dp[4 * c + 2]), __uint_as_float(dp[4 * c + 3])), f2(nd.z, nd.w)));
-          float g[4];
-          f2split(g01, g[0], g[1]);
-          f2split(g23, g[2], g[3]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) g[i] = e[i] * (__uint_as_float(dp[4 * c + i]) + nds[i]);
           pp[2 * c] = pk2<T>(e[0], e[1]);
           pp[2 * c + 1] = pk2<T>(e[2], e[3]);
           dd[2 * c] = pk2<T>(g[0], g[1]);
@@ -494,11 +489,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
 
 // Number of head subsets per (key block, kv head): enough CTAs to fill the GPU about three times,
 // never more than the group size. One subset keeps dK / dV on chip (no fp32 accumulators).
+constexpr int kSplitWaves = 3;
 int bwd_sm100_splits(int64_t n_tok, int n_rows, int n_heads, int n_kv) {
   const int groups = n_heads / n_kv;
   const int64_t base = ((n_tok + BN - 1) / BN + n_rows) * static_cast<int64_t>(n_kv);
-  const int64_t want = (3 * static_cast<int64_t>(sm_count()) + base - 1) / std::max<int64_t>(base, 1);
-  return static_cast<int>(std::min<int64_t>(std::max<int64_t>(want, 1), groups));
+  const int64_t want = std::min<int64_t>(
+      std::max<int64_t>((kSplitWaves * static_cast<int64_t>(sm_count()) + base - 1) / std::max<int64_t>(base, 1), 1),
+      groups);
+  const int per = static_cast<int>((groups + want - 1) / want);  // heads per subset
+  return (groups + per - 1) / per;                                // no empty subset
 }
 
 int bwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor3& v, const decik_tensor3& dout,
