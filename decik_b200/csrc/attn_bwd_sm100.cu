@@ -6,21 +6,22 @@
 // CTA = one 128-key block of one row x one kv head x one subset of the group's query heads. It
 // loops over its query heads and the 128-query blocks at or below the diagonal. Per iteration
 // (S^T etc. are key-major; every MMA is M=128 N=128, kind::f16):
-//   S^T  = K Q^T      SS              -> TMEM S/P
-//   dP^T = V dO^T     SS              -> TMEM dP/dQ
-//   softmax warps: P^T = exp2(S^T*scale*log2e - lse*log2e) -> TMEM (16-bit, over the S^T columns
-//                  each warpgroup has read), dS^T = P^T (dP^T - delta) -> shared memory
+//   S^T  = K Q^T      SS              -> TMEM S
+//   dP^T = V dO^T     SS              -> TMEM dP/P/dQ
+//   softmax warps: P^T = exp2(S^T*scale*log2e - lse*log2e) -> TMEM (16-bit, over dP^T columns the
+//                  same warpgroup has read), dS^T = P^T (dP^T - delta) -> shared memory
 //   dV  += P^T dO     TS (A = P^T in TMEM)
 //   dK  += dS^T Q     SS (A = dS^T, K-major)
-//   dQ   = dS K       SS (A = the same dS^T tile read MN-major)  -> TMEM dP/dQ once dP^T is read
+//   dQ   = dS K       SS (A = the same dS^T tile read MN-major)  -> TMEM dP/P/dQ after dV
 //   dQ warps: read dQ out of TMEM at once (freeing the columns for the next dP^T), then stream it as
 //   16-column fp32 chunks through two staging buffers (64-byte swizzle) into the fp32 dq
 //   accumulator by TMA bulk reduce-add, concurrently with the next softmax.
-// TMEM (512 columns): dK [0,128) dV [128,256) dP^T/dQ [256,384) S^T/P^T [384,512).
-// Issue order per iteration i: dV(i), dQ(i), dK(i), S(i+1), dP(i+1). dQ(i) may only overwrite the
-// dP^T columns after the softmax read dP^T(i) (it has: dS(i) exists); dP(i+1) waits until the dQ
-// warps read dQ(i) out; S(i+1) overwrites P^T(i) after dV(i) in issue order (tcgen05 MMAs of one
-// thread execute in order).
+// TMEM (512 columns): dK [0,128) dV [128,256) dP^T/P^T/dQ [256,384) S^T [384,512). The softmax
+// warpgroups take interleaved 32-query blocks (w and w + 2), so each writes P^T only over dP^T
+// columns it has itself read. Issue order per iteration i: S(i+1) as soon as both warpgroups have
+// loaded S^T(i) (it runs under their softmax), dV(i), dQ(i), dP(i+1), dK(i). dQ(i) overwrites P^T(i)
+// after dV(i) in issue order (tcgen05 MMAs of one thread execute in order); dP(i+1) waits until
+// the dQ warps read dQ(i) out; dK(i) runs under the next softmax.
 // With more than one head subset per key block, dK / dV go to fp32 accumulators by TMA reduce-add
 // (the caller casts them); with one, they are written directly. Blocks are launched key block 0
 // first (the longest: it sees every query of its row).
@@ -56,8 +57,8 @@ constexpr int OFF_DO = 4 * TILE, OFF_DS = 5 * TILE;       // dO (one stage), dS^
 constexpr int OFF_STG = 6 * TILE;                          // dQ staging: two chunk buffers
 constexpr int OFF_STAT = OFF_STG + 2 * CHUNK;              // [2][-lse*log2e 128 | -delta 128] fp32
 constexpr int OFF_BAR = OFF_STAT + 2 * 2 * BM * 4;
-enum { B_KV = 0, B_QF, B_QF1, B_QE, B_QE1, B_DOF, B_DOE, B_SF, B_DPF, B_PF, B_DSF, B_DSFREE, B_DQF, B_DQFREE,
-       B_DONE, N_BAR };
+enum { B_KV = 0, B_QF, B_QF1, B_QE, B_QE1, B_DOF, B_DOE, B_SF, B_SREAD, B_DPF, B_PF, B_DSF, B_DSFREE, B_DQF,
+       B_DQFREE, B_DONE, N_BAR };
 constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
 constexpr int kSmem = OFF_TMEM + 16 + 1024;
 constexpr uint32_t T_DK = 0, T_DV = 128, T_DPQ = 256, T_SP = 384;
@@ -121,11 +122,14 @@ __device__ __forceinline__ void issue_ss_mm(uint32_t d, uint64_t a, uint64_t b, 
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) umma_ss(d, kstep_mn(a, kk), kstep_mn(b, kk), idesc, (acc || kk > 0) ? 1u : 0u);
 }
-// dV += P^T dO: P^T of queries [0,64) sits in S/P columns [0,32), queries [64,128) in [64,96)
+// TMEM column (16-bit pairs) of P^T for the 32-query block b, within the dP^T/P^T columns: the
+// softmax warpgroup that owns block b writes it over dP^T columns it has already read
+__host__ __device__ constexpr int p_col(int b) { return 16 * (b >> 1) + 32 * (b & 1); }
+// dV += P^T dO: k-step kk covers queries [16 kk, 16 kk + 16), i.e. block kk / 2
 __device__ __forceinline__ void issue_pv(uint32_t d, uint32_t p_tmem, uint64_t b, uint32_t idesc, bool acc) {
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    umma_ts(d, p_tmem + (kk >> 2) * 64 + (kk & 3) * 8, kstep_mn(b, kk), idesc, (acc || kk > 0) ? 1u : 0u);
+    umma_ts(d, p_tmem + p_col(kk >> 1) + (kk & 1) * 8, kstep_mn(b, kk), idesc, (acc || kk > 0) ? 1u : 0u);
 }
 
 template <typename T>
@@ -177,6 +181,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
     mbar_init(bar(B_DOF), 1);
     mbar_init(bar(B_DOE), 1);
     mbar_init(bar(B_SF), 1);
+    mbar_init(bar(B_SREAD), 256);
     mbar_init(bar(B_DPF), 1);
     mbar_init(bar(B_PF), 256);
     mbar_init(bar(B_DSF), 256);
@@ -212,6 +217,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       load_tile(sb + OFF_K, &p.tk, bar(B_KV), p.order_k, start + n0, kvh);
       load_tile(sb + OFF_V, &p.tv, bar(B_KV), p.order_v, start + n0, kvh);
     }
+    // -lse * log2e and -delta of iteration j's 128 queries, 4 + 4 per lane, loaded one iteration
+    // ahead so that their latency hides behind the waits below
+    float nl[4], nd[4];
+    auto fetch_stats = [&](int j) {
+      const int hj = it_head(j), mj = it_m0(j);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int qi = mj + lane + 32 * k;
+        const int64_t idx = static_cast<int64_t>(hj) * p.n_tok + start + qi;
+        nl[k] = qi < L ? -__ldg(p.lse + idx) * kLog2e : -INFINITY;
+        nd[k] = qi < L ? -__ldg(p.delta + idx) : 0.f;
+      }
+    };
+    fetch_stats(0);
     bool ok = true;
     for (int it = 0; it < n_iter && ok; ++it) {
       const int s = it & 1;
@@ -225,14 +244,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
         load_tile(sb + OFF_Q + s * TILE, &p.tq, bar(B_QF + s), p.order_q, start + m0, h);
       }
       float* st = stat + s * 2 * BM;
-      for (int i = lane; i < BM; i += 32) {
-        const int qi = m0 + i;
-        const int64_t idx = static_cast<int64_t>(h) * p.n_tok + start + qi;
-        st[i] = qi < L ? -p.lse[idx] * kLog2e : -INFINITY;
-        st[BM + i] = qi < L ? -p.delta[idx] : 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        st[lane + 32 * k] = nl[k];
+        st[BM + lane + 32 * k] = nd[k];
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(B_QF + s));
+      if (it + 1 < n_iter) fetch_stats(it + 1);
       issued_q = it + 1;
       // the single dO stage is free once dV of iteration it - 1 completed
       if (it >= 1) ok = mbar_wait(bar(B_DOE), (it - 1) & 1, p.err, 402);
@@ -252,7 +271,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
     }
   } else if (warp == 13) {
     // ---------------------------------------------------------------- MMA issue (one thread)
-    // Per iteration: dV(it), dQ(it), dK(it), S(it+1), dP(it+1).
+    // Per iteration: S(it+1) (under the softmax of it), dV(it), dQ(it), dP(it+1), dK(it).
     if (lane == 0) {
       constexpr int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t id_kk = idesc_f16(ab, 128, 128, 0, 0);  // S^T, dP^T
@@ -278,29 +297,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       }
       for (int it = 0; it < n_iter && ok; ++it) {
         const int s = it & 1;
-        // dV += P^T dO once the softmax wrote P^T(it); frees dO
+        if (it + 1 < n_iter) {
+          // S^T(it+1) once the softmax loaded S^T(it): runs under the softmax of it
+          ok = mbar_wait(bar(B_SREAD), it & 1, p.err, 510) &&
+               mbar_wait(bar(B_QF + (s ^ 1)), ((it + 1) >> 1) & 1, p.err, 506);
+          if (!ok) break;
+          tc_fence_after();
+          issue_ss_kk(tmem + T_SP, dKk, dQk0 + (s ^ 1) * kStage, id_kk, false);
+          umma_commit(bar(B_SF));
+        }
+        // dV += P^T dO once the softmax wrote P^T(it) (over the dP^T columns); frees dO
         ok = mbar_wait(bar(B_PF), it & 1, p.err, 504);
         if (!ok) break;
         tc_fence_after();
-        issue_pv(tmem + T_DV, tmem + T_SP, dOm, id_km, it > 0);
+        issue_pv(tmem + T_DV, tmem + T_DPQ, dOm, id_km, it > 0);
         umma_commit(bar(B_DOE));
-        // dQ(it) = dS K into the dP^T columns (the softmax read dP^T(it) before it wrote dS)
+        // dQ(it) = dS K over the dP^T / P^T columns: after dV(it) in issue order, and the softmax read
+        // dP^T(it) before it wrote dS
         ok = mbar_wait(bar(B_DSF), it & 1, p.err, 505);
         if (!ok) break;
         tc_fence_after();
         issue_ss_mm(tmem + T_DPQ, dSm, dKm, id_mm, false);
         umma_commit(bar(B_DQF));
-        // dK += dS^T Q(it); frees dS^T and the Q stage
-        issue_ss_km(tmem + T_DK, dSk, dQm0 + s * kStage, id_km, it > 0);
-        umma_commit(bar(B_DSFREE));
-        umma_commit(bar(B_QE + s));
         if (it + 1 < n_iter) {
-          // S^T(it+1) over P^T(it): dV(it) read it first (issue order)
-          ok = mbar_wait(bar(B_QF + (s ^ 1)), ((it + 1) >> 1) & 1, p.err, 506);
-          if (!ok) break;
-          tc_fence_after();
-          issue_ss_kk(tmem + T_SP, dKk, dQk0 + (s ^ 1) * kStage, id_kk, false);
-          umma_commit(bar(B_SF));
           // dP^T(it+1) once dO(it+1) landed and the dQ warps read dQ(it) out
           ok = mbar_wait(bar(B_DOF), (it + 1) & 1, p.err, 507) && mbar_wait(bar(B_DQFREE), it & 1, p.err, 508);
           if (!ok) break;
@@ -308,6 +327,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
           issue_ss_kk(tmem + T_DPQ, dVk, dOk, id_kk, false);
           umma_commit(bar(B_DPF));
         }
+        // dK += dS^T Q(it) (runs under the next softmax); frees dS^T and the Q stage
+        issue_ss_km(tmem + T_DK, dSk, dQm0 + s * kStage, id_km, it > 0);
+        umma_commit(bar(B_DSFREE));
+        umma_commit(bar(B_QE + s));
       }
       umma_commit(bar(B_DONE));
       mbar_wait(bar(B_DONE), 0, p.err, 509);
@@ -359,7 +382,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
     const int key = n0 + r;
     const int bar_id = 1 + wg;                     // named barrier of this warpgroup
     const bool leader = (warp & 3) == 0 && lane == 0;
-    uint8_t* ds_half = smem + OFF_DS + wg * HALF + r * 128;
+    uint8_t* ds_row = smem + OFF_DS + r * 128;
     bool ok = true;
     // a bounded wait, made uniform across the warp (the TMEM accesses below are warp-collective)
     auto wait_w = [&](int b, int parity, int code) -> bool {
@@ -376,11 +399,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       const float* st = stat + s * 2 * BM;
 #pragma unroll 1
       for (int h2 = 0; h2 < 2 && ok; ++h2) {
-        const int c0 = 64 * wg + 32 * h2;  // query column of this pass
+        const int blk = 2 * h2 + wg;       // 32-query block of this pass: warpgroup w takes w, w + 2
+        const int c0 = 32 * blk;           // its first query column
         uint32_t sv[32], dp[32];
         tmem_ld32(tmem + lane_off + T_SP + c0, sv);
         tmem_ld32(tmem + lane_off + T_DPQ + c0, dp);
         tmem_ld_wait();
+        if (h2 == 1) {  // both blocks of S^T(it) are in registers: S^T(it+1) may overwrite them
+          tc_fence_before();
+          mbar_arrive(bar(B_SREAD));
+        }
         const float4* nl4 = reinterpret_cast<const float4*>(st + c0);       // -lse * log2e
         const float4* nd4 = reinterpret_cast<const float4*>(st + BM + c0);  // -delta
         // visible query columns of this key: q >= key (causal) and q < L (row end)
@@ -408,15 +436,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
           dd[2 * c] = pk2<T>(g[0], g[1]);
           dd[2 * c + 1] = pk2<T>(g[2], g[3]);
         }
-        // P^T over S^T columns this warpgroup has already read: [64 wg + 16 h2, +16)
-        tmem_st16(tmem + lane_off + T_SP + 64 * wg + 16 * h2, pp);
+        // P^T over dP^T columns this warpgroup has already read
+        tmem_st16(tmem + lane_off + T_DPQ + p_col(blk), pp);
         // dS^T into shared memory once dQ(it - 1) / dK(it - 1) have read the previous one
         if (h2 == 0 && it > 0) ok = wait_w(B_DSFREE, (it - 1) & 1, 605);
         if (!ok) break;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {  // 16-byte unit (4 h2 + c) of this key's 64 queries, 128B-swizzled
-          const int unit = 4 * h2 + c;
-          *reinterpret_cast<uint4*>(ds_half + ((unit ^ (r & 7)) << 4)) =
+        for (int c = 0; c < 4; ++c) {  // 16-byte unit of this key's row in its 64-query half, 128B-swizzled
+          const int unit = 4 * (blk & 1) + c;
+          *reinterpret_cast<uint4*>(ds_row + (blk >> 1) * HALF + ((unit ^ (r & 7)) << 4)) =
               make_uint4(dd[4 * c], dd[4 * c + 1], dd[4 * c + 2], dd[4 * c + 3]);
         }
       }

@@ -283,31 +283,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-// 2^x of two values on the FMA and integer pipes, leaving the MUFU/conversion pipe to the 16-bit
-// packs. Cody-Waite style reduction: adding 1.5 * 2^23 rounds x to the nearest integer j (its low
-// mantissa bits), f = x - j lies in [-1/2, 1/2]; 2^f comes from a cubic fitted here to 2^f on that
-// interval with relative weights (iterated weighted least squares; max relative error 7.5e-5 in
-// fp32 Horner form); 2^j is added to the exponent field: (bits of x + 1.5 * 2^23) << 23 = j << 23.
-// x is clamped to -126 first, so -inf gives a denormal-sized result instead of NaN (callers that
-// need exact zeros mask them).
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
-  float a, b;
-  f2split(x, a, b);
-  x = f2(fmaxf(a, -126.f), fmaxf(b, -126.f));
-  const uint64_t magic = f2(12582912.f, 12582912.f);
-  const uint64_t t = fadd2(x, magic);
-  const uint64_t j = fadd2(t, f2(-12582912.f, -12582912.f));
-  const uint64_t f = fadd2(x, fmul2(j, f2(-1.f, -1.f)));
-  uint64_t p = ffma2(f2(0.05517132207751274f, 0.05517132207751274f), f, f2(0.24261054396629333f, 0.24261054396629333f));
-  p = ffma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
-  p = ffma2(p, f, f2(0.9999281167984009f, 0.9999281167984009f));
-  float pa, pb, ta, tb;
-  f2split(p, pa, pb);
-  f2split(t, ta, tb);
-  return f2(__uint_as_float(__float_as_uint(pa) + (__float_as_uint(ta) << 23)),
-            __uint_as_float(__float_as_uint(pb) + (__float_as_uint(tb) << 23)));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
