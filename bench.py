@@ -7,8 +7,10 @@ GQA attention, then the backward (attention, RoPE, LoRA A/B grads, the projectio
 gradient), then, on N > 1 GPUs, the NCCL all-reduce of the LoRA gradients (data-parallel by whole
 packed sequences). Shapes: Qwen2.5-1.5B layer (hidden 1536, 12 q / 2 kv heads, head_dim 128).
 Packing: config 3 of the baseline, 16,384 tokens per GPU, row lengths uniform in [64, 4096].
+``--workload config4`` runs the baseline's 7B block instead (hidden 3584, 28 q / 4 kv heads,
+131,072 tokens per GPU, log-normal lengths of median 4096 up to 32,768).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload config3|config4]
 
 Prints one JSON line (rank 0). ``value`` is whole-job tokens/s with inputs resident in HBM;
 ``e2e`` is the same step with the inputs copied from pinned host memory and the LoRA gradients
@@ -40,6 +42,8 @@ HIDDEN, HQ, HK, D = 1536, 12, 2, 128
 TOKENS = 16384
 WORKLOAD = ("attention block fwd+bwd of one Qwen2.5-1.5B QLoRA layer (NF4 dq q/k/v + bias, "
             "LoRA r16 q,v, RoPE, varlen causal GQA attention) over config-3 packing")
+WORKLOAD7B = ("attention block fwd+bwd of one Qwen2.5-7B QLoRA layer (NF4 dq q/k/v + bias, "
+              "LoRA r16 q,v, RoPE, varlen causal GQA attention) over config-4 packing")
 
 
 def lengths_for(seed: int, total: int = TOKENS, lo: int = 64, hi: int = 4096) -> list[int]:
@@ -51,6 +55,29 @@ def lengths_for(seed: int, total: int = TOKENS, lo: int = 64, hi: int = 4096) ->
         out.append(L)
         t += L
     return out
+
+
+def lengths_config4(seed: int, total: int = 131072, median: int = 4096, sigma: float = 1.0, lo: int = 16,
+                    hi: int = 32768, first_max: bool = True) -> list[int]:
+    """The 7B block's packing: log-normal lengths (median 4096, sigma 1, clipped to [16, 32768]),
+    packed greedily to ``total`` tokens (last row truncated). With ``first_max`` the first row has
+    the maximum length, so the longest case is always present."""
+    rng = np.random.default_rng(seed)
+    out, t = ([hi], hi) if first_max else ([], 0)
+    while t < total:
+        L = int(np.clip(round(rng.lognormal(np.log(median), sigma)), lo, hi))
+        L = min(L, total - t)
+        out.append(L)
+        t += L
+    return out
+
+
+# name -> (hidden, q heads, kv heads, lengths(seed), workload text, lengths text)
+WORKLOADS = {
+    "config3": (HIDDEN, HQ, HK, lambda seed: lengths_for(seed), WORKLOAD, "U[64,4096]"),
+    "config4": (3584, 28, 4, lambda seed: lengths_config4(seed), WORKLOAD7B,
+                "log-normal median 4096 sigma 1 in [16,32768], first row 32768"),
+}
 
 
 def causal_flops(lengths, n_heads=HQ, head_dim=D) -> float:
@@ -149,7 +176,8 @@ def dist_setup():
     return world, rank, local
 
 
-def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0):
+def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0, hidden: int = HIDDEN,
+                        n_heads: int = HQ, n_kv: int = HK):
     """Times the reference's CPU path (oracle.block, torch fp32) on the first rows of the packing,
     ``sample_tokens`` tokens (last row truncated). Returns (tokens/s, sample description, threads)."""
     from decik_b200.nf4_quant import quantize_nf4
@@ -171,18 +199,19 @@ def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0
     T = s
     rng = np.random.default_rng(seed)
     g = torch.Generator().manual_seed(seed)
-    inputs = dict(x=torch.randn(T, HIDDEN, generator=g), spans=spans, n_heads=HQ, n_kv=HK, scaling=2.0)
-    for name, n_out in (("q", HQ * D), ("k", HK * D), ("v", HK * D)):
-        inputs[f"nf4_{name}"] = quantize_nf4((rng.standard_normal((n_out, HIDDEN)) * 0.02).astype(np.float32))
+    inputs = dict(x=torch.randn(T, hidden, generator=g), spans=spans, n_heads=n_heads, n_kv=n_kv, scaling=2.0)
+    for name, n_out in (("q", n_heads * D), ("k", n_kv * D), ("v", n_kv * D)):
+        inputs[f"nf4_{name}"] = quantize_nf4((rng.standard_normal((n_out, hidden)) * 0.02).astype(np.float32))
         inputs[f"b_{name}"] = torch.randn(n_out, generator=g) * 0.02
-    inputs.update(a_q=torch.randn(16, HIDDEN, generator=g) * 0.02, bb_q=torch.randn(HQ * D, 16, generator=g) * 0.02,
-                  a_v=torch.randn(16, HIDDEN, generator=g) * 0.02, bb_v=torch.randn(HK * D, 16, generator=g) * 0.02)
+    inputs.update(a_q=torch.randn(16, hidden, generator=g) * 0.02,
+                  bb_q=torch.randn(n_heads * D, 16, generator=g) * 0.02,
+                  a_v=torch.randn(16, hidden, generator=g) * 0.02, bb_v=torch.randn(n_kv * D, 16, generator=g) * 0.02)
     pos = torch.cat([torch.arange(L) for L in rows]).float()
     inv = 1.0 / (1e6 ** (torch.arange(0, D, 2).float() / D))
     fr = torch.outer(pos, inv)
     emb = torch.cat((fr, fr), -1)
     inputs["cos"], inputs["sin"] = emb.cos(), emb.sin()
-    grad = torch.randn(T, HQ * D, generator=g)
+    grad = torch.randn(T, n_heads * D, generator=g)
     times = []
     for _ in range(n_steps):
         t0 = time.perf_counter()
@@ -195,17 +224,18 @@ def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    lengths = lengths_for(1000)
+    hidden, hq, hk, lengths_of, workload, _ = WORKLOADS[args.workload]
+    lengths = lengths_of(1000)
     sample = args.ref_tokens
     # warm-up steps (untimed), then K timed steps, each one bounded sample of the workload
     if args.warmup:
-        cpu_reference_steps(lengths, min(args.warmup, 1), sample)
-    value, desc, threads, times = cpu_reference_steps(lengths, args.steps, sample)
+        cpu_reference_steps(lengths, min(args.warmup, 1), sample, hidden=hidden, n_heads=hq, n_kv=hk)
+    value, desc, threads, times = cpu_reference_steps(lengths, args.steps, sample, hidden=hidden, n_heads=hq, n_kv=hk)
     line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1e3 * statistics.mean(times), 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD + " (bounded CPU sample)", "tokens_per_gpu": TOKENS,
+            "config": {"workload": workload + " (bounded CPU sample)", "tokens_per_gpu": sum(lengths),
                        "sample": desc, "parallelism": "cpu"},
             "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": desc},
@@ -221,14 +251,15 @@ def run_ours(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    block = QLoRAAttentionBlock.random(seed=0, device=dev)          # replicated frozen weights + LoRA
-    lengths = lengths_for(1000 + rank)                                # each rank its own sequences
+    hidden, hq, hk, lengths_of, workload, lengths_text = WORKLOADS[args.workload]
+    block = QLoRAAttentionBlock.random(hidden=hidden, n_heads=hq, n_kv=hk, seed=0, device=dev)  # frozen + LoRA
+    lengths = lengths_of(1000 + rank)                                 # each rank its own sequences
     T = sum(lengths)
     packing = packing_from_lengths(lengths, dev)
     cos, sin = rope_cos_sin(packing.positions, D)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
-    x = torch.randn(T, HIDDEN, device=dev, generator=g).requires_grad_(True)
-    dout = torch.randn(T, HQ * D, device=dev, generator=g).to(torch.bfloat16)
+    x = torch.randn(T, hidden, device=dev, generator=g).requires_grad_(True)
+    dout = torch.randn(T, hq * D, device=dev, generator=g).to(torch.bfloat16)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
     bucket = GradBucket(block.lora_params())                         # LoRA grads: views of one fp32 buffer
     if world > 1:
@@ -302,7 +333,7 @@ def run_ours(args, world, rank, local):
     if rank != 0:
         return
     pk = peaks()
-    f_fwd = causal_flops(lengths)
+    f_fwd = causal_flops(lengths, n_heads=hq)
     fwd_ms = statistics.mean(op_ms.get("varlen_attn_fwd", [float("nan")]))
     bwd_ms = statistics.mean(op_ms.get("varlen_attn_bwd", [float("nan")]))
     attn_tflops = 3.0 * f_fwd / ((fwd_ms + bwd_ms) / 1e3) / 1e12
@@ -315,9 +346,9 @@ def run_ours(args, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded lengths, N(0,1) activations, random-init NF4/LoRA weights)",
-        "config": {"workload": WORKLOAD, "tokens_per_gpu": T, "rows_rank0": len(lengths),
-                   "lengths": "U[64,4096], numpy default_rng(1000 + rank)", "hidden": HIDDEN,
-                   "heads": f"{HQ}/{HK}", "head_dim": D, "lora": "r16 alpha32 q,v", "nf4": "bs64, double quant bs256",
+        "config": {"workload": workload, "tokens_per_gpu": T, "rows_rank0": len(lengths),
+                   "lengths": f"{lengths_text}, numpy default_rng(1000 + rank)", "hidden": hidden,
+                   "heads": f"{hq}/{hk}", "head_dim": D, "lora": "r16 alpha32 q,v", "nf4": "bs64, double quant bs256",
                    "l2": "flushed between timed steps (256 MiB write, untimed)", "parallelism": f"dp{world}"},
         "roofline": {"bound": "tensor", "kernel": "varlen attention fwd+bwd (decik_varlen_attn_fwd/bwd)",
                      "achieved": round(attn_tflops, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
@@ -332,7 +363,7 @@ def run_ours(args, world, rank, local):
                 "d2h_bytes_per_step": g_host.numel() * 4},
     }
     if world == 1 and not args.no_cpu_baseline:
-        cv, desc, threads, _ = cpu_reference_steps(lengths, 1, args.ref_tokens)
+        cv, desc, threads, _ = cpu_reference_steps(lengths, 1, args.ref_tokens, hidden=hidden, n_heads=hq, n_kv=hk)
         line["cpu_baseline"] = {"value": round(cv, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
                                 "sample": desc}
     print(json.dumps(line), flush=True)
@@ -346,6 +377,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ref-tokens", type=int, default=4096, help="tokens of the bounded CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config3",
+                    help="config3: the 1.5B block over 16,384 tokens (default); config4: the 7B block over 131,072")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:

@@ -37,6 +37,16 @@ inline int sm_count() {
   }
   return n;
 }
+inline int64_t l2_bytes() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrL2CacheSize, dev);
+    if (n <= 0) n = 126 << 20;
+  }
+  return n;
+}
 
 // ---- dtype traits: 16-bit storage types and fp32 conversions (round to nearest even) ----
 template <typename T> struct Dt;

@@ -38,18 +38,16 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// The suspend-time hint (ns) lets the hardware park the waiting warp until the phase completes (or
-// the hint expires) instead of spinning: waiting warps then take no issue slots from the warps
-// that share their SM sub-partition.
-constexpr uint32_t kSuspendHintNs = 1000000;
+// No suspend-time hint: with one (1 ms), a woken waiter was measured to resume ~200 cycles after
+// the phase completed, on the backward's critical path; the hardware's default limit is shorter.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }

@@ -298,3 +298,91 @@ def test_varlen_attention_large_properties(cuda_lib):
     assert_close16(_np(dq[sl]), rdq, "dq row")
     assert_close16(_np(dk[sl]), rdk, "dk row")
     assert_close16(_np(dv[sl]), rdv, "dv row")
+
+
+def _attn_fp32_rows(q, k, v, do, spans, scale, chunk=512):
+    """The math of oracle/attention.py (per-row causal softmax attention, query head h reading kv
+    head h // groups, and its gradients with delta = rowsum(dO * O)) restated in fp32 torch on the
+    GPU, query-chunked so that rows of 32,768 tokens fit: the full-size reference."""
+    T, HQ, D = q.shape
+    HK = k.shape[1]
+    g = HQ // HK
+    dev = q.device
+    out = torch.empty(T, HQ, D, device=dev)
+    lse = torch.empty(HQ, T, device=dev)
+    dq = torch.empty(T, HQ, D, device=dev)
+    dk = torch.empty(T, HK, D, device=dev)
+    dv = torch.empty(T, HK, D, device=dev)
+    for s, L in spans:
+        qf = q[s:s + L].float().transpose(0, 1)
+        kf = k[s:s + L].float().transpose(0, 1).repeat_interleave(g, 0)
+        vf = v[s:s + L].float().transpose(0, 1).repeat_interleave(g, 0)
+        dof = do[s:s + L].float().transpose(0, 1)
+        dkf = torch.zeros(HQ, L, D, device=dev)
+        dvf = torch.zeros(HQ, L, D, device=dev)
+        for c0 in range(0, L, chunk):
+            c1 = min(L, c0 + chunk)
+            sc = torch.bmm(qf[:, c0:c1], kf[:, :c1].transpose(1, 2)) * scale
+            qi = torch.arange(c0, c1, device=dev)[:, None]
+            kj = torch.arange(c1, device=dev)[None, :]
+            sc.masked_fill_(kj > qi, float("-inf"))
+            lc = torch.logsumexp(sc, -1)
+            p = torch.exp(sc - lc[..., None])
+            del sc
+            o = torch.bmm(p, vf[:, :c1])
+            dp = torch.bmm(dof[:, c0:c1], vf[:, :c1].transpose(1, 2))
+            ds = p * (dp - (dof[:, c0:c1] * o).sum(-1, keepdim=True))
+            del dp
+            dvf[:, :c1] += torch.bmm(p.transpose(1, 2), dof[:, c0:c1])
+            del p
+            dq[s + c0:s + c1] = (torch.bmm(ds, kf[:, :c1]) * scale).transpose(0, 1)
+            dkf[:, :c1] += torch.bmm(ds.transpose(1, 2), qf[:, c0:c1]) * scale
+            del ds
+            out[s + c0:s + c1] = o.transpose(0, 1)
+            lse[:, s + c0:s + c1] = lc
+        dk[s:s + L] = dkf.view(HK, g, L, D).sum(1).transpose(0, 1)
+        dv[s:s + L] = dvf.view(HK, g, L, D).sum(1).transpose(0, 1)
+    return out, lse, dq, dk, dv
+
+
+def _close_gpu(actual, expected, what):
+    """tests/tolerance.py's bar, evaluated on the device (the arrays are GBs)."""
+    from tests.tolerance import MAX_ABS, REL_L2
+
+    a, e = actual.float(), expected.float()
+    assert torch.isfinite(a).all(), f"{what}: non-finite values"
+    d = a - e
+    rel = (d.norm() / e.norm().clamp_min(1.0)).item()
+    mx = (d.abs().max() / e.abs().max().clamp_min(1.0)).item()
+    assert rel <= REL_L2 and mx <= MAX_ABS, f"{what}: rel-L2 {rel:.3e} (<= {REL_L2}), max-abs {mx:.3e} (<= {MAX_ABS})"
+
+
+def test_varlen_attention_config4_full_size(cuda_lib):
+    """The 7B block's attention at full size (28 / 4 heads, 131,072 tokens, rows up to 32,768)
+    against the fp32 restatement, every row and every output."""
+    from bench import lengths_config4
+
+    ops = _ops()
+    lengths = lengths_config4(0)
+    assert sum(lengths) == 131072 and max(lengths) == 32768
+    spans, cu, q, k, v, do = _attn_case(lengths, 28, 4, torch.bfloat16, seed=7, layout="ref")
+    scale = 128 ** -0.5
+    out, lse = ops.varlen_attn_fwd(q, k, v, cu, max(lengths), scale)
+    dq, dk, dv = ops.varlen_attn_bwd(do, q, k, v, out, lse, cu, max(lengths), scale)
+    torch.cuda.synchronize()
+    assert cuda_lib.decik_kernel_error(1) == 0
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ro, rl, rdq, rdk, rdv = _attn_fp32_rows(q, k, v, do, spans, scale)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    _close_gpu(out, ro, "out")
+    assert (lse - rl).abs().max().item() <= 2e-3
+    _close_gpu(dq, rdq, "dq")
+    _close_gpu(dk, rdk, "dk")
+    _close_gpu(dv, rdv, "dv")
+    # the longest row alone meets the bar too (not only through the sums over all rows)
+    s, L = spans[0]
+    for name, a, e in (("out", out, ro), ("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+        _close_gpu(a[s:s + L], e[s:s + L], f"{name} of the 32,768-token row")
