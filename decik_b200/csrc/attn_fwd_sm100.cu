@@ -49,7 +49,8 @@ struct Params {
   float* lse;
   const int32_t* cu;
   int64_t n_tok;
-  int n_heads, groups, pairs, n_mblocks;
+  int n_heads, groups, pairs, n_mblocks, n_rows;
+  int heavy_first;  // grid x = (row, kv head, pair), y = query block from the last; else see below
   int order_q, order_k, order_v;  // 0: coordinates (d, tok, head); 1: (d, head, tok)
   float scale_log2;
   int* err;
@@ -88,10 +89,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
   const uint32_t sb = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int m_block = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);
-  const int row = blockIdx.y;
-  const int kvh = blockIdx.z / p.pairs;
-  const int pair = blockIdx.z % p.pairs;
+  // heavy_first: y walks the query blocks from the last (the most key blocks) for every row at once;
+  // else x walks one row's query blocks from its last, y the rows, z the (kv head, pair)
+  const int m_block = p.n_mblocks - 1 - static_cast<int>(p.heavy_first ? blockIdx.y : blockIdx.x);
+  const int row = p.heavy_first ? static_cast<int>(blockIdx.x % p.n_rows) : static_cast<int>(blockIdx.y);
+  const int z = p.heavy_first ? static_cast<int>(blockIdx.x / p.n_rows) : static_cast<int>(blockIdx.z);
+  const int kvh = z / p.pairs;
+  const int pair = z % p.pairs;
   const int h0 = kvh * p.groups + 2 * pair;
   const bool has1 = 2 * pair + 1 < p.groups;
   const int start = p.cu[row];
@@ -355,7 +359,20 @@ int fwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor
   p.n_mblocks = (max_len + BM - 1) / BM;
   p.scale_log2 = scale * kLog2e;
   p.err = attn_error_word();
-  dim3 grid(p.n_mblocks, n_rows, n_kv * p.pairs);
+  p.n_rows = n_rows;
+  // Launch order (blocks start in grid order, x fastest). A CTA's work grows with its query block,
+  // so starting the last query blocks of every row first is the longest-first order that keeps the
+  // tail short. It spreads the resident CTAs over all rows, each reading its own row's K / V: fine
+  // while K and V fit well inside L2. Beyond that, one row's query blocks launch together so that
+  // they share its K / V tiles through L2.
+  const int64_t kv_bytes = n_tok * n_kv * D * 2 * 2;
+  const int64_t zs = static_cast<int64_t>(n_kv) * p.pairs;
+  p.heavy_first = kv_bytes <= l2_bytes() / 2 && n_rows * zs <= INT32_MAX && p.n_mblocks <= 65535;
+  if (!p.heavy_first && (n_rows > 65535 || zs > 65535))
+    return set_error(DECIK_ERR_UNSUPPORTED, "varlen_attn_fwd: grid too large (%d rows)", n_rows);
+  const dim3 grid = p.heavy_first ? dim3(static_cast<unsigned>(n_rows * zs), static_cast<unsigned>(p.n_mblocks), 1)
+                                  : dim3(static_cast<unsigned>(p.n_mblocks), static_cast<unsigned>(n_rows),
+                                         static_cast<unsigned>(zs));
   if (dtype == DECIK_BF16) {
     static bool set = false;
     if (!set) {
