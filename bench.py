@@ -112,6 +112,8 @@ class ClockSampler:
         self.thread = None
         self.stop = False
         self.error = None
+        import threading
+        self.started = threading.Event()  # set once the first sample is in (or sampling failed)
 
     def _nvml_index(self) -> int:
         try:
@@ -126,12 +128,15 @@ class ClockSampler:
             h = nv.nvmlDeviceGetHandleByIndex(self._nvml_index())
             self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
             masks = [(name, getattr(nv, attr)) for name, attr in self.REASONS if hasattr(nv, attr)]
-            while not self.stop:
+            while True:
                 self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
                 active = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
                 for name, m in masks:
                     if active & m:
                         self.reasons.add(name)
+                self.started.set()
+                if self.stop:
+                    break
                 time.sleep(0.005)
             nv.nvmlShutdown()
         except Exception as e:  # NVML missing: one nvidia-smi reading instead
@@ -144,12 +149,13 @@ class ClockSampler:
                 self.max_mhz = float(mx)
             except Exception:
                 pass
+            self.started.set()
 
     def __enter__(self):
         import threading
         self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
-        time.sleep(0.02)
+        self.started.wait(timeout=30)  # the first sample precedes the timed region
         return self
 
     def __exit__(self, *exc):
@@ -221,15 +227,22 @@ def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0
     return T / statistics.mean(times), desc, threads, times
 
 
+REF_BUDGET_S = 90.0  # the reference arm's timed steps, seconds
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
     hidden, hq, hk, lengths_of, workload, _ = WORKLOADS[args.workload]
     lengths = lengths_of(1000)
     sample = args.ref_tokens
-    # warm-up steps (untimed), then K timed steps, each one bounded sample of the workload
+    # warm-up step (untimed), then K timed steps, each one bounded sample of the workload; the
+    # sample shrinks (attention is superlinear in it, so it is stated in the line) when K steps of
+    # it would run past the time budget
     if args.warmup:
-        cpu_reference_steps(lengths, min(args.warmup, 1), sample, hidden=hidden, n_heads=hq, n_kv=hk)
+        _, _, _, warm = cpu_reference_steps(lengths, 1, sample, hidden=hidden, n_heads=hq, n_kv=hk)
+        if args.steps * warm[0] > REF_BUDGET_S:
+            sample = max(512, int(sample * REF_BUDGET_S / (args.steps * warm[0])) // 128 * 128)
     value, desc, threads, times = cpu_reference_steps(lengths, args.steps, sample, hidden=hidden, n_heads=hq, n_kv=hk)
     line = {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -372,14 +385,18 @@ def run_ours(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 100; 10 with --impl reference)")
+    ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 10; 1 with --impl reference)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ref-tokens", type=int, default=4096, help="tokens of the bounded CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config3",
                     help="config3: the 1.5B block over 16,384 tokens (default); config4: the 7B block over 131,072")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 10 if args.impl == "reference" else 100
+    if args.warmup is None:
+        args.warmup = 1 if args.impl == "reference" else 10
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":

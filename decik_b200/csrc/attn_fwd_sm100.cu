@@ -3,12 +3,18 @@
 // launch over every row of the packed sequence, GQA without expanding K/V, fully-masked causal
 // tiles never visited, logsumexp written for the backward.
 //
-// CTA = one 128-query block of one row x two query heads of the same kv head (so each K/V tile
-// loaded by TMA feeds two 128x128x128 QK^T and two PV products). 10 warps:
-//   warps 0-3  softmax of query tile 0 (thread = one query row = one TMEM lane)
-//   warps 4-7  softmax of query tile 1
-//   warp 8     TMA producer: Q0, Q1 once, then K_j / V_j into a 2-stage ring
+// Work tile = one 128-query block of one row x two query heads of the same kv head (so each K/V
+// tile loaded by TMA feeds two 128x128x128 QK^T and two PV products). In the longest-first tile
+// order the kernel is persistent: one CTA per SM takes tiles from a ticket counter until none are
+// left, so TMEM allocation and barrier setup happen once per SM, and the next tile's first QK^T
+// runs while the softmax warps write the previous tile's output; in the row-major order (see
+// fwd_sm100) each CTA takes one tile. 10 warps:
+//   warps 0-3  softmax of query tile 0 (thread = one query row = one TMEM lane) and its output
+//   warps 4-7  the same for query tile 1
+//   warp 8     tile tickets and the TMA producer: Q0, Q1 per tile, K_j / V_j through a 2-stage ring
+//              that runs on across tiles
 //   warp 9     TMEM allocation and the single-thread tcgen05.mma issue
+//   warps 10-11 idle (they complete the third warpgroup for the register split)
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512); P (16-bit) overwrites
 // the first 64 columns of its S. The MMA thread ping-pongs the two tiles so the tensor core runs
 // one tile's QK^T / PV while the other tile's softmax runs:
@@ -18,6 +24,9 @@
 // gives up records a code in the error word and the CTA winds down (waiting for its own MMAs and
 // TMA loads, then freeing TMEM).
 #include <cudaTypedefs.h>
+
+#include <atomic>
+#include <type_traits>
 
 #include "attn_common.cuh"
 #include "sm100.cuh"
@@ -36,11 +45,32 @@ using namespace sm100;
 constexpr int BM = 128, BN = 128;
 constexpr int HALF = BM * 64 * 2;       // one [128 rows x 64] 16-bit swizzled half tile: 16 KB
 constexpr int TILE = 2 * HALF;          // 32 KB
-constexpr int NTHREADS = 320;
-constexpr int OFF_Q0 = 0, OFF_Q1 = TILE, OFF_K = 2 * TILE, OFF_V = 4 * TILE, OFF_BAR = 6 * TILE;
-enum { B_Q = 0, B_KF = 1, B_KE = 3, B_VF = 5, B_VE = 7, B_SF = 9, B_PR = 11, B_OF = 13, B_DONE = 15, N_BAR = 16 };
+constexpr int NTHREADS = 384;  // 12 warps = 3 warpgroups (warps 10-11 only complete warpgroup 2)
+// registers per thread: 168 at launch (the most 384 threads can have), then per warpgroup: the
+// softmax warpgroups 184 (their loop plus the persistent tile state), warpgroup 2 (producer and
+// MMA issue) 128. The sum must not exceed what the block was launched with, or setmaxnreg.inc
+// would wait forever.
+constexpr int kRegsLaunch = 168, kRegsSoftmax = 184, kRegsIssue = 128;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsIssue <= NTHREADS * kRegsLaunch, "register split");
+static_assert(NTHREADS * kRegsLaunch <= 65536, "launch register count");
+constexpr int OFF_Q0 = 0, OFF_Q1 = TILE, OFF_K = 2 * TILE, OFF_V = 4 * TILE;
+constexpr int STAGE = 32 * 64;                                 // per softmax warp: 32 rows x 32 columns
+constexpr int OFF_STAGE = 6 * TILE;                            // 8 warps x STAGE: output staging
+constexpr int OFF_RING = OFF_STAGE + 8 * STAGE;                // int32 [2] tile tickets
+constexpr int OFF_BAR = OFF_RING + 16;
+enum {
+  B_Q = 0, B_QE, B_KF, B_KE = B_KF + 2, B_VF = B_KE + 2, B_VE = B_VF + 2, B_SF = B_VE + 2, B_PR = B_SF + 2,
+  B_OF = B_PR + 2, B_OE = B_OF + 2, B_TF = B_OE + 2, B_TE = B_TF + 2, B_DONE = B_TE + 2, N_BAR
+};
 constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
 constexpr int kSmem = OFF_TMEM + 16 + 1024;  // + slack for the 1024-byte alignment
+static_assert(kSmem <= 227 * 1024, "shared memory");
+
+// Ticket counters, one per launch that may be in flight at the same time (a launch takes the next
+// slot round-robin). The last CTA of a launch to finish puts its slot back to zero.
+constexpr int kSlots = 64;
+__device__ unsigned int g_ticket[kSlots];
+__device__ unsigned int g_exit[kSlots];
 
 struct Params {
   CUtensorMap tq, tk, tv;
@@ -49,12 +79,46 @@ struct Params {
   float* lse;
   const int32_t* cu;
   int64_t n_tok;
-  int n_heads, groups, pairs, n_mblocks, n_rows;
-  int heavy_first;  // grid x = (row, kv head, pair), y = query block from the last; else see below
+  int n_heads, groups, pairs, n_mblocks, n_rows, zs;
+  unsigned n_tickets;
+  int heavy_first;  // ticket order: see fwd_sm100
+  int persistent;   // tickets from the counter; else CTA b takes ticket b and nothing else
+  int slot;
   int order_q, order_k, order_v;  // 0: coordinates (d, tok, head); 1: (d, head, tok)
   float scale_log2;
   int* err;
 };
+
+struct WorkTile {
+  int start, L, m0, n_kv, kvh, h0;
+  bool has1;
+};
+
+// Ticket t -> work tile; false for a query block past its row's end. heavy_first: tickets walk the
+// query blocks from the last (the most key blocks) for every row at once; else one row's query
+// blocks from its last, row after row.
+__device__ __forceinline__ bool decode_tile(const Params& p, const int* cu, unsigned t, WorkTile& w) {
+  int mb, rz;
+  if (p.heavy_first) {
+    const unsigned per = static_cast<unsigned>(p.n_rows) * p.zs;
+    mb = p.n_mblocks - 1 - static_cast<int>(t / per);
+    rz = static_cast<int>(t % per);
+  } else {
+    mb = p.n_mblocks - 1 - static_cast<int>(t % p.n_mblocks);
+    rz = static_cast<int>(t / p.n_mblocks);
+  }
+  const int row = rz % p.n_rows, z = rz / p.n_rows;
+  w.start = __ldg(cu + row);
+  w.L = __ldg(cu + row + 1) - w.start;
+  w.m0 = mb * BM;
+  if (w.m0 >= w.L) return false;
+  w.n_kv = (min(w.m0 + BM, w.L) + BN - 1) / BN;
+  w.kvh = z / p.pairs;
+  const int pair = z % p.pairs;
+  w.h0 = w.kvh * p.groups + 2 * pair;
+  w.has1 = 2 * pair + 1 < p.groups;
+  return true;
+}
 
 __device__ __forceinline__ void load_half(uint32_t dst, const CUtensorMap* map, uint32_t bar, int order,
                                           int c, int tok, int head) {
@@ -88,25 +152,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  // heavy_first: y walks the query blocks from the last (the most key blocks) for every row at once;
-  // else x walks one row's query blocks from its last, y the rows, z the (kv head, pair)
-  const int m_block = p.n_mblocks - 1 - static_cast<int>(p.heavy_first ? blockIdx.y : blockIdx.x);
-  const int row = p.heavy_first ? static_cast<int>(blockIdx.x % p.n_rows) : static_cast<int>(blockIdx.y);
-  const int z = p.heavy_first ? static_cast<int>(blockIdx.x / p.n_rows) : static_cast<int>(blockIdx.z);
-  const int kvh = z / p.pairs;
-  const int pair = z % p.pairs;
-  const int h0 = kvh * p.groups + 2 * pair;
-  const bool has1 = 2 * pair + 1 < p.groups;
-  const int start = p.cu[row];
-  const int L = p.cu[row + 1] - start;
-  const int m0 = m_block * BM;
-  if (m0 >= L) return;  // uniform: before any barrier or TMEM use
-  const int n_kv = (min(m0 + BM, L) + BN - 1) / BN;
   auto bar = [&](int i) { return sb + OFF_BAR + 8 * i; };
+  volatile int* ring = reinterpret_cast<volatile int*>(smem + OFF_RING);
+
+  const int* cu = p.cu;
+  if (!p.persistent) {  // one ticket per CTA: a query block past its row's end leaves at once
+    WorkTile w0;
+    if (!decode_tile(p, cu, blockIdx.x, w0)) return;  // uniform: before any barrier or TMEM use
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B_Q), 1);
+    mbar_init(bar(B_QE), 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(B_KF + s), 1);
       mbar_init(bar(B_KE + s), 1);
@@ -115,6 +172,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
       mbar_init(bar(B_SF + s), 1);
       mbar_init(bar(B_PR + s), 128);
       mbar_init(bar(B_OF + s), 1);
+      mbar_init(bar(B_OE + s), 128);
+      mbar_init(bar(B_TF + s), 1);
+      mbar_init(bar(B_TE + s), 1 + 256);  // the MMA thread and every softmax thread
     }
     mbar_init(bar(B_DONE), 1);
     fence_barrier_init();
@@ -128,214 +188,324 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + OFF_TMEM);
 
-  if (warp == 8) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      prefetch_tmap(&p.tq);
-      prefetch_tmap(&p.tk);
-      prefetch_tmap(&p.tv);
-      mbar_expect_tx(bar(B_Q), has1 ? 2 * TILE : TILE);
-      for (int hh = 0; hh < (has1 ? 2 : 1); ++hh)
-        for (int c = 0; c < 2; ++c)
-          load_half(sb + (hh ? OFF_Q1 : OFF_Q0) + c * HALF, &p.tq, bar(B_Q), p.order_q, 64 * c, start + m0, h0 + hh);
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j & 1;
-        if (j >= 2) ok = mbar_wait(bar(B_KE + s), ((j - 2) >> 1) & 1, p.err, 101);
-        if (!ok) break;
-        mbar_expect_tx(bar(B_KF + s), TILE);
-        for (int c = 0; c < 2; ++c)
-          load_half(sb + OFF_K + s * TILE + c * HALF, &p.tk, bar(B_KF + s), p.order_k, 64 * c, start + j * BN, kvh);
-        if (j >= 2) ok = mbar_wait(bar(B_VE + s), ((j - 2) >> 1) & 1, p.err, 102);
-        if (!ok) break;
-        mbar_expect_tx(bar(B_VF + s), TILE);
-        for (int c = 0; c < 2; ++c)
-          load_half(sb + OFF_V + s * TILE + c * HALF, &p.tv, bar(B_VF + s), p.order_v, 64 * c, start + j * BN, kvh);
-        issued = j + 1;
-      }
-      // wind down: the loads of the last two uses must have landed before the CTA exits
-      for (int j = max(0, issued - 2); j < issued; ++j) {
-        mbar_wait(bar(B_KF + (j & 1)), (j >> 1) & 1, p.err, 103);
-        mbar_wait(bar(B_VF + (j & 1)), (j >> 1) & 1, p.err, 104);
-      }
-      mbar_wait(bar(B_Q), 0, p.err, 105);
-    }
-  } else if (warp == 9) {
-    // ---------------------------------------------------------------- MMA issue (one thread)
-    if (lane == 0) {
-      constexpr int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-      const uint32_t id_qk = idesc_f16(ab, BM, BN, 0, 0);
-      const uint32_t id_pv = idesc_f16(ab, BM, D, 0, 1);
-      const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
-      const uint32_t q0 = sb + OFF_Q0, q1 = sb + OFF_Q1;
-      bool ok = mbar_wait(bar(B_Q), 0, p.err, 201) && mbar_wait(bar(B_KF), 0, p.err, 202);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(tS0, q0, sb + OFF_K, id_qk);
-        umma_commit(bar(B_SF + 0));
-        if (has1) {
-          issue_qk(tS1, q1, sb + OFF_K, id_qk);
-          umma_commit(bar(B_SF + 1));
-        }
-        umma_commit(bar(B_KE + 0));
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t v = sb + OFF_V + s * TILE;
-        const bool next = j + 1 < n_kv;
-        const uint32_t kn = sb + OFF_K + ((j + 1) & 1) * TILE;
-        ok = mbar_wait(bar(B_VF + s), (j >> 1) & 1, p.err, 203) && mbar_wait(bar(B_PR + 0), j & 1, p.err, 204);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(tO0, tS0, v, id_pv, j > 0);
-        if (next) {
-          ok = mbar_wait(bar(B_KF + ((j + 1) & 1)), ((j + 1) >> 1) & 1, p.err, 205);
+  if (warp >= 8) {
+    reg_set<kRegsLaunch, kRegsIssue>();
+    if (warp == 8) {
+      // ---------------------------------------------------------------- tickets + TMA producer
+      if (lane == 0) {
+        prefetch_tmap(&p.tq);
+        prefetch_tmap(&p.tk);
+        prefetch_tmap(&p.tv);
+        unsigned* ticket = &g_ticket[p.slot];
+        int k = 0;          // tiles published
+        int q_loaded = 0;   // tiles whose Q load was issued
+        uint32_t g = 0;     // K/V loads issued (ring position, across tiles)
+        bool ok = true;
+        while (ok) {
+          WorkTile w;
+          unsigned t;
+          if (p.persistent) {
+            do {
+              t = atomicAdd(ticket, 1u);
+            } while (t < p.n_tickets && !decode_tile(p, cu, t, w));
+          } else {
+            t = k == 0 && decode_tile(p, cu, blockIdx.x, w) ? blockIdx.x : p.n_tickets;
+          }
+          const bool end = t >= p.n_tickets;
+          // ring slot k & 1 was last used by tile k - 2: wait until everyone read it
+          if (k >= 2) ok = mbar_wait(bar(B_TE + (k & 1)), ((k - 2) >> 1) & 1, p.err, 106);
           if (!ok) break;
+          ring[k & 1] = end ? -1 : static_cast<int>(t);
+          mbar_arrive(bar(B_TF + (k & 1)));
+          ++k;
+          if (end) break;
+          // Q of this tile once the previous tile's QK^T products are done with the Q buffers
+          if (q_loaded >= 1) ok = mbar_wait(bar(B_QE), (q_loaded - 1) & 1, p.err, 107);
+          if (!ok) break;
+          mbar_expect_tx(bar(B_Q), w.has1 ? 2 * TILE : TILE);
+          for (int hh = 0; hh < (w.has1 ? 2 : 1); ++hh)
+            for (int c = 0; c < 2; ++c)
+              load_half(sb + (hh ? OFF_Q1 : OFF_Q0) + c * HALF, &p.tq, bar(B_Q), p.order_q, 64 * c, w.start + w.m0,
+                        w.h0 + hh);
+          ++q_loaded;
+          for (int j = 0; j < w.n_kv && ok; ++j, ++g) {
+            const int s = g & 1;
+            if (g >= 2) ok = mbar_wait(bar(B_KE + s), ((g - 2) >> 1) & 1, p.err, 101);
+            if (!ok) break;
+            mbar_expect_tx(bar(B_KF + s), TILE);
+            for (int c = 0; c < 2; ++c)
+              load_half(sb + OFF_K + s * TILE + c * HALF, &p.tk, bar(B_KF + s), p.order_k, 64 * c, w.start + j * BN, w.kvh);
+            if (g >= 2) ok = mbar_wait(bar(B_VE + s), ((g - 2) >> 1) & 1, p.err, 102);
+            if (!ok) {
+              ++g;  // its K load is in flight
+              break;
+            }
+            mbar_expect_tx(bar(B_VF + s), TILE);
+            for (int c = 0; c < 2; ++c)
+              load_half(sb + OFF_V + s * TILE + c * HALF, &p.tv, bar(B_VF + s), p.order_v, 64 * c, w.start + j * BN, w.kvh);
+          }
+        }
+        // wind down: the last loads must have landed before the CTA exits
+        for (uint32_t j = g >= 2 ? g - 2 : 0; j < g; ++j) {
+          mbar_wait(bar(B_KF + (j & 1)), (j >> 1) & 1, p.err, 103);
+          mbar_wait(bar(B_VF + (j & 1)), (j >> 1) & 1, p.err, 104);
+        }
+        if (q_loaded > 0) mbar_wait(bar(B_Q), (q_loaded - 1) & 1, p.err, 105);
+      }
+    } else if (warp == 9) {
+      // ---------------------------------------------------------------- MMA issue (one thread)
+      if (lane == 0) {
+        constexpr int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+        const uint32_t id_qk = idesc_f16(ab, BM, BN, 0, 0);
+        const uint32_t id_pv = idesc_f16(ab, BM, D, 0, 1);
+        const uint32_t tS0 = tmem, tS1 = tmem + 128, tO0 = tmem + 256, tO1 = tmem + 384;
+        const uint32_t q0 = sb + OFF_Q0, q1 = sb + OFF_Q1;
+        int k = 0, k1 = 0;                  // tiles taken; of them with a second query head
+        uint32_t g = 0, g0 = 0, g1 = 0;     // K/V uses; softmax iterations of query tile 0 / 1
+        bool ok = true;
+        while (ok) {
+          ok = mbar_wait(bar(B_TF + (k & 1)), (k >> 1) & 1, p.err, 208);
+          if (!ok) break;
+          const int t = ring[k & 1];
+          mbar_arrive(bar(B_TE + (k & 1)));
+          if (t < 0) break;
+          WorkTile w;
+          decode_tile(p, cu, static_cast<unsigned>(t), w);
+          ok = mbar_wait(bar(B_Q), k & 1, p.err, 201) && mbar_wait(bar(B_KF + (g & 1)), (g >> 1) & 1, p.err, 202);
+          if (!ok) break;
+          // S0(0), S1(0): S0 / S1 were last read by the previous tile's PV products, issued before
           tc_fence_after();
-          issue_qk(tS0, q0, kn, id_qk);
+          issue_qk(tS0, q0, sb + OFF_K + (g & 1) * TILE, id_qk);
           umma_commit(bar(B_SF + 0));
-        }
-        if (has1) {
-          ok = mbar_wait(bar(B_PR + 1), j & 1, p.err, 206);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(tO1, tS1, v, id_pv, j > 0);
-        }
-        umma_commit(bar(B_VE + s));
-        if (next) {
-          if (has1) {
-            issue_qk(tS1, q1, kn, id_qk);
+          if (w.has1) {
+            issue_qk(tS1, q1, sb + OFF_K + (g & 1) * TILE, id_qk);
             umma_commit(bar(B_SF + 1));
           }
-          umma_commit(bar(B_KE + ((j + 1) & 1)));
+          umma_commit(bar(B_KE + (g & 1)));
+          // O0 / O1 are overwritten by the tile's first PV: the previous tile's output must be read out
+          if (k >= 1) ok = mbar_wait(bar(B_OE + 0), (k - 1) & 1, p.err, 209);
+          if (ok && w.has1 && k1 >= 1) ok = mbar_wait(bar(B_OE + 1), (k1 - 1) & 1, p.err, 210);
+          // one key block: PV0(j), [S0(j+1)], PV1(j), [S1(j+1)]; the last block (no next) is peeled
+          // off so that the steady loop carries no per-block branches
+          auto block = [&](auto has_next, int j) -> bool {
+            constexpr bool next = decltype(has_next)::value;
+            const int s = g & 1;
+            const uint32_t v = sb + OFF_V + s * TILE;
+            const uint32_t kn = sb + OFF_K + ((g + 1) & 1) * TILE;
+            if (!mbar_wait(bar(B_VF + s), (g >> 1) & 1, p.err, 203) || !mbar_wait(bar(B_PR + 0), g0 & 1, p.err, 204))
+              return false;
+            tc_fence_after();
+            issue_pv(tO0, tS0, v, id_pv, j > 0);
+            ++g0;
+            if (next) {
+              if (!mbar_wait(bar(B_KF + ((g + 1) & 1)), ((g + 1) >> 1) & 1, p.err, 205)) return false;
+              tc_fence_after();
+              issue_qk(tS0, q0, kn, id_qk);
+              umma_commit(bar(B_SF + 0));
+            }
+            if (w.has1) {
+              if (!mbar_wait(bar(B_PR + 1), g1 & 1, p.err, 206)) return false;
+              tc_fence_after();
+              issue_pv(tO1, tS1, v, id_pv, j > 0);
+              ++g1;
+            }
+            umma_commit(bar(B_VE + s));
+            if (next) {
+              if (w.has1) {
+                issue_qk(tS1, q1, kn, id_qk);
+                umma_commit(bar(B_SF + 1));
+              }
+              umma_commit(bar(B_KE + ((g + 1) & 1)));
+            }
+            ++g;
+            return true;
+          };
+          for (int j = 0; ok && j + 1 < w.n_kv; ++j) ok = block(std::true_type{}, j);
+          umma_commit(bar(B_QE));  // every QK^T of the tile is issued: Q is free once they are done
+          if (ok) ok = block(std::false_type{}, w.n_kv - 1);
+          if (!ok) break;
+          umma_commit(bar(B_OF + 0));
+          if (w.has1) umma_commit(bar(B_OF + 1));
+          ++k;
+          if (w.has1) ++k1;
         }
+        umma_commit(bar(B_DONE));
+        mbar_wait(bar(B_DONE), 0, p.err, 207);  // nothing in flight before TMEM is freed
       }
-      umma_commit(bar(B_OF + 0));
-      umma_commit(bar(B_OF + 1));
-      umma_commit(bar(B_DONE));
-      mbar_wait(bar(B_DONE), 0, p.err, 207);  // nothing in flight before TMEM is freed
     }
-  } else if (warp < 8 && (warp < 4 || has1)) {
+  } else {
+    reg_set<kRegsLaunch, kRegsSoftmax>();
     // ---------------------------------------------------------------- softmax of one query tile
     const int tile = warp >> 2;
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + tile * 128 + lane_off;
     const uint32_t tO = tmem + 256 + tile * 128 + lane_off;
-    const int qi = m0 + r;
-    float m_run = -INFINITY, l = 0.f;
+    int k = 0, kt = 0;     // tiles taken; of them with this query tile
+    uint32_t gi = 0;       // softmax iterations of this query tile
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      ok = mbar_wait(bar(B_SF + tile), j & 1, p.err, 301 + tile);
+    // a bounded wait, made uniform across the warp (the TMEM accesses below are warp-collective)
+    auto wait_w = [&](int b, int parity, int code) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, p.err, code));
+    };
+    while (ok) {
+      ok = wait_w(B_TF + (k & 1), (k >> 1) & 1, 305);
+      if (!ok) break;
+      const int t = ring[k & 1];
+      mbar_arrive(bar(B_TE + (k & 1)));
+      ++k;
+      if (t < 0) break;
+      WorkTile w;
+      decode_tile(p, cu, static_cast<unsigned>(t), w);
+      if (tile == 1 && !w.has1) continue;
+      const int qi = w.m0 + r;
+      float m_run = -INFINITY, l = 0.f;
+      for (int j = 0; j < w.n_kv; ++j, ++gi) {
+        ok = wait_w(B_SF + tile, gi & 1, 301 + tile);
+        if (!ok) break;
+        tc_fence_after();
+        // keys past min(query, row end) are masked; only the diagonal / last block has any
+        const int lim = min(qi, w.L - 1) - j * BN;  // last visible column of this row in this block
+        const bool masked = lim < BN - 1;
+        // pass 1: row max of the raw scores (scale > 0 commutes with max), 64 columns at a time
+        float mx = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t sv[64];
+          tmem_ld32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_ld_wait();
+          if (masked) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+              if (64 * h + c > lim) sv[c] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int c = 0; c < 64; c += 2) mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+        }
+        const float m_new = fmaxf(m_run, mx * p.scale_log2);
+        const bool resc = m_new > m_run + 8.f;
+        float alpha = 1.f;
+        if (resc) {
+          alpha = ptx::ex2(m_run - m_new);
+          m_run = m_new;
+          l *= alpha;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, resc)) {  // rescale this warp's O rows in TMEM
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c4, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + 32 * c4, o);
+          }
+          tmem_st_wait();
+        }
+        // pass 2: P = exp2(s * scale*log2e - m_run), packed FMA for the arguments and packed adds for
+        // the sum; P (16-bit pairs) overwrites the first 64 columns of S
+        const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
+        const uint64_t nm2 = f2(-m_run, -m_run);
+        uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t sv[64], pk[32];
+          tmem_ld32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_ld_wait();
+          if (masked) {
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+              if (64 * h + c > lim) sv[c] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            float x0, x1;
+            f2split(ffma2(f2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])), sc2, nm2), x0, x1);
+            const float e0 = ptx::ex2(x0), e1 = ptx::ex2(x1);
+            acc[c & 3] = fadd2(acc[c & 3], f2(e0, e1));
+            pk[c] = pk2<T>(e0, e1);
+          }
+          tmem_st32(tS + 32 * h, pk);
+        }
+        float s0, s1, s2, s3, s4, s5, s6, s7;
+        f2split(acc[0], s0, s1);
+        f2split(acc[1], s2, s3);
+        f2split(acc[2], s4, s5);
+        f2split(acc[3], s6, s7);
+        l += ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar(B_PR + tile));
+      }
+      if (!ok) break;
+      // output: O / l -> 16-bit row, logsumexp; then O is free for the next tile's first PV
+      ok = wait_w(B_OF + tile, kt & 1, 311 + tile);
       if (!ok) break;
       tc_fence_after();
-      // keys past min(query, row end) are masked; only the diagonal / last block has any
-      const int lim = min(qi, L - 1) - j * BN;  // last visible column of this row in this block
-      const bool masked = lim < BN - 1;
-      // pass 1: row max of the raw scores (scale > 0 commutes with max), 64 columns at a time
-      float mx = -INFINITY;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sv[64];
-        tmem_ld32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_ld_wait();
-        if (masked) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (64 * h + c > lim) sv[c] = __float_as_uint(-INFINITY);
-        }
-#pragma unroll
-        for (int c = 0; c < 64; c += 2) mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
-      }
-      const float m_new = fmaxf(m_run, mx * p.scale_log2);
-      const bool resc = m_new > m_run + 8.f;
-      float alpha = 1.f;
-      if (resc) {
-        alpha = ptx::ex2(m_run - m_new);
-        m_run = m_new;
-        l *= alpha;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, resc)) {  // rescale this warp's O rows in TMEM
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t o[32];
-          tmem_ld32(tO + 32 * c4, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + 32 * c4, o);
-        }
-        tmem_st_wait();
-      }
-      // pass 2: P = exp2(s * scale*log2e - m_run), packed FMA for the arguments and packed adds for
-      // the sum; P (16-bit pairs) overwrites the first 64 columns of S
-      const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
-      const uint64_t nm2 = f2(-m_run, -m_run);
-      uint64_t acc[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sv[64], pk[32];
-        tmem_ld32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_ld_wait();
-        if (masked) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (64 * h + c > lim) sv[c] = __float_as_uint(-INFINITY);
-        }
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          float x0, x1;
-          f2split(ffma2(f2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])), sc2, nm2), x0, x1);
-          const float e0 = ptx::ex2(x0), e1 = ptx::ex2(x1);
-          acc[c & 3] = fadd2(acc[c & 3], f2(e0, e1));
-          pk[c] = pk2<T>(e0, e1);
-        }
-        tmem_st32(tS + 32 * h, pk);
-      }
-      float s0, s1, s2, s3, s4, s5, s6, s7;
-      f2split(acc[0], s0, s1);
-      f2split(acc[1], s2, s3);
-      f2split(acc[2], s4, s5);
-      f2split(acc[3], s6, s7);
-      l += ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(bar(B_PR + tile));
-    }
-    // epilogue: O / l -> 16-bit row, logsumexp
-    if (ok && mbar_wait(bar(B_OF + tile), 0, p.err, 311 + tile)) {
-      tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int h = h0 + tile;
-      T* dst = static_cast<T*>(p.o) + (static_cast<int64_t>(start) + qi) * p.o_tok + static_cast<int64_t>(h) * p.o_head;
+      const int h = w.h0 + tile;
+      // 32 columns at a time through this warp's staging rows (16-byte unit u of row x at unit
+      // u ^ ((x >> 1) & 3): conflict-free both ways), then stored as 8 rows x 64 contiguous bytes
+      // per instruction instead of 32 rows x 16 bytes; O is read in two halves (register budget)
+      uint8_t* stg = smem + OFF_STAGE + warp * STAGE;
+      const int rr = lane >> 2, uu = lane & 3;  // store lane map: row 8 i + rr, unit uu
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t o[32];
-        tmem_ld32(tO + 32 * c4, o);
+      for (int half = 0; half < 2; ++half) {
+        uint32_t o[2][32];
+        tmem_ld32(tO + 64 * half, o[0]);
+        tmem_ld32(tO + 64 * half + 32, o[1]);
         tmem_ld_wait();
-        uint32_t w[16];
+        if (half == 1) {  // O is free for the next tile's first PV
+          tc_fence_before();
+          mbar_arrive(bar(B_OE + tile));
+          ++kt;
+        }
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          w[i] = pk2<T>(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-        if (qi < L) {
+        for (int c2 = 0; c2 < 2; ++c2) {
+          const int c4 = 2 * half + c2;
+          uint32_t wv[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            reinterpret_cast<uint4*>(dst + 32 * c4)[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          for (int i = 0; i < 16; ++i)
+            wv[i] = pk2<T>(__uint_as_float(o[c2][2 * i]) * inv, __uint_as_float(o[c2][2 * i + 1]) * inv);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            *reinterpret_cast<uint4*>(stg + lane * 64 + ((u ^ ((lane >> 1) & 3)) << 4)) =
+                make_uint4(wv[4 * u], wv[4 * u + 1], wv[4 * u + 2], wv[4 * u + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int x = 8 * i + rr;             // row within the warp
+            const int q = w.m0 + (warp & 3) * 32 + x;
+            const uint4 val = *reinterpret_cast<const uint4*>(stg + x * 64 + ((uu ^ ((x >> 1) & 3)) << 4));
+            if (q < w.L)
+              *reinterpret_cast<uint4*>(static_cast<T*>(p.o) + (static_cast<int64_t>(w.start) + q) * p.o_tok +
+                                        static_cast<int64_t>(h) * p.o_head + 32 * c4 + 8 * uu) = val;
+          }
+          __syncwarp();
         }
       }
-      if (qi < L) p.lse[static_cast<int64_t>(h) * p.n_tok + start + qi] = (m_run + __log2f(l)) * kLn2;
+      if (qi < w.L) p.lse[static_cast<int64_t>(h) * p.n_tok + w.start + qi] = (m_run + __log2f(l)) * kLn2;
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (p.persistent && threadIdx.x == 0) {
+    // every CTA has drawn its last ticket once it is here: the last one resets the slot
+    __threadfence();
+    if (atomicAdd(&g_exit[p.slot], 1u) == gridDim.x - 1) {
+      atomicExch(&g_ticket[p.slot], 0u);
+      atomicExch(&g_exit[p.slot], 0u);
+    }
+  }
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
 }
+
+std::atomic<unsigned> g_next_slot{0};
 
 }  // namespace
 
@@ -357,22 +527,27 @@ int fwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor
   p.groups = n_heads / n_kv;
   p.pairs = (p.groups + 1) / 2;
   p.n_mblocks = (max_len + BM - 1) / BM;
+  p.n_rows = n_rows;
+  p.zs = n_kv * p.pairs;
   p.scale_log2 = scale * kLog2e;
   p.err = attn_error_word();
-  p.n_rows = n_rows;
-  // Launch order (blocks start in grid order, x fastest). A CTA's work grows with its query block,
-  // so starting the last query blocks of every row first is the longest-first order that keeps the
-  // tail short. It spreads the resident CTAs over all rows, each reading its own row's K / V: fine
-  // while K and V fit well inside L2. Beyond that, one row's query blocks launch together so that
-  // they share its K / V tiles through L2.
+  const uint64_t tickets = static_cast<uint64_t>(p.n_mblocks) * n_rows * p.zs;
+  if (tickets >= (1ull << 31))
+    return set_error(DECIK_ERR_UNSUPPORTED, "varlen_attn_fwd: too many tiles (%llu)", (unsigned long long)tickets);
+  p.n_tickets = static_cast<unsigned>(tickets);
+  // Ticket order. A tile's work grows with its query block, so taking the last query blocks of
+  // every row first is the longest-first order that keeps the tail short. It spreads the CTAs
+  // working at a time over all rows, each reading its own row's K / V: fine while K and V fit well
+  // inside L2. Beyond that, one row's query blocks go together so that they share its K / V tiles
+  // through L2 (the 7B block at 131,072 tokens).
   const int64_t kv_bytes = n_tok * n_kv * D * 2 * 2;
-  const int64_t zs = static_cast<int64_t>(n_kv) * p.pairs;
-  p.heavy_first = kv_bytes <= l2_bytes() / 2 && n_rows * zs <= INT32_MAX && p.n_mblocks <= 65535;
-  if (!p.heavy_first && (n_rows > 65535 || zs > 65535))
-    return set_error(DECIK_ERR_UNSUPPORTED, "varlen_attn_fwd: grid too large (%d rows)", n_rows);
-  const dim3 grid = p.heavy_first ? dim3(static_cast<unsigned>(n_rows * zs), static_cast<unsigned>(p.n_mblocks), 1)
-                                  : dim3(static_cast<unsigned>(p.n_mblocks), static_cast<unsigned>(n_rows),
-                                         static_cast<unsigned>(zs));
+  p.heavy_first = kv_bytes <= l2_bytes() / 2;
+  // Persistent CTAs pay off where tiles are short (their setup and output then weigh) and the
+  // longest-first order puts few past-the-row-end tickets among them. The row-major order has a
+  // run of such tickets per row and long tiles: there every CTA takes one ticket, its own index.
+  p.persistent = p.heavy_first;
+  p.slot = static_cast<int>(g_next_slot.fetch_add(1u) % kSlots);
+  const dim3 grid(static_cast<unsigned>(p.persistent ? std::min<uint64_t>(sm_count(), tickets) : tickets));
   if (dtype == DECIK_BF16) {
     static bool set = false;
     if (!set) {
