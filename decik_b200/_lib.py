@@ -55,6 +55,11 @@ SIGNATURES = {
     "decik_varlen_attn_bwd": (c_int, [Tensor3, Tensor3, Tensor3, Tensor3, Tensor3, c_void_p, Tensor3, Tensor3,
                                       Tensor3, c_void_p, c_int, c_int, c_int64, c_int, c_int, c_int, c_float,
                                       c_int, c_void_p, c_void_p]),
+    "decik_attn_qkv_bwd_workspace": (c_int64, [c_int64, c_int, c_int, c_int]),
+    "decik_set_stage_events": (None, [c_void_p, c_int]),
+    "decik_attn_qkv_bwd": (c_int, [Tensor3, Tensor3, Tensor3, Tensor3, Tensor3, c_void_p, c_void_p, c_int, c_int,
+                                   c_int64, c_int, c_int, c_int, c_float, c_void_p, c_void_p, c_void_p, c_float,
+                                   c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "decik_varlen_attn_bwd_noalloc": (c_int, [Tensor3, Tensor3, Tensor3, Tensor3, Tensor3, c_void_p, Tensor3,
                                               Tensor3, Tensor3, c_void_p, c_int, c_int, c_int64, c_int, c_int, c_int,
                                               c_float, c_int, c_void_p]),

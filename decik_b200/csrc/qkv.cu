@@ -75,6 +75,13 @@ struct QkvBwdParams {
   int64_t ldy;
   int64_t n_tok;
   int hq, hk;
+  // fp32 accumulators of the attention backward, token-major [tok][heads][128], read instead of
+  // the 16-bit gradients when set: q_acc (x q_mul) replaces gq, k_acc (x k_mul) gk, and v_acc is
+  // rounded into dy's v columns (else the caller placed dv there)
+  const float* q_acc;
+  const float* k_acc;
+  const float* v_acc;
+  float q_mul, k_mul;
 };
 
 __device__ __forceinline__ uint32_t ld_u32(const void* p) {
@@ -122,6 +129,25 @@ __device__ __forceinline__ void stage_tile(T* tile, const T* src, int64_t tok, i
     const int chunk = (lane & 15) * 8;
     const bool ok = row < nrows;
     ptx::cp_async16(ptx::smem_u32(tile + row * kLd + chunk), ok ? src + row * tok + chunk : src, ok);
+  }
+}
+
+// The same [16 x 128] tile from an fp32 accumulator with row stride `tok` (floats), each value
+// scaled by `mul` and rounded to T: what the attention backward's cast pass would have stored.
+template <typename T>
+__device__ __forceinline__ void stage_tile_acc(T* tile, const float* src, int64_t tok, int nrows, int lane, float mul) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int row = 2 * i + (lane >> 4);
+    const int chunk = (lane & 15) * 8;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (row < nrows) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(src + row * tok + chunk));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(src + row * tok + chunk + 4));
+      f[0] = a.x * mul; f[1] = a.y * mul; f[2] = a.z * mul; f[3] = a.w * mul;
+      f[4] = b.x * mul; f[5] = b.y * mul; f[6] = b.z * mul; f[7] = b.w * mul;
+    }
+    *reinterpret_cast<uint4*>(tile + row * kLd + chunk) = pack8<T>(f);
   }
 }
 
@@ -322,7 +348,8 @@ qkv_bwd_kernel(const QkvBwdParams p) {
   T* dy = static_cast<T*>(p.dy);
   const int n_heads = p.hq + 2 * p.hk;
   const bool lora = p.frag != nullptr;
-  const int n_work = lora ? n_heads : p.hq + p.hk;  // v heads only feed the LoRA gradient
+  // v heads feed the LoRA gradient, and are rounded into dy when they come as an accumulator
+  const int n_work = lora || p.v_acc != nullptr ? n_heads : p.hq + p.hk;
   const auto src_of = [&](int hh, int64_t& tok) -> const T* {
     if (hh < p.hq) {
       tok = p.gq_tok;
@@ -335,14 +362,35 @@ qkv_bwd_kernel(const QkvBwdParams p) {
     tok = p.ldy;
     return dy + t0 * p.ldy + static_cast<int64_t>(hh) * kD;  // dv, placed by the caller
   };
+  // stages head hh's tile: from an fp32 accumulator when there is one, else by cp.async
+  const auto stage = [&](int hh) {
+    const float* acc = nullptr;
+    int64_t rs = 0;
+    float mul = 1.f;
+    if (hh < p.hq) {
+      acc = p.q_acc ? p.q_acc + (t0 * p.hq + hh) * kD : nullptr;
+      rs = static_cast<int64_t>(p.hq) * kD;
+      mul = p.q_mul;
+    } else if (hh < p.hq + p.hk) {
+      acc = p.k_acc ? p.k_acc + (t0 * p.hk + (hh - p.hq)) * kD : nullptr;
+      rs = static_cast<int64_t>(p.hk) * kD;
+      mul = p.k_mul;
+    } else {
+      acc = p.v_acc ? p.v_acc + (t0 * p.hk + (hh - p.hq - p.hk)) * kD : nullptr;
+      rs = static_cast<int64_t>(p.hk) * kD;
+    }
+    if (acc != nullptr) {
+      stage_tile_acc<T>(ts, acc, rs, nrows, lane, mul);
+    } else {
+      int64_t tok;
+      const T* src = src_of(hh, tok);
+      stage_tile<T>(ts, src, tok, nrows, lane);
+    }
+  };
 
   stage_cos_sin(cs, p.cosp, p.sinp, t0, nrows);
   int h = warp;
-  if (h < n_work) {
-    int64_t tok;
-    const T* src = src_of(h, tok);
-    stage_tile<T>(ts, src, tok, nrows, lane);
-  }
+  if (h < n_work) stage(h);
   ptx::cp_async_commit();
   ptx::cp_async_wait<0>();
   __syncthreads();
@@ -356,6 +404,7 @@ qkv_bwd_kernel(const QkvBwdParams p) {
     const bool is_v = h >= p.hq + p.hk;
     const bool is_q = h < p.hq;
     const bool to_g = lora && (is_q || is_v);
+    const bool v_store = is_v && p.v_acc != nullptr;  // dv rounded from its accumulator into dy
     const int64_t ycol = static_cast<int64_t>(h) * kD;
 #pragma unroll 4
     for (int i = 0; i < 8; ++i) {
@@ -384,6 +433,9 @@ qkv_bwd_kernel(const QkvBwdParams p) {
         }
         unpack4<T>(wl, lo);  // the rounded values are what the LoRA branch scales
         unpack4<T>(wh, hi);
+      } else if (v_store && row < nrows) {
+        st_u64(dy + (t0 + row) * p.ldy + ycol + c4, pack4<T>(lo));
+        st_u64(dy + (t0 + row) * p.ldy + ycol + c4 + kD / 2, pack4<T>(hi));
       }
       if (to_g) {
         // g = dt(x * scaling) (solution/attn.py:250), in place: the A operand of du = g . B16
@@ -418,9 +470,7 @@ qkv_bwd_kernel(const QkvBwdParams p) {
     h += kWarps;
     if (h >= n_work) break;
     __syncwarp();
-    int64_t tok;
-    const T* src = src_of(h, tok);
-    stage_tile<T>(ts, src, tok, nrows, lane);
+    stage(h);
     ptx::cp_async_commit();
     ptx::cp_async_wait<0>();
     __syncwarp();
@@ -533,6 +583,46 @@ extern "C" int decik_qkv_epilogue_fwd(const void* y, int64_t ldy, const void* u,
   return check_launch("qkv_epilogue_fwd");
 }
 
+namespace decik {
+int qkv_bwd_launch(const QkvBwdParams& p, int dtype, cudaStream_t stream) {
+  const unsigned grid = static_cast<unsigned>((p.n_tok + 15) / 16);
+  const int smem = kCsBytes + kWarps * kTile * 2;  // >= the du partials [warps][2][16][16] fp32
+  static_assert(kWarps * kTile * 2 >= kWarps * 2 * 256 * 4, "du partials must fit in the tiles' space");
+  cudaError_t e;
+  if (dtype == DECIK_BF16) {
+    e = cudaFuncSetAttribute(qkv_bwd_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) qkv_bwd_kernel<__nv_bfloat16><<<grid, kWarps * 32, smem, stream>>>(p);
+  } else {
+    e = cudaFuncSetAttribute(qkv_bwd_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess) qkv_bwd_kernel<__half><<<grid, kWarps * 32, smem, stream>>>(p);
+  }
+  if (e != cudaSuccess) return set_error(DECIK_ERR_CUDA, "qkv_epilogue_bwd: %s", cudaGetErrorString(e));
+  return check_launch("qkv_epilogue_bwd");
+}
+
+// The projection epilogue's backward reading the attention backward's fp32 accumulators (token-major
+// [n_tok][heads][128]): dq = q_mul * q_acc always; dk = k_mul * k_acc when k_acc is set, else the
+// 16-bit grad_k; dv = v_acc rounded into dy's v columns when v_acc is set, else already there.
+// Called by decik_attn_qkv_bwd with validated, aligned buffers.
+int qkv_epilogue_bwd_acc(const float* q_acc, float q_mul, const decik_tensor3& grad_k, const float* k_acc,
+                         float k_mul, const float* v_acc, const float* cos, const float* sin, const void* frag,
+                         float scaling, void* dy, int64_t ldy, int64_t n_tok, int n_heads, int n_kv, int dtype,
+                         cudaStream_t stream) {
+  if (n_tok == 0) return DECIK_OK;
+  const bool lora = frag != nullptr;
+  const int64_t width = static_cast<int64_t>(n_heads + 2 * n_kv) * kD + (lora ? 2 * kR : 0);
+  if (ldy < width || (ldy % 8) || !al16(dy) || !al16(cos) || !al16(sin) || (lora && !al16(frag)) ||
+      !al16(q_acc) || (k_acc && !al16(k_acc)) || (v_acc && !al16(v_acc)) ||
+      (!k_acc && (!al16(grad_k.ptr) || (grad_k.tok_stride % 8) || (grad_k.head_stride % 8))))
+    return set_error(DECIK_ERR_INVALID, "qkv_epilogue_bwd: misaligned pointer or leading dimension");
+  const uint32_t* bfrag =
+      lora ? static_cast<const uint32_t*>(frag) + static_cast<int64_t>(n_heads + n_kv) * kFragWords : nullptr;
+  QkvBwdParams p{nullptr, 0, 0, grad_k.ptr, grad_k.tok_stride, grad_k.head_stride, cos, sin, bfrag, scaling,
+                 dy, ldy, n_tok, n_heads, n_kv, q_acc, k_acc, v_acc, q_mul, k_mul};
+  return qkv_bwd_launch(p, dtype, stream);
+}
+}  // namespace decik
+
 extern "C" int decik_qkv_epilogue_bwd(decik_tensor3 grad_q, decik_tensor3 grad_k, const float* cos,
                                       const float* sin, const void* frag, float scaling, void* dy,
                                       int64_t ldy, int64_t n_tok, int n_heads, int n_kv, int head_dim,
@@ -556,18 +646,7 @@ extern "C" int decik_qkv_epilogue_bwd(decik_tensor3 grad_q, decik_tensor3 grad_k
   const uint32_t* bfrag =
       lora ? static_cast<const uint32_t*>(frag) + static_cast<int64_t>(n_heads + n_kv) * kFragWords : nullptr;
   QkvBwdParams p{grad_q.ptr, grad_q.tok_stride, grad_q.head_stride, grad_k.ptr, grad_k.tok_stride,
-                 grad_k.head_stride, cos, sin, bfrag, scaling, dy, ldy, n_tok, n_heads, n_kv};
-  const unsigned grid = static_cast<unsigned>((n_tok + 15) / 16);
-  const int smem = kCsBytes + kWarps * kTile * 2;  // >= the du partials [warps][2][16][16] fp32
-  static_assert(kWarps * kTile * 2 >= kWarps * 2 * 256 * 4, "du partials must fit in the tiles' space");
-  cudaError_t e;
-  if (dtype == DECIK_BF16) {
-    e = cudaFuncSetAttribute(qkv_bwd_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess) qkv_bwd_kernel<__nv_bfloat16><<<grid, kWarps * 32, smem, as_stream(stream)>>>(p);
-  } else {
-    e = cudaFuncSetAttribute(qkv_bwd_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess) qkv_bwd_kernel<__half><<<grid, kWarps * 32, smem, as_stream(stream)>>>(p);
-  }
-  if (e != cudaSuccess) return set_error(DECIK_ERR_CUDA, "qkv_epilogue_bwd: %s", cudaGetErrorString(e));
-  return check_launch("qkv_epilogue_bwd");
+                 grad_k.head_stride, cos, sin, bfrag, scaling, dy, ldy, n_tok, n_heads, n_kv,
+                 nullptr, nullptr, nullptr, 1.f, 1.f};
+  return decik::qkv_bwd_launch(p, dtype, as_stream(stream));
 }

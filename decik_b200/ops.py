@@ -7,6 +7,8 @@ only on CUDA tensors; anything else raises (there is no CPU fallback).
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -298,6 +300,42 @@ def qkv_epilogue_bwd(grad_q: torch.Tensor, grad_k: torch.Tensor, cos: torch.Tens
             _t3any(grad_q), _t3any(grad_k), _p(cos), _p(sin), _p(frag), float(scaling), _p(dy), dy.stride(0),
             T, n_heads, n_kv, D, _dt(dy), _stream(dy))
     _lib.check(rc, "qkv_epilogue_bwd")
+    return dy
+
+
+def attn_qkv_bwd(dout, q, k, v, out, lse, cu_seqlens, max_len: int, scale: float, cos: torch.Tensor,
+                 sin: torch.Tensor, frag: torch.Tensor | None, scaling: float, dy: torch.Tensor,
+                 workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The attention backward and the projection epilogue backward in one call
+    (decik_attn_qkv_bwd): fills dy [T, ld] (dq, dk after RoPE^T, dv, du) from the attention's
+    fp32 accumulators. q, k, v, out, dout: [T, H, D] views as for varlen_attn_bwd."""
+    _cuda(dout, q, k, v, out, lse, cu_seqlens, cos, sin, frag, dy)
+    T, Hq, D = q.shape
+    Hk = k.shape[1]
+    if dy.stride(1) != 1:
+        raise RuntimeError("decik_b200 attn_qkv_bwd: dy needs contiguous rows")
+    nbytes = int(_lib.lib().decik_attn_qkv_bwd_workspace(T, Hq, Hk, D))
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    lib = _lib.lib()
+    args = (_t3(dout), _t3(q), _t3(k), _t3(v), _t3(out), _p(lse), _p(cu_seqlens), cu_seqlens.numel() - 1,
+            int(max_len), T, Hq, Hk, D, float(scale), _p(cos), _p(sin), _p(frag), float(scaling), _p(dy),
+            dy.stride(0), _dt(q), _p(workspace), _stream(q))
+    if _timer is None:
+        rc = lib.decik_attn_qkv_bwd(*args)
+    else:  # the two stages timed apart: an event recorded between them by the library
+        a, mid, b = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        mid.record()  # creates the event; the library records it again between the stages
+        handles = (ctypes.c_void_p * 1)(mid.cuda_event)
+        lib.decik_set_stage_events(handles, 1)
+        a.record()
+        rc = lib.decik_attn_qkv_bwd(*args)
+        b.record()
+        lib.decik_set_stage_events(None, 0)
+        _timer.events.append(("varlen_attn_bwd", a, mid))
+        _timer.events.append(("qkv_epilogue_bwd", mid, b))
+        _timer.launches += 3
+    _lib.check(rc, "attn_qkv_bwd")
     return dy
 
 

@@ -81,13 +81,11 @@ class FusedAttentionBlock(torch.autograd.Function):
         n_proj = n_q + 2 * n_kvd
         dt = x16.dtype
         dy = torch.empty((T, n_proj + 2 * r), dtype=dt, device=x16.device)
-        dq = torch.empty((T, n_heads, D), dtype=dt, device=x16.device)
-        dk = torch.empty((T, n_kv, D), dtype=dt, device=x16.device)
-        dv = dy[:, n_q + n_kvd:n_proj].view(T, n_kv, D)
         g = grad_out if grad_out.stride(-1) == 1 else grad_out.contiguous()
-        ops.varlen_attn_bwd(g, q.transpose(0, 1), k.transpose(0, 1), v, out, lse, cu, max_len, scale,
-                            dq=dq, dk=dk, dv=dv)
-        ops.qkv_epilogue_bwd(dq, dk, cos, sin, frag, scaling, dy, n_heads, n_kv)
+        # attention backward + RoPE^T + du in one call; dq / dk / dv never exist in 16 bits apart
+        # from their place in dy
+        ops.attn_qkv_bwd(g, q.transpose(0, 1), k.transpose(0, 1), v, out, lse, cu, max_len, scale, cos, sin,
+                         frag, scaling, dy)
         dx = torch.mm(dy, w_cat, out_dtype=torch.float32)
         da = torch.mm(dy[:, n_proj:].t(), x16, out_dtype=torch.float32)
         db = torch.mm(dy[:, :n_proj].t(), u, out_dtype=torch.float32)

@@ -164,6 +164,27 @@ DECIK_API int decik_qkv_epilogue_bwd(decik_tensor3 grad_q, decik_tensor3 grad_k,
                            const float* sin, const void* frag, float scaling, void* dy, int64_t ldy,
                            int64_t n_tok, int n_heads, int n_kv, int head_dim, int dtype, void* stream);
 
+/* The fused block's backward in one call: decik_varlen_attn_bwd followed by
+ * decik_qkv_epilogue_bwd, without the 16-bit dq / dk / dv in between. The epilogue reads the
+ * attention backward's fp32 accumulators and rounds them exactly as decik_varlen_attn_bwd's cast
+ * pass does (dq = bf16/fp16(scale * acc)), so the results are those of the two calls up to the
+ * order of the attention's fp32 reduce-adds. q, k, v, dout, out, lse, cu_seqlens: as for
+ * decik_varlen_attn_bwd; cos, sin, frag, scaling, dy, ldy: as for decik_qkv_epilogue_bwd, except
+ * that dy's v columns are written here (dv) instead of being supplied. workspace:
+ * decik_attn_qkv_bwd_workspace() bytes, 256-byte aligned. Replaces, for one fused node, the
+ * backward of VarlenSDPA (solution/varlen.py:154-168), FusedQKRope (solution/attn.py:113-126) and
+ * LoRAPairFromNorm's grad_u (solution/attn.py:250-253). */
+/* Profiling hook: calls made on this host thread with n > 0 events set record them between their
+ * stages, on their stream (decik_attn_qkv_bwd: events[0] after the attention backward, before the
+ * projection epilogue). events are cudaEvent_t handles; n = 0 or NULL clears the hook. */
+DECIK_API void decik_set_stage_events(void* const* events, int n);
+DECIK_API int64_t decik_attn_qkv_bwd_workspace(int64_t n_tok, int n_heads, int n_kv, int head_dim);
+DECIK_API int decik_attn_qkv_bwd(decik_tensor3 dout, decik_tensor3 q, decik_tensor3 k, decik_tensor3 v,
+                       decik_tensor3 out, const float* lse, const int32_t* cu_seqlens, int n_rows,
+                       int max_len, int64_t n_tok, int n_heads, int n_kv, int head_dim, float scale,
+                       const float* cos, const float* sin, const void* frag, float scaling, void* dy,
+                       int64_t ldy, int dtype, void* workspace, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * RMSNorm (Qwen2RMSNorm), the producer of the LoRA input (norm_link recompute).
  * Replaces skc_rmsnorm_fwd_kernel / skc_rmsnorm_bwd_kernel (solution/rmsnorm.py:17-45) and

@@ -145,3 +145,51 @@ def test_qkv_epilogue_rejects_bad_arguments(cuda_lib):
     assert lib.decik_qkv_epilogue_bwd(t3, t3, cos.data_ptr(), sin.data_ptr(), None, 2.0,
                                       y.data_ptr(), NPROJ + 2 * R, T, HQ, HK, 64, 1, None) == 3
     assert cuda_lib.decik_kernel_error(1) == 0
+
+
+@pytest.mark.parametrize("lengths,hq,hk,lora", [
+    ([37, 128, 211, 454], 12, 2, True),      # config 1: query heads split over CTAs (fp32 dK / dV)
+    ([4096, 4096, 4096, 4096], 28, 4, True),  # 7B heads, 16k tokens: dK / dV written directly
+    ([300, 1, 129], 12, 2, False),            # no LoRA: dv still rounded into dy
+])
+def test_attn_qkv_bwd_matches_two_calls(cuda_lib, lengths, hq, hk, lora):
+    """decik_attn_qkv_bwd against decik_varlen_attn_bwd + decik_qkv_epilogue_bwd on the same inputs:
+    the same roundings, so equal up to the order of the attention's fp32 reduce-adds."""
+    import numpy as np
+
+    ops = _ops()
+    dtype = torch.bfloat16
+    T, nq, nk = sum(lengths), hq * D, hk * D
+    nproj = nq + 2 * nk
+    g = torch.Generator(device="cuda").manual_seed(len(lengths) + hq)
+    q = torch.randn(hq, T, D, generator=g, device="cuda").to(dtype).transpose(0, 1)
+    k = torch.randn(hk, T, D, generator=g, device="cuda").to(dtype).transpose(0, 1)
+    v = torch.randn(T, hk, D, generator=g, device="cuda").to(dtype)
+    do = torch.randn(T, hq, D, generator=g, device="cuda").to(dtype)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device="cuda")
+    scale = D ** -0.5
+    out, lse = ops.varlen_attn_fwd(q, k, v, cu, max(lengths), scale)
+    cos, sin = _cos_sin(T)
+    frag = None
+    if lora:
+        frag = ops.lora_pack(torch.zeros(R, 64, device="cuda"), torch.zeros(R, 64, device="cuda"),
+                             torch.randn(nq, R, generator=g, device="cuda") * 0.05,
+                             torch.randn(nk, R, generator=g, device="cuda") * 0.05, dtype)
+    width = nproj + (2 * R if lora else 0)
+    dy1 = torch.full((T, width), float("nan"), dtype=dtype, device="cuda")
+    dq = torch.empty(T, hq, D, dtype=dtype, device="cuda")
+    dk = torch.empty(T, hk, D, dtype=dtype, device="cuda")
+    dv = dy1[:, nq + nk:nproj].view(T, hk, D)
+    ops.varlen_attn_bwd(do, q, k, v, out, lse, cu, max(lengths), scale, dq=dq, dk=dk, dv=dv)
+    ops.qkv_epilogue_bwd(dq, dk, cos, sin, frag, 2.0, dy1, hq, hk)
+    dy2 = torch.full((T, width), float("nan"), dtype=dtype, device="cuda")
+    ops.attn_qkv_bwd(do, q, k, v, out, lse, cu, max(lengths), scale, cos, sin, frag, 2.0, dy2)
+    assert torch.isfinite(dy2).all()
+    for name, sl in (("dq", slice(0, nq)), ("dk", slice(nq, nq + nk)), ("dv", slice(nq + nk, nproj)),
+                     ("du", slice(nproj, width))):
+        a, b = dy2[:, sl].float(), dy1[:, sl].float()
+        if a.numel() == 0:
+            continue
+        assert (a - b).norm() <= 2e-3 * b.norm().clamp_min(1e-6), name
+        assert (a == b).float().mean().item() >= 0.5, name
+    assert cuda_lib.decik_kernel_error(1) == 0
