@@ -229,6 +229,10 @@ def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0
 
 REF_BUDGET_S = 90.0  # the reference arm's timed steps, seconds
 
+# DRAM bytes (read + write) of the two attention kernels in one config-3 step, from the ncu capture
+# in profiles/attn_block_fused_config3.md (forward 68.1 + 15.6 MB, backward 412.0 + 186.0 MB)
+ATTN_DRAM_BYTES = {"config3": 681.6e6}
+
 
 def run_reference(args, world, rank):
     if rank != 0:
@@ -365,7 +369,10 @@ def run_ours(args, world, rank, local):
                    "l2": "flushed between timed steps (256 MiB write, untimed)", "parallelism": f"dp{world}"},
         "roofline": {"bound": "tensor", "kernel": "varlen attention fwd+bwd (decik_varlen_attn_fwd/bwd)",
                      "achieved": round(attn_tflops, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": round(attn_tflops / pk["bf16_tflops"], 4), "traffic": None,
+                     "frac": round(attn_tflops / pk["bf16_tflops"], 4),
+                     "traffic": ATTN_DRAM_BYTES.get(args.workload),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of both kernels, one step"
+                     if args.workload in ATTN_DRAM_BYTES else None,
                      "flops_per_step": 3.0 * f_fwd, "peak_source": pk["source"]},
         "attn_tflops": round(attn_tflops, 2),
         "kernels": kernels,
