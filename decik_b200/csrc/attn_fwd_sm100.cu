@@ -367,21 +367,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
         // keys past min(query, row end) are masked; only the diagonal / last block has any
         const int lim = min(qi, w.L - 1) - j * BN;  // last visible column of this row in this block
         const bool masked = lim < BN - 1;
-        // pass 1: row max of the raw scores (scale > 0 commutes with max), 64 columns at a time
+        // pass 1: row max of the raw scores (scale > 0 commutes with max); keys past min(query, row
+        // end) count as -inf. The second 64 columns stay in registers for pass 2.
         float mx = -INFINITY;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        uint32_t s1v[64];
+        {
           uint32_t sv[64];
-          tmem_ld32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-          tmem_ld32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+          tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+          tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(&s1v[0]));
+          tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(&s1v[32]));
           tmem_ld_wait();
           if (masked) {
 #pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (64 * h + c > lim) sv[c] = __float_as_uint(-INFINITY);
+            for (int c = 0; c < 64; ++c) {
+              if (c > lim) sv[c] = __float_as_uint(-INFINITY);
+              if (64 + c > lim) s1v[c] = __float_as_uint(-INFINITY);
+            }
           }
 #pragma unroll
-          for (int c = 0; c < 64; c += 2) mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+          for (int c = 0; c < 64; c += 2) {
+            mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+            mx = fmax3(mx, __uint_as_float(s1v[c]), __uint_as_float(s1v[c + 1]));
+          }
         }
         const float m_new = fmaxf(m_run, mx * p.scale_log2);
         const bool resc = m_new > m_run + 8.f;
@@ -404,25 +412,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
           tmem_st_wait();
         }
         // pass 2: P = exp2(s * scale*log2e - m_run), packed FMA for the arguments and packed adds for
-        // the sum; P (16-bit pairs) overwrites the first 64 columns of S
+        // the sum; P (16-bit pairs) overwrites the first 64 columns of S: the first half's P over
+        // columns 0-31 (re-read just before), then the second half's over 32-63
         const uint64_t sc2 = f2(p.scale_log2, p.scale_log2);
         const uint64_t nm2 = f2(-m_run, -m_run);
         uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t sv[64], pk[32];
-          tmem_ld32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-          tmem_ld32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-          tmem_ld_wait();
-          if (masked) {
+          if (h == 0) {
+            tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+            tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+            tmem_ld_wait();
+            if (masked) {
 #pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (64 * h + c > lim) sv[c] = __float_as_uint(-INFINITY);
+              for (int c = 0; c < 64; ++c)
+                if (c > lim) sv[c] = __float_as_uint(-INFINITY);
+            }
           }
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
+            const uint32_t a0 = h ? s1v[2 * c] : sv[2 * c], a1 = h ? s1v[2 * c + 1] : sv[2 * c + 1];
             float x0, x1;
-            f2split(ffma2(f2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])), sc2, nm2), x0, x1);
+            f2split(ffma2(f2(__uint_as_float(a0), __uint_as_float(a1)), sc2, nm2), x0, x1);
             const float e0 = ptx::ex2(x0), e1 = ptx::ex2(x1);
             acc[c & 3] = fadd2(acc[c & 3], f2(e0, e1));
             pk[c] = pk2<T>(e0, e1);
