@@ -16,6 +16,14 @@ F16, BF16, F32 = 0, 1, 2
 c_void_p, c_int, c_int64, c_float = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 
 
+class Nf4Job(ctypes.Structure):
+    """decik_nf4_job of include/decik_b200.h."""
+    _fields_ = [("packed", ctypes.c_void_p), ("absmax", ctypes.c_void_p), ("absmax2", ctypes.c_void_p),
+                ("code2", ctypes.c_void_p), ("offset", ctypes.c_void_p), ("code", ctypes.c_void_p),
+                ("out", ctypes.c_void_p), ("n_bytes", ctypes.c_int64), ("nested", ctypes.c_int),
+                ("blocksize", ctypes.c_int), ("blocksize2", ctypes.c_int)]
+
+
 class Tensor3(ctypes.Structure):
     """decik_tensor3 / decik_tensor3_mut: (pointer, token stride, head stride), strides in elements."""
     _fields_ = [("ptr", c_void_p), ("tok_stride", c_int64), ("head_stride", c_int64)]
@@ -26,6 +34,7 @@ SIGNATURES = {
     "decik_last_error": (ctypes.c_char_p, []),
     "decik_abi_version": (c_int, []),
     "decik_kernel_error": (c_int, [c_int]),
+    "decik_nf4_dequant_batch": (c_int, [c_void_p, c_int, c_int, c_void_p]),
     "decik_nf4_dequant": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_int64, c_int, c_int, c_int, c_int, c_void_p]),
     "decik_rope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

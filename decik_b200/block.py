@@ -108,17 +108,18 @@ class QLoRAAttentionBlock:
     def dequant_cat(self) -> torch.Tensor:
         """This step's W_q, W_k, W_v (NF4 -> dtype, bit-exact) as the first rows of a fresh
         [(Hq+2Hk)*D + 2r, hidden] matrix; the fused forward fills the last 2r rows with A_q, A_v."""
-        from .solution.nf4 import dequantize_nf4
+        from .solution.nf4 import dequantize_nf4_many
 
         rows = [self.weights[n][1].shape[0] for n in ("q", "k", "v")]
         rank = self.lora["a_q"].shape[0]
         hidden = self.weights["q"][1].shape[1]
         w = torch.empty((sum(rows) + 2 * rank, hidden), dtype=self.dtype, device=self.device)
-        r0 = 0
+        items, r0 = [], 0
         for n, nr in zip(("q", "k", "v"), rows):
             packed, qs = self.weights[n]
-            dequantize_nf4(packed, qs, self.dtype, out=w[r0:r0 + nr])
+            items.append((packed, qs, w[r0:r0 + nr]))
             r0 += nr
+        dequantize_nf4_many(items, self.dtype)  # one launch for the three
         return w
 
     def forward(self, x: torch.Tensor, packing: Packing, cos: torch.Tensor, sin: torch.Tensor,

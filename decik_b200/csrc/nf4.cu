@@ -59,6 +59,14 @@ struct Nf4Args {
   int blocksize2;
 };
 
+// Up to kMaxJobs weights in one launch: grid y = job. All of a launch's jobs share the template
+// flags (nested, vectorised) and the output type.
+constexpr int kMaxJobs = 4;
+struct Nf4Batch {
+  Nf4Args a[kMaxJobs];
+  void* out[kMaxJobs];
+};
+
 template <bool NESTED>
 __device__ __forceinline__ float block_scale(const Nf4Args& a, const float* s_code2, float offset,
                                              int64_t block) {
@@ -72,7 +80,9 @@ __device__ __forceinline__ float block_scale(const Nf4Args& a, const float* s_co
 
 // VEC: 16 bytes per step (needs 16-byte aligned packed and out). Otherwise one byte per step.
 template <typename OutT, bool NESTED, bool VEC>
-__global__ void __launch_bounds__(256) nf4_dequant_kernel(Nf4Args a, OutT* __restrict__ out) {
+__global__ void __launch_bounds__(256) nf4_dequant_kernel(const __grid_constant__ Nf4Batch bt) {
+  const Nf4Args& a = bt.a[blockIdx.y];
+  OutT* __restrict__ out = static_cast<OutT*>(bt.out[blockIdx.y]);
   __shared__ float s_code[16];
   __shared__ float s_code2[256];
   if (threadIdx.x < 16) s_code[threadIdx.x] = a.code[threadIdx.x];
@@ -128,21 +138,75 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(Nf4Args a, OutT* __res
 }
 
 template <typename OutT>
-int launch(const Nf4Args& a, void* out, bool nested, cudaStream_t stream) {
-  const bool vec = aligned16(a.packed) && aligned16(out);
-  const int64_t work = vec ? (a.n_bytes >> 4) + 1 : a.n_bytes;
+int launch(const Nf4Batch& bt, int n, bool nested, bool vec, cudaStream_t stream) {
+  int64_t work = 0;
+  for (int j = 0; j < n; ++j) work = std::max<int64_t>(work, vec ? (bt.a[j].n_bytes >> 4) + 1 : bt.a[j].n_bytes);
   const int64_t want = (work + 255) / 256;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
-  const int grid = static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
-  OutT* o = reinterpret_cast<OutT*>(out);
+  const int64_t cap = std::max<int64_t>(1, static_cast<int64_t>(sm_count()) * 8 / n);
+  const dim3 grid(static_cast<unsigned>(want < cap ? (want > 0 ? want : 1) : cap), static_cast<unsigned>(n));
   if (nested) {
-    if (vec) nf4_dequant_kernel<OutT, true, true><<<grid, 256, 0, stream>>>(a, o);
-    else nf4_dequant_kernel<OutT, true, false><<<grid, 256, 0, stream>>>(a, o);
+    if (vec) nf4_dequant_kernel<OutT, true, true><<<grid, 256, 0, stream>>>(bt);
+    else nf4_dequant_kernel<OutT, true, false><<<grid, 256, 0, stream>>>(bt);
   } else {
-    if (vec) nf4_dequant_kernel<OutT, false, true><<<grid, 256, 0, stream>>>(a, o);
-    else nf4_dequant_kernel<OutT, false, false><<<grid, 256, 0, stream>>>(a, o);
+    if (vec) nf4_dequant_kernel<OutT, false, true><<<grid, 256, 0, stream>>>(bt);
+    else nf4_dequant_kernel<OutT, false, false><<<grid, 256, 0, stream>>>(bt);
   }
   return check_launch("nf4_dequant");
+}
+
+int check_job(const decik_nf4_job& j) {
+  if (j.n_bytes < 0) return set_error(DECIK_ERR_INVALID, "nf4_dequant: n_bytes < 0");
+  if (j.n_bytes > 0 && (!j.packed || !j.absmax || !j.code || !j.out))
+    return set_error(DECIK_ERR_INVALID, "nf4_dequant: null pointer");
+  if (j.blocksize <= 0 || j.blocksize % 2 != 0)
+    return set_error(DECIK_ERR_INVALID, "nf4_dequant: blocksize %d must be even and > 0", j.blocksize);
+  if (j.nested && (!j.absmax2 || !j.code2 || !j.offset || j.blocksize2 <= 0))
+    return set_error(DECIK_ERR_INVALID, "nf4_dequant: nested needs absmax2, code2, offset, blocksize2");
+  return DECIK_OK;
+}
+
+// groups the jobs by (nested, vectorised) and launches each group in batches of kMaxJobs
+int run_jobs(const decik_nf4_job* jobs, int n_jobs, int out_dtype, cudaStream_t s) {
+  if (out_dtype != DECIK_F16 && out_dtype != DECIK_BF16 && out_dtype != DECIK_F32)
+    return set_error(DECIK_ERR_INVALID, "nf4_dequant: out_dtype %d", out_dtype);
+  for (int j = 0; j < n_jobs; ++j) {
+    const int rc = check_job(jobs[j]);
+    if (rc) return rc;
+  }
+  for (int kind = 0; kind < 4; ++kind) {
+    const bool nested = kind & 1, vec = kind & 2;
+    Nf4Batch bt;
+    int n = 0;
+    for (int j = 0; j < n_jobs; ++j) {
+      const decik_nf4_job& jb = jobs[j];
+      if (jb.n_bytes == 0 || (jb.nested != 0) != nested || (aligned16(jb.packed) && aligned16(jb.out)) != vec) continue;
+      bt.a[n] = Nf4Args{jb.packed, jb.absmax, jb.absmax2, jb.code2, jb.offset, jb.code, jb.n_bytes, jb.blocksize,
+                        jb.blocksize2};
+      bt.out[n] = jb.out;
+      if (++n == kMaxJobs || j == n_jobs - 1) {
+        int rc = DECIK_OK;
+        if (n > 0) {
+          switch (out_dtype) {
+            case DECIK_F16: rc = launch<__half>(bt, n, nested, vec, s); break;
+            case DECIK_BF16: rc = launch<__nv_bfloat16>(bt, n, nested, vec, s); break;
+            default: rc = launch<float>(bt, n, nested, vec, s); break;
+          }
+        }
+        if (rc) return rc;
+        n = 0;
+      }
+    }
+    if (n > 0) {  // the last job of the list was not of this kind
+      int rc;
+      switch (out_dtype) {
+        case DECIK_F16: rc = launch<__half>(bt, n, nested, vec, s); break;
+        case DECIK_BF16: rc = launch<__nv_bfloat16>(bt, n, nested, vec, s); break;
+        default: rc = launch<float>(bt, n, nested, vec, s); break;
+      }
+      if (rc) return rc;
+    }
+  }
+  return DECIK_OK;
 }
 
 }  // namespace
@@ -152,21 +216,14 @@ extern "C" int decik_nf4_dequant(const uint8_t* packed, const void* absmax, cons
                                  const float* code2, const float* offset, const float* code,
                                  void* out, int64_t n_bytes, int nested, int blocksize,
                                  int blocksize2, int out_dtype, void* stream) {
-  using namespace decik;
-  if (n_bytes < 0) return set_error(DECIK_ERR_INVALID, "nf4_dequant: n_bytes < 0");
+  if (n_bytes < 0) return decik::set_error(DECIK_ERR_INVALID, "nf4_dequant: n_bytes < 0");
   if (n_bytes == 0) return DECIK_OK;
-  if (!packed || !absmax || !code || !out)
-    return set_error(DECIK_ERR_INVALID, "nf4_dequant: null pointer");
-  if (blocksize <= 0 || blocksize % 2 != 0)
-    return set_error(DECIK_ERR_INVALID, "nf4_dequant: blocksize %d must be even and > 0", blocksize);
-  if (nested && (!absmax2 || !code2 || !offset || blocksize2 <= 0))
-    return set_error(DECIK_ERR_INVALID, "nf4_dequant: nested needs absmax2, code2, offset, blocksize2");
-  Nf4Args a{packed, absmax, absmax2, code2, offset, code, n_bytes, blocksize, blocksize2};
-  cudaStream_t s = as_stream(stream);
-  switch (out_dtype) {
-    case DECIK_F16: return launch<__half>(a, out, nested != 0, s);
-    case DECIK_BF16: return launch<__nv_bfloat16>(a, out, nested != 0, s);
-    case DECIK_F32: return launch<float>(a, out, nested != 0, s);
-    default: return set_error(DECIK_ERR_INVALID, "nf4_dequant: out_dtype %d", out_dtype);
-  }
+  const decik_nf4_job j{packed, absmax, absmax2, code2, offset, code, out, n_bytes, nested, blocksize, blocksize2};
+  return decik::run_jobs(&j, 1, out_dtype, decik::as_stream(stream));
+}
+
+extern "C" int decik_nf4_dequant_batch(const decik_nf4_job* jobs, int n_jobs, int out_dtype, void* stream) {
+  if (n_jobs < 0 || (n_jobs > 0 && jobs == nullptr))
+    return decik::set_error(DECIK_ERR_INVALID, "nf4_dequant_batch: bad job list");
+  return decik::run_jobs(jobs, n_jobs, out_dtype, decik::as_stream(stream));
 }

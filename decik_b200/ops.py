@@ -65,6 +65,31 @@ def nf4_dequant(packed: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, 
     return out
 
 
+def nf4_dequant_batch(jobs, out_dtype: torch.dtype) -> None:
+    """Several NF4 weights in one launch (decik_nf4_dequant_batch). ``jobs``: tuples (packed, absmax,
+    code, shape, blocksize, absmax2, code2, offset, blocksize2, out) with nf4_dequant's meaning; each
+    ``out`` a contiguous [N, K] of ``out_dtype`` (e.g. row slices of one matrix)."""
+    arr = (_lib.Nf4Job * len(jobs))()
+    stream = None
+    for i, (packed, absmax, code, shape, blocksize, absmax2, code2, offset, blocksize2, out) in enumerate(jobs):
+        nested = absmax.dtype == torch.uint8
+        _cuda(packed, absmax, code, absmax2, code2, offset, out)
+        n_out, n_in = int(shape[0]), int(shape[1])
+        if packed.numel() < n_out * n_in // 2:
+            raise RuntimeError("decik_b200 nf4_dequant: packed tensor smaller than shape")
+        if not (out.is_contiguous() and out.numel() == n_out * n_in and out.dtype == out_dtype):
+            raise RuntimeError("decik_b200 nf4_dequant: out must be contiguous [N, K] of out_dtype")
+        arr[i] = _lib.Nf4Job(_p(packed), _p(absmax), _p(absmax2) if nested else None, _p(code2) if nested else None,
+                             _p(offset) if nested else None, _p(code), _p(out), n_out * n_in // 2, int(nested),
+                             int(blocksize), int(blocksize2))
+        stream = _stream(packed)
+    if not jobs:
+        return
+    with _timed("nf4_dequant", 1):
+        rc = _lib.lib().decik_nf4_dequant_batch(ctypes.addressof(arr), len(jobs), _DT[out_dtype], stream)
+    _lib.check(rc, "nf4_dequant_batch")
+
+
 # ------------------------------------------------------------------------------------------------
 # RoPE
 # ------------------------------------------------------------------------------------------------

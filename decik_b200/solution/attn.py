@@ -258,7 +258,7 @@ def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_k
     """The attention output [1, T, Hq*D] through FusedAttentionBlock, or None when this layer does not
     qualify: both LoRA branches without dropout, rank 16 and one scaling; q, k, v NF4 linears of the
     compute dtype; the varlen attention switched on; head_dim 128."""
-    from .nf4 import dequantize_nf4
+    from .nf4 import dequantize_nf4_many
 
     pq, pv = _lora_parts(self.q_proj, q_name), _lora_parts(self.v_proj, v_name)
     if not (STATE.varlen_attention and head_dim == 128 and pq is not None and pv is not None
@@ -275,11 +275,12 @@ def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_k
         return None
     n_tok = x.shape[1]
     w_cat = torch.empty((sum(rows) + 32, hidden), dtype=dtype, device=x.device)
-    biases, r0 = [], 0
+    biases, items, r0 = [], [], 0
     for (packed, qs, bias), nr in zip(parts, rows):
-        dequantize_nf4(packed, qs, dtype, out=w_cat[r0:r0 + nr])
+        items.append((packed, qs, w_cat[r0:r0 + nr]))
         biases.append(bias.float() if bias is not None else torch.zeros(nr, device=x.device))
         r0 += nr
+    dequantize_nf4_many(items, dtype)  # W_q, W_k, W_v into their rows, one launch
     bias_cat = torch.cat(biases + [torch.zeros(32, device=x.device)]).to(dtype)
     out = FusedAttentionBlock.apply(x.reshape(n_tok, hidden), pq[0], pq[1], pv[0], pv[1], w_cat, bias_cat,
                                     cos.reshape(n_tok, -1), sin.reshape(n_tok, -1),

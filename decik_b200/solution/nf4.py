@@ -49,6 +49,24 @@ def dequantize_nf4(packed, quant_state, dtype=torch.float16, out=None):
     return ops.nf4_dequant(packed, qs.absmax, code, qs.shape, qs.blocksize, out_dtype=dtype, out=out)
 
 
+def dequantize_nf4_many(items, dtype):
+    """Several weights at once, one launch: ``items`` = [(packed, quant_state, out)], each out a
+    contiguous [N, K] of ``dtype`` (e.g. the row slices of one matrix). Same values as
+    dequantize_nf4 per item."""
+    jobs = []
+    for packed, qs, out in items:
+        code = qs.code if qs.code.device == packed.device else qs.code.to(packed.device)
+        if qs.nested:
+            offset = qs.offset
+            if not torch.is_tensor(offset):
+                offset = torch.tensor([float(offset)], dtype=torch.float32, device=packed.device)
+            jobs.append((packed, qs.absmax, code, qs.shape, qs.blocksize, qs.state2.absmax, qs.state2.code,
+                         offset.reshape(1).to(device=packed.device, dtype=torch.float32), qs.state2.blocksize, out))
+        else:
+            jobs.append((packed, qs.absmax, code, qs.shape, qs.blocksize, None, None, None, 256, out))
+    ops.nf4_dequant_batch(jobs, dtype)
+
+
 class NF4Linear(torch.autograd.Function):
     """F.linear(x, dequant(W), bias) with 16-bit x; the input gradient dequantizes W again, as
     bitsandbytes' MatMul4Bit does (solution/nf4.py:88-104)."""

@@ -67,6 +67,25 @@ DECIK_API int decik_nf4_dequant(const uint8_t* packed, const void* absmax, const
                       int64_t n_bytes, int nested, int blocksize, int blocksize2, int out_dtype,
                       void* stream);
 
+/* Several NF4 weights in one launch (the block's W_q, W_k, W_v into the row slices of one matrix):
+ * each job has decik_nf4_dequant's arguments; all share the output dtype. Jobs whose form differs
+ * (nested or not, 16-byte aligned or not) go to separate launches. Same results as one
+ * decik_nf4_dequant call per job. */
+typedef struct {
+  const uint8_t* packed;
+  const void* absmax;
+  const float* absmax2;
+  const float* code2;
+  const float* offset;
+  const float* code;
+  void* out;
+  int64_t n_bytes;
+  int nested;
+  int blocksize;
+  int blocksize2;
+} decik_nf4_job;
+DECIK_API int decik_nf4_dequant_batch(const decik_nf4_job* jobs, int n_jobs, int out_dtype, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * LoRA add + RoPE + cast, forward. Replaces FusedQKRope.forward / skc_rope_fwd_kernel
  * (solution/attn.py:28-61, :97-111). Bit-exact (each fp32 product and sum rounded, no FMA):

@@ -86,6 +86,38 @@ def test_nf4_vs_oracle_bit_exact(cuda_lib, shape, nested, bs, dtype):
         assert np.array_equal(out.numpy().view(np.uint32), ref.view(np.uint32))
 
 
+def test_nf4_dequant_batch_matches_single_calls(cuda_lib):
+    """decik_nf4_dequant_batch over a mixed batch (nested and plain weights, one output slice not
+    16-byte aligned, so the jobs go to separate launches by kind) equals one call per weight."""
+    ops = _ops()
+    rng = np.random.default_rng(11)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+    shapes = [((1536, 1536), True), ((256, 1536), True), ((256, 1536), False), ((64, 96), True)]
+    states = [o_nf4.quantize_nf4((rng.standard_normal(sh) * 0.02).astype(np.float32), nested=nested)
+              for sh, nested in shapes]
+    rows = sum(sh[0] for sh, _ in shapes)
+    big = torch.zeros(rows * 1536 + 8, dtype=torch.bfloat16, device=DEV)
+    jobs, refs, r0 = [], [], 0
+    for (sh, nested), st in zip(shapes, states):
+        n = sh[0] * sh[1]
+        # the last weight's output starts 8 bytes off a 16-byte boundary
+        off = r0 + (4 if sh == (64, 96) else 0)
+        out = big[off:off + n].view(sh)
+        args = (t(st["packed"]), t(st["absmax"]), t(st["code"]), sh, 64)
+        if nested:
+            extra = (t(st["absmax2"]), t(st["code2"]), torch.tensor([float(st["offset"])], device=DEV), 256)
+        else:
+            extra = (None, None, None, 256)
+        jobs.append(args + extra + (out,))
+        refs.append(ops.nf4_dequant(*args, absmax2=extra[0], code2=extra[1], offset=extra[2], blocksize2=256,
+                                    out_dtype=torch.bfloat16))
+        r0 += n
+    ops.nf4_dequant_batch(jobs, torch.bfloat16)
+    for job, ref in zip(jobs, refs):
+        assert torch.equal(job[-1], ref)
+    assert cuda_lib.decik_kernel_error(1) == 0
+
+
 def test_nf4_unaligned_views(cuda_lib):
     """Packed bytes at an odd offset take the scalar path; results are still bit-exact."""
     ops = _ops()
