@@ -82,6 +82,18 @@ WORKLOADS = {
 }
 
 
+# full QLoRA train steps of the 28-layer Qwen2.5-1.5B shape (decik_b200.qlora_model):
+# name -> (tokens per GPU, log-normal median, min, max length, workload text)
+FULL_STEP = {
+    "config2": (830, 180, 16, 1024,
+                "28-layer Qwen2.5-1.5B NF4 QLoRA train step (fwd + loss + bwd + AdamW lr 2e-4, LoRA r16 q,v) "
+                "over ~830 packed tokens, through solution.apply()"),
+    "config5": (16384, 512, 16, 4096,
+                "28-layer Qwen2.5-1.5B NF4 QLoRA train step (fwd + loss + bwd + LoRA-grad all-reduce + AdamW "
+                "lr 2e-4) over 16,384 packed tokens per GPU, through solution.apply()"),
+}
+
+
 def causal_flops(lengths, n_heads=HQ, head_dim=D) -> float:
     return 4.0 * head_dim * n_heads * sum(L * (L + 1) // 2 for L in lengths)
 
@@ -421,6 +433,193 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def full_step_lengths(workload: str, rank: int) -> list[int]:
+    from decik_b200.qlora_model import lognormal_lengths
+
+    total, median, lo, hi, _ = FULL_STEP[workload]
+    return lognormal_lengths(1000 + rank, total, median, lo, hi)
+
+
+def run_full_step(args, world, rank, local):
+    """The whole QLoRA train step of the 28-layer model through the reference-facing surface:
+    solution.apply() patches the model; each step is forward + loss + backward (+ the LoRA-grad
+    all-reduce on N > 1) + AdamW."""
+    from decik_b200 import ops, solution
+    from decik_b200.dp import GradBucket, global_count
+    from decik_b200.qlora_model import (QWEN25_15B, Linear4bit, LoraLinear, build_qlora_qwen2,
+                                        lora_parameters, padded_batch, qlora_train_step)
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    total, median, lo, hi, workload = FULL_STEP[args.workload]
+    model = build_qlora_qwen2(device=dev, seed=0)
+    solution.apply(linear4bit_cls=Linear4bit, lora_classes=(LoraLinear,))
+    n_layers = QWEN25_15B["layers"]
+    lengths = full_step_lengths(args.workload, rank)
+    T = sum(lengths)
+    ids, mask, labels = padded_batch(lengths, QWEN25_15B["vocab"], 2000 + rank, dev)
+    params = lora_parameters(model)
+    bucket = GradBucket(params)
+    opt = torch.optim.AdamW(params, lr=2e-4)
+    # labelled tokens of this step over all ranks (each row's last token has no next-token label)
+    n_labels = global_count(torch.tensor(float(T - len(lengths)), device=dev)).to(dev)
+
+    def step(i_ids, i_mask, i_labels):
+        bucket.zero_()
+        loss = qlora_train_step(model, i_ids, i_mask, i_labels, n_labels=n_labels)
+        bucket.all_reduce()
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step(ids, mask, labels)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    timer = ops.OpTimer()
+    ops.install_timer(timer)
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            starts[i].record()
+            step(ids, mask, labels)
+            ends[i].record()
+        torch.cuda.synchronize()
+    ops.install_timer(None)
+    op_ms = timer.elapsed_ms()
+    step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = world * T * args.steps / (total_ms / 1e3)
+
+    # end to end: each step's token ids, mask and labels copied from pinned host memory and its loss
+    # read back into pinned host memory, all inside the timed region
+    h_ids, h_mask, h_labels = (t.cpu().pin_memory() for t in (ids, mask, labels))
+    h_loss = torch.empty(args.steps, dtype=torch.float32).pin_memory()
+    d_ids, d_mask, d_labels = torch.empty_like(ids), torch.empty_like(mask), torch.empty_like(labels)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        d_ids.copy_(h_ids, non_blocking=True)
+        d_mask.copy_(h_mask, non_blocking=True)
+        d_labels.copy_(h_labels, non_blocking=True)
+        loss = step(d_ids, d_mask, d_labels)
+        h_loss[i:i + 1].copy_(loss.reshape(1), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+    if rank != 0:
+        return
+    pk = peaks()
+    f_fwd = causal_flops(lengths, n_heads=QWEN25_15B["heads"]) * n_layers
+    fwd_ms = sum(op_ms.get("varlen_attn_fwd", [float("nan")])) / args.steps
+    bwd_ms = sum(op_ms.get("varlen_attn_bwd", [float("nan")])) / args.steps
+    attn_tflops = 3.0 * f_fwd / ((fwd_ms + bwd_ms) / 1e3) / 1e12
+    kernels = {name: {"ms_per_step": round(sum(v) / args.steps, 4), "calls_per_step": len(v) // max(args.steps, 1)}
+               for name, v in op_ms.items()}
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded log-normal lengths, uniform token ids, random-init NF4 weights and LoRA)",
+        "config": {"workload": workload, "tokens_per_gpu": T, "rows_rank0": len(lengths),
+                   "lengths": f"log-normal median {median} sigma 1 in [{lo},{hi}], numpy default_rng(1000 + rank)",
+                   "model": "Qwen2.5-1.5B shape: 28 layers, hidden 1536, inter 8960, 12/2 heads, vocab 151936",
+                   "lora": "r16 alpha32 q,v", "nf4": "bs64, double quant bs256 (all 7 linears per layer)",
+                   "l2": "not flushed: each step streams the 0.7 GB of NF4 weights and the 0.9 GB embedding (> L2)",
+                   "parallelism": f"dp{world}"},
+        "roofline": {"bound": "tensor", "kernel": "varlen attention fwd+bwd of the 28 layers (decik_varlen_attn_fwd/bwd)",
+                     "achieved": round(attn_tflops, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(attn_tflops / pk["bf16_tflops"], 4), "traffic": None,
+                     "flops_per_step": 3.0 * f_fwd, "peak_source": pk["source"]},
+        "attn_tflops": round(attn_tflops, 2),
+        "kernels": kernels,
+        "gpu_launches": timer.launches,
+        "clocks": clocks.summary(),
+        "loss_last": round(float(h_loss[-1]), 5),
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (h_ids, h_mask, h_labels)),
+                "d2h_bytes_per_step": 4},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_full(args, world, rank):
+    """The reference's CPU path for the full step: the same model on the host in fp32 with the
+    original transformers code (no patches), NF4 weights dequantised by the torch restatement of
+    solution/nf4.py:36-48 each call; a bounded sample of the first rows of the workload."""
+    if rank != 0:
+        return
+    from decik_b200.qlora_model import (QWEN25_15B, Linear4bit, build_qlora_qwen2, lora_parameters,
+                                        padded_batch, qlora_train_step)
+    from oracle.block import dequant_torch_qs
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    *_, workload = FULL_STEP[args.workload]
+    t_build = time.perf_counter()
+    model = build_qlora_qwen2(device="cpu", seed=0, share_layer_weights=True)
+    build_s = time.perf_counter() - t_build
+
+    def cpu_forward(self, x):
+        w = dequant_torch_qs(self.weight.data, self.weight.quant_state)
+        return torch.nn.functional.linear(x.float(), w, None if self.bias is None else self.bias.float())
+
+    Linear4bit.forward = cpu_forward
+    lengths = full_step_lengths(args.workload, 0)
+    opt = torch.optim.AdamW(lora_parameters(model), lr=2e-4)
+
+    def run(sample_tokens, n):
+        rows, t = [], 0
+        for L in lengths:
+            if t >= sample_tokens:
+                break
+            rows.append(min(L, sample_tokens - t))
+            t += rows[-1]
+        ids, mask, labels = padded_batch(rows, QWEN25_15B["vocab"], 2000, "cpu")
+        times = []
+        for _ in range(n):
+            t0 = time.perf_counter()
+            model.zero_grad(set_to_none=True)
+            qlora_train_step(model, ids, mask, labels)
+            opt.step()
+            times.append(time.perf_counter() - t0)
+        return rows, times
+
+    sample = min(args.ref_tokens, 256)
+    if args.warmup:
+        _, warm = run(sample, 1)
+        if args.steps * warm[0] > REF_BUDGET_S:
+            sample = max(16, int(sample * REF_BUDGET_S / (args.steps * warm[0])))
+    rows, times = run(sample, args.steps)
+    value = sum(rows) / statistics.mean(times)
+    desc = (f"{len(rows)} rows, {sum(rows)} tokens (first rows of the packing), full 28-layer step fwd+bwd+AdamW, "
+            f"fp32, frozen NF4 weights shared by the layers (model build {build_s:.0f} s, untimed)")
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * statistics.mean(times), 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload + " (bounded CPU sample)", "tokens_per_gpu": sum(lengths),
+                       "sample": desc, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -429,8 +628,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ref-tokens", type=int, default=4096, help="tokens of the bounded CPU sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config3",
-                    help="config3: the 1.5B block over 16,384 tokens (default); config4: the 7B block over 131,072")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(FULL_STEP), default="config3",
+                    help="config3: the 1.5B block over 16,384 tokens (default); config4: the 7B block over "
+                         "131,072; config2 / config5: the full 28-layer QLoRA train step over ~830 / "
+                         "16,384 tokens per GPU")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 10 if args.impl == "reference" else 100
@@ -438,7 +639,12 @@ def main():
         args.warmup = 1 if args.impl == "reference" else 10
     world, rank, local = dist_setup()
     try:
-        if args.impl == "reference":
+        if args.workload in FULL_STEP:
+            if args.impl == "reference":
+                run_reference_full(args, world, rank)
+            else:
+                run_full_step(args, world, rank, local)
+        elif args.impl == "reference":
             run_reference(args, world, rank)
         else:
             run_ours(args, world, rank, local)

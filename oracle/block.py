@@ -44,6 +44,23 @@ def dequant_torch(state: dict) -> torch.Tensor:
     return w.reshape(state["shape"])
 
 
+def dequant_torch_qs(packed: torch.Tensor, qs) -> torch.Tensor:
+    """fp32 [N, K] weights from packed uint8 bytes and a QuantState-like object (fields absmax,
+    code, blocksize, shape, nested, state2.{absmax, code, blocksize}, offset), the same torch ops
+    as dequant_torch (solution/nf4.py:36-48)."""
+    p = packed.reshape(-1).to(torch.int64)
+    bs = int(qs.blocksize)
+    block = (torch.arange(p.numel(), dtype=torch.int64, device=p.device) * 2) // bs
+    if qs.nested:
+        q = qs.absmax.to(torch.int64)
+        scale = qs.state2.code[q[block]] * qs.state2.absmax[block // int(qs.state2.blocksize)]
+        scale = scale + qs.offset.reshape(-1)[0]
+    else:
+        scale = qs.absmax[block]
+    w = torch.stack((qs.code[p >> 4] * scale, qs.code[p & 15] * scale), dim=1)
+    return w.reshape(qs.shape)
+
+
 def rope_torch(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """x [T, H, D] -> x * cos + rotate_half(x) * sin (transformers' apply_rotary_pos_emb)."""
     half = x.shape[-1] // 2
