@@ -4,6 +4,14 @@
 //
 // One warp per row; each lane reads 4 consecutive floats per step (16-byte loads) and the row
 // reductions (mean of x^2, mean of g*x) are warp-shuffle trees.
+//
+// The decoder's residual add + post-attention norm (AddRMSNormFn, solution/rmsnorm.py:108-144,
+// called from the patched decoder layer, solution/varlen.py:323-337) is one pass each way:
+// forward h = residual + f32(delta), y = norm(h), writing h, y and rstd; backward rebuilds h from
+// residual and delta (h is not kept, as in the reference), then total = grad_h + norm_bwd(dy, h)
+// and its copy in delta's 16-bit type. The per-element and per-row arithmetic is the same source
+// as the plain kernels (sumsq4 / wdot4 / the output lines), so y and the norm gradient equal
+// rmsnorm_fwd / rmsnorm_bwd applied to the same h bit for bit.
 #include "common.cuh"
 
 namespace decik {
@@ -22,6 +30,58 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 constexpr int kMaxCols = 8192;
 
+// x . x of four values and the weighted dot g . (w x) of four, the per-step row terms of the
+// forward and backward reductions (shared by the plain and the fused kernels)
+__device__ __forceinline__ float sumsq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
+template <typename W>
+__device__ __forceinline__ float wdot4(float4 g, float4 v, const W* w, int c) {
+  return g.x * wload<W>(w, c) * v.x + g.y * wload<W>(w, c + 1) * v.y + g.z * wload<W>(w, c + 2) * v.z +
+         g.w * wload<W>(w, c + 3) * v.w;
+}
+template <typename W>
+__device__ __forceinline__ float4 norm_out4(float4 v, const W* w, int c, float rstd) {
+  float4 o;
+  o.x = wload<W>(w, c) * (v.x * rstd);
+  o.y = wload<W>(w, c + 1) * (v.y * rstd);
+  o.z = wload<W>(w, c + 2) * (v.z * rstd);
+  o.w = wload<W>(w, c + 3) * (v.w * rstd);
+  return o;
+}
+template <typename W>
+__device__ __forceinline__ float4 norm_grad4(float4 g, float4 v, const W* w, int c, float rstd, float k) {
+  float4 o;
+  o.x = rstd * (g.x * wload<W>(w, c) - v.x * k);
+  o.y = rstd * (g.y * wload<W>(w, c + 1) - v.y * k);
+  o.z = rstd * (g.z * wload<W>(w, c + 2) - v.z * k);
+  o.w = rstd * (g.w * wload<W>(w, c + 3) - v.w * k);
+  return o;
+}
+
+// four consecutive values of the delta operand as fp32, and four fp32 values stored in its type
+template <typename D>
+__device__ __forceinline__ float4 dload4(const D* p);
+template <> __device__ __forceinline__ float4 dload4<float>(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+template <typename D>
+__device__ __forceinline__ float4 dload4(const D* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  return make_float4(Dt<D>::lo_f(u.x), Dt<D>::hi_f(u.x), Dt<D>::lo_f(u.y), Dt<D>::hi_f(u.y));
+}
+template <typename D>
+__device__ __forceinline__ void dstore4(D* p, float4 v);
+template <> __device__ __forceinline__ void dstore4<float>(float* p, float4 v) {
+  *reinterpret_cast<float4*>(p) = v;
+}
+template <typename D>
+__device__ __forceinline__ void dstore4(D* p, float4 v) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(Dt<D>::pack2(v.x, v.y), Dt<D>::pack2(v.z, v.w));
+}
+// residual + f32(delta), one fp32 rounding per element (the reference's fp32 + fp16 add)
+__device__ __forceinline__ float4 add4(float4 r, float4 d) {
+  return make_float4(__fadd_rn(r.x, d.x), __fadd_rn(r.y, d.y), __fadd_rn(r.z, d.z), __fadd_rn(r.w, d.w));
+}
+
 template <typename W>
 __global__ void __launch_bounds__(256)
 rmsnorm_fwd_kernel(const float* __restrict__ x, const W* __restrict__ w, float* __restrict__ y,
@@ -32,22 +92,12 @@ rmsnorm_fwd_kernel(const float* __restrict__ x, const W* __restrict__ w, float* 
   if (row >= n_rows) return;
   const float* xr = x + row * sx;
   float acc = 0.f;
-  for (int c = lane * 4; c < n_cols; c += 128) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(xr + c));
-    acc += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-  }
+  for (int c = lane * 4; c < n_cols; c += 128) acc += sumsq4(__ldg(reinterpret_cast<const float4*>(xr + c)));
   const float mean_sq = warp_sum(acc) / static_cast<float>(n_cols);
   const float rstd = rsqrtf(mean_sq + eps);
   float* yr = y + row * sy;
-  for (int c = lane * 4; c < n_cols; c += 128) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(xr + c));
-    float4 o;
-    o.x = wload<W>(w, c) * (v.x * rstd);
-    o.y = wload<W>(w, c + 1) * (v.y * rstd);
-    o.z = wload<W>(w, c + 2) * (v.z * rstd);
-    o.w = wload<W>(w, c + 3) * (v.w * rstd);
-    *reinterpret_cast<float4*>(yr + c) = o;
-  }
+  for (int c = lane * 4; c < n_cols; c += 128)
+    *reinterpret_cast<float4*>(yr + c) = norm_out4<W>(__ldg(reinterpret_cast<const float4*>(xr + c)), w, c, rstd);
   if (rstd_out != nullptr && lane == 0) rstd_out[row] = rstd;
 }
 
@@ -63,24 +113,67 @@ rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
   const float* gr = dy + row * n_cols;
   const float rstd = rstd_in[row];
   float acc = 0.f;
-  for (int c = lane * 4; c < n_cols; c += 128) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(xr + c));
-    const float4 g = __ldg(reinterpret_cast<const float4*>(gr + c));
-    acc += g.x * wload<W>(w, c) * v.x + g.y * wload<W>(w, c + 1) * v.y +
-           g.z * wload<W>(w, c + 2) * v.z + g.w * wload<W>(w, c + 3) * v.w;
-  }
+  for (int c = lane * 4; c < n_cols; c += 128)
+    acc += wdot4<W>(__ldg(reinterpret_cast<const float4*>(gr + c)), __ldg(reinterpret_cast<const float4*>(xr + c)), w, c);
   const float dot = warp_sum(acc) / static_cast<float>(n_cols);
   const float k = rstd * rstd * dot;
   float* dr = dx + row * n_cols;
+  for (int c = lane * 4; c < n_cols; c += 128)
+    *reinterpret_cast<float4*>(dr + c) = norm_grad4<W>(__ldg(reinterpret_cast<const float4*>(gr + c)),
+                                                       __ldg(reinterpret_cast<const float4*>(xr + c)), w, c, rstd, k);
+}
+
+// h = residual + f32(delta); y = w * (h * rstd); rows contiguous ([n_rows, n_cols])
+template <typename W, typename D>
+__global__ void __launch_bounds__(256)
+add_rmsnorm_fwd_kernel(const float* __restrict__ residual, const D* __restrict__ delta, const W* __restrict__ w,
+                       float* __restrict__ h, float* __restrict__ y, float* __restrict__ rstd_out, int64_t n_rows,
+                       int n_cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
+  const int64_t off = row * n_cols;
+  float acc = 0.f;
   for (int c = lane * 4; c < n_cols; c += 128) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(xr + c));
-    const float4 g = __ldg(reinterpret_cast<const float4*>(gr + c));
-    float4 o;
-    o.x = rstd * (g.x * wload<W>(w, c) - v.x * k);
-    o.y = rstd * (g.y * wload<W>(w, c + 1) - v.y * k);
-    o.z = rstd * (g.z * wload<W>(w, c + 2) - v.z * k);
-    o.w = rstd * (g.w * wload<W>(w, c + 3) - v.w * k);
-    *reinterpret_cast<float4*>(dr + c) = o;
+    const float4 v = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
+    *reinterpret_cast<float4*>(h + off + c) = v;
+    acc += sumsq4(v);
+  }
+  const float mean_sq = warp_sum(acc) / static_cast<float>(n_cols);
+  const float rstd = rsqrtf(mean_sq + eps);
+  for (int c = lane * 4; c < n_cols; c += 128) {
+    const float4 v = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
+    *reinterpret_cast<float4*>(y + off + c) = norm_out4<W>(v, w, c, rstd);
+  }
+  if (rstd_out != nullptr && lane == 0) rstd_out[row] = rstd;
+}
+
+// total = grad_h + norm_bwd(dy, h) with h = residual + f32(delta) rebuilt; total in fp32 and,
+// when dx16 is set, in delta's type (the delta input's gradient)
+template <typename W, typename D>
+__global__ void __launch_bounds__(256)
+add_rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ grad_h,
+                       const float* __restrict__ residual, const D* __restrict__ delta, const W* __restrict__ w,
+                       const float* __restrict__ rstd_in, float* __restrict__ dx, D* __restrict__ dx16,
+                       int64_t n_rows, int n_cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
+  const int64_t off = row * n_cols;
+  const float rstd = rstd_in[row];
+  float acc = 0.f;
+  for (int c = lane * 4; c < n_cols; c += 128) {
+    const float4 v = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
+    acc += wdot4<W>(__ldg(reinterpret_cast<const float4*>(dy + off + c)), v, w, c);
+  }
+  const float dot = warp_sum(acc) / static_cast<float>(n_cols);
+  const float k = rstd * rstd * dot;
+  for (int c = lane * 4; c < n_cols; c += 128) {
+    const float4 v = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
+    float4 o = norm_grad4<W>(__ldg(reinterpret_cast<const float4*>(dy + off + c)), v, w, c, rstd, k);
+    if (grad_h != nullptr) o = add4(__ldg(reinterpret_cast<const float4*>(grad_h + off + c)), o);
+    *reinterpret_cast<float4*>(dx + off + c) = o;
+    if (dx16 != nullptr) dstore4<D>(dx16 + off + c, o);
   }
 }
 
@@ -124,4 +217,87 @@ extern "C" int decik_rmsnorm_bwd(const float* dy, const float* x, const void* w,
   else
     return set_error(DECIK_ERR_INVALID, "rmsnorm_bwd: w_dtype must be F32 or F16");
   return check_launch("rmsnorm_bwd");
+}
+
+namespace decik {
+namespace {
+
+int add_rmsnorm_check(int64_t n_rows, int n_cols, const void* delta, int d_dtype, int w_dtype, const char* what) {
+  using namespace decik;
+  if (n_rows < 0 || n_cols <= 0 || n_cols % 4 != 0 || n_cols > kMaxCols)
+    return set_error(DECIK_ERR_INVALID, "%s: n_cols %d (multiple of 4, <= 8192)", what, n_cols);
+  if (w_dtype != DECIK_F32 && w_dtype != DECIK_F16)
+    return set_error(DECIK_ERR_INVALID, "%s: w_dtype must be F32 or F16", what);
+  if (d_dtype != DECIK_F32 && d_dtype != DECIK_F16 && d_dtype != DECIK_BF16)
+    return set_error(DECIK_ERR_INVALID, "%s: delta dtype must be F32, F16 or BF16", what);
+  const uintptr_t align = d_dtype == DECIK_F32 ? 15u : 7u;
+  if (reinterpret_cast<uintptr_t>(delta) & align)
+    return set_error(DECIK_ERR_INVALID, "%s: delta must be %d-byte aligned", what, static_cast<int>(align + 1));
+  return DECIK_OK;
+}
+
+template <typename W, typename D>
+void launch_add_fwd(const float* residual, const void* delta, const void* w, float* h, float* y, float* rstd,
+                    int64_t n_rows, int n_cols, float eps, cudaStream_t st) {
+  add_rmsnorm_fwd_kernel<W, D><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+      residual, static_cast<const D*>(delta), static_cast<const W*>(w), h, y, rstd, n_rows, n_cols, eps);
+}
+template <typename W, typename D>
+void launch_add_bwd(const float* dy, const float* grad_h, const float* residual, const void* delta, const void* w,
+                    const float* rstd, float* dx, void* dx16, int64_t n_rows, int n_cols, cudaStream_t st) {
+  add_rmsnorm_bwd_kernel<W, D><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+      dy, grad_h, residual, static_cast<const D*>(delta), static_cast<const W*>(w), rstd, dx, static_cast<D*>(dx16),
+      n_rows, n_cols);
+}
+
+}  // namespace
+}  // namespace decik
+
+extern "C" int decik_add_rmsnorm_fwd(const float* residual, const void* delta, int delta_dtype, const void* w,
+                                     int w_dtype, float* h, float* y, float* rstd, int64_t n_rows, int n_cols,
+                                     float eps, void* stream) {
+  using namespace decik;
+  if (n_rows == 0) return DECIK_OK;
+  if (!residual || !delta || !w || !h || !y) return set_error(DECIK_ERR_INVALID, "add_rmsnorm_fwd: null pointer");
+  if (int rc = add_rmsnorm_check(n_rows, n_cols, delta, delta_dtype, w_dtype, "add_rmsnorm_fwd")) return rc;
+  if (!aligned16(residual) || !aligned16(h) || !aligned16(y))
+    return set_error(DECIK_ERR_INVALID, "add_rmsnorm_fwd: residual, h, y must be 16-byte aligned");
+  const cudaStream_t st = as_stream(stream);
+  const bool wf = w_dtype == DECIK_F32;
+  if (delta_dtype == DECIK_F32) {
+    (wf ? launch_add_fwd<float, float> : launch_add_fwd<__half, float>)(residual, delta, w, h, y, rstd, n_rows, n_cols, eps, st);
+  } else if (delta_dtype == DECIK_F16) {
+    (wf ? launch_add_fwd<float, __half> : launch_add_fwd<__half, __half>)(residual, delta, w, h, y, rstd, n_rows, n_cols, eps, st);
+  } else {
+    (wf ? launch_add_fwd<float, __nv_bfloat16> : launch_add_fwd<__half, __nv_bfloat16>)(residual, delta, w, h, y, rstd,
+                                                                                       n_rows, n_cols, eps, st);
+  }
+  return check_launch("add_rmsnorm_fwd");
+}
+
+extern "C" int decik_add_rmsnorm_bwd(const float* dy, const float* grad_h, const float* residual, const void* delta,
+                                     int delta_dtype, const void* w, int w_dtype, const float* rstd, float* dx,
+                                     void* dx16, int64_t n_rows, int n_cols, void* stream) {
+  using namespace decik;
+  if (n_rows == 0) return DECIK_OK;
+  if (!dy || !residual || !delta || !w || !rstd || !dx)
+    return set_error(DECIK_ERR_INVALID, "add_rmsnorm_bwd: null pointer");
+  if (int rc = add_rmsnorm_check(n_rows, n_cols, delta, delta_dtype, w_dtype, "add_rmsnorm_bwd")) return rc;
+  if (!aligned16(dy) || !aligned16(residual) || !aligned16(dx) || (grad_h && !aligned16(grad_h)))
+    return set_error(DECIK_ERR_INVALID, "add_rmsnorm_bwd: dy, grad_h, residual, dx must be 16-byte aligned");
+  if (dx16 && (reinterpret_cast<uintptr_t>(dx16) & (delta_dtype == DECIK_F32 ? 15u : 7u)))
+    return set_error(DECIK_ERR_INVALID, "add_rmsnorm_bwd: dx16 misaligned");
+  const cudaStream_t st = as_stream(stream);
+  const bool wf = w_dtype == DECIK_F32;
+  if (delta_dtype == DECIK_F32) {
+    (wf ? launch_add_bwd<float, float> : launch_add_bwd<__half, float>)(dy, grad_h, residual, delta, w, rstd, dx, dx16,
+                                                                      n_rows, n_cols, st);
+  } else if (delta_dtype == DECIK_F16) {
+    (wf ? launch_add_bwd<float, __half> : launch_add_bwd<__half, __half>)(dy, grad_h, residual, delta, w, rstd, dx, dx16,
+                                                                        n_rows, n_cols, st);
+  } else {
+    (wf ? launch_add_bwd<float, __nv_bfloat16> : launch_add_bwd<__half, __nv_bfloat16>)(dy, grad_h, residual, delta, w,
+                                                                                       rstd, dx, dx16, n_rows, n_cols, st);
+  }
+  return check_launch("add_rmsnorm_bwd");
 }

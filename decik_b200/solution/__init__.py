@@ -4,7 +4,8 @@
 ``SKC_<NAME>=0`` switches:
 - ``SKC_NF4``         bitsandbytes Linear4bit forward -> sm_100a NF4 dequant + linear (nf4.py)
 - ``SKC_RMSNORM``     Qwen2RMSNorm -> sm_100a RMSNorm, recorded as the LoRA input link (rmsnorm.py)
-- ``SKC_VARLEN``      padding-free decoder + varlen attention (varlen.py); ``SKC_VARLEN_ATTN``
+- ``SKC_VARLEN``      padding-free decoder + varlen attention (varlen.py); ``SKC_VARLEN_ATTN``;
+                      ``SKC_ADDNORM`` (residual add + post-attention norm as one node)
 - ``SKC_ATTN``        Qwen2Attention forward: LoRA + RoPE + varlen attention (attn.py);
                       ``SKC_LORA_RECOMPUTE``; ``SKC_FUSED_BLOCK`` (this build's addition: LoRA
                       without dropout runs as one fused projection + attention node)
@@ -35,7 +36,8 @@ def apply(linear4bit_cls=None, lora_classes=None):
     if _enabled("RMSNORM"):
         _try(rmsnorm.patch, "Qwen2RMSNorm")
     if _enabled("VARLEN"):
-        _try(varlen.patch, "Qwen2Model", varlen_attention=_enabled("VARLEN_ATTN"))
+        _try(varlen.patch, "Qwen2Model", varlen_attention=_enabled("VARLEN_ATTN"),
+             fuse_residual=_enabled("ADDNORM"))
         if _enabled("ATTN"):
             _try(attn.patch, "Qwen2Attention", recompute_lora=_enabled("LORA_RECOMPUTE"),
                  linear4bit_cls=linear4bit_cls, lora_classes=lora_classes,

@@ -1,7 +1,9 @@
 """Qwen2RMSNorm on the B200 kernel and the norm_link recompute (solution/rmsnorm.py).
 
-Only the parts the attention block needs: ``RMSNormFn`` (so the recompute in the LoRA backward
-is bit-identical to the forward, same kernel) and ``recompute`` (solution/rmsnorm.py:76-80).
+The parts on the attention block's path: ``RMSNormFn`` (so the recompute in the LoRA backward
+is bit-identical to the forward, same kernel), ``recompute`` (solution/rmsnorm.py:76-80), and
+``AddRMSNormFn`` / ``fusable`` (:108-155), the decoder's residual add + post-attention norm that
+consumes the block's output.
 """
 
 from __future__ import annotations
@@ -46,6 +48,42 @@ class RMSNormFn(torch.autograd.Function):
         x2, weight, rstd = ctx.saved_tensors
         dx = ops.rmsnorm_bwd(dy.reshape(x2.shape), x2, weight, rstd)
         return dx.view(ctx.shape), None, None
+
+
+class AddRMSNormFn(torch.autograd.Function):
+    """``h = residual + delta; y = norm(h)``, both returned (solution/rmsnorm.py:108-144). h is not
+    kept for backward: it is rebuilt from the residual (the layer input, kept by the input norm
+    anyway) and delta (the 16-bit attention output). One sm_100a kernel each way
+    (``decik_add_rmsnorm_fwd/bwd``); y equals RMSNormFn on the same h bit for bit, and the input
+    gradient is grad_h + the norm's gradient, returned to both inputs (fp32, and in delta's dtype)."""
+
+    @staticmethod
+    def forward(ctx, residual, delta, weight, eps):
+        h, y, rstd = ops.add_rmsnorm_fwd(residual, delta, weight, eps)
+        ctx.save_for_backward(residual, delta, weight, rstd)
+        ctx.eps = eps
+        return h, y
+
+    @staticmethod
+    def backward(ctx, grad_h, grad_y):
+        residual, delta, weight, rstd = ctx.saved_tensors
+        if grad_y is None:
+            if grad_h is None:
+                return None, None, None, None
+            return grad_h, grad_h.to(delta.dtype), None, None
+        total, total16 = ops.add_rmsnorm_bwd(grad_y, grad_h, residual, delta, weight, rstd)
+        return total, total16, None, None
+
+
+def fusable(module, x):
+    """The sm_100a kernel can run this Qwen2RMSNorm on x (the patched forward's conditions,
+    solution/rmsnorm.py:147-155)."""
+    weight = getattr(module, "weight", None)
+    return (isinstance(x, torch.Tensor) and on_gpu(x) and x.dtype == torch.float32 and x.numel() > 0
+            and isinstance(weight, torch.Tensor) and on_gpu(weight)
+            and weight.dtype in (torch.float32, torch.float16) and not weight.requires_grad
+            and weight.dim() == 1 and x.shape[-1] == weight.shape[0] and x.shape[-1] <= 8192
+            and x.shape[-1] % 4 == 0 and getattr(type(module).forward, "_skc", False))
 
 
 def patch(norm_cls=None):

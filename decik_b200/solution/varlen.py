@@ -163,10 +163,11 @@ class PackedDropout(torch.autograd.Function):
         return grad * keep * ctx.scale, None, None, None
 
 
-def patch(varlen_attention=True):
-    """Patch Qwen2Model.forward (packing), ALL_ATTENTION_FUNCTIONS["sdpa"] and nn.Dropout
-    (solution/varlen.py:229-359). Inputs the packed path is not for go to the original code;
-    eligible packed attention always runs the sm_100a kernel (no per-row fallback)."""
+def patch(varlen_attention=True, fuse_residual=True):
+    """Patch Qwen2Model.forward (packing), ALL_ATTENTION_FUNCTIONS["sdpa"], Qwen2DecoderLayer.forward
+    (with ``fuse_residual``: the residual add + post-attention norm as one AddRMSNormFn) and
+    nn.Dropout (solution/varlen.py:229-359). Inputs the packed path is not for go to the original
+    code; eligible packed attention always runs the sm_100a kernel (no per-row fallback)."""
     import torch.nn.functional as F
     from transformers.modeling_outputs import BaseModelOutputWithPast
     from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
@@ -224,6 +225,46 @@ def patch(varlen_attention=True):
                                 packing.max_len, groups, scaling), None
 
     ALL_ATTENTION_FUNCTIONS["sdpa"] = sdpa_packed
+
+    from . import rmsnorm
+
+    layer_cls = modeling_qwen2.Qwen2DecoderLayer
+    layer_forward = layer_cls.forward
+
+    def decoder_layer(self, hidden_states, attention_mask=None, position_ids=None,
+                      past_key_values=None, use_cache=False, position_embeddings=None, **kwargs):
+        packing = STATE.packing
+        post_norm = getattr(self, "post_attention_layernorm", None)
+        if not (fuse_residual and STATE.packing_active and packing is not None
+                and attention_mask is None and past_key_values is None and not use_cache
+                and isinstance(hidden_states, torch.Tensor) and hidden_states.dim() == 3
+                and hidden_states.shape[0] == 1 and hidden_states.shape[1] == packing.n_tokens
+                and rmsnorm.fusable(post_norm, hidden_states)):
+            return layer_forward(self, hidden_states, attention_mask=attention_mask,
+                                 position_ids=position_ids, past_key_values=past_key_values,
+                                 use_cache=use_cache, position_embeddings=position_embeddings, **kwargs)
+        # Qwen2DecoderLayer.forward with the residual add and the post-attention norm as one node
+        # (solution/varlen.py:323-343): the norm's input is rebuilt in backward from the layer
+        # input and the 16-bit attention output instead of being kept
+        residual = hidden_states
+        hidden_states = self.input_layernorm(hidden_states)
+        attn_out, _ = self.self_attn(hidden_states=hidden_states, attention_mask=attention_mask,
+                                     position_ids=position_ids, past_key_values=past_key_values,
+                                     use_cache=use_cache, position_embeddings=position_embeddings, **kwargs)
+        if (isinstance(attn_out, torch.Tensor) and attn_out.dtype in (torch.float16, torch.bfloat16)
+                and attn_out.shape == residual.shape and attn_out.is_cuda):
+            eps = float(post_norm.variance_epsilon)
+            hidden_states, normed = rmsnorm.AddRMSNormFn.apply(residual, attn_out, post_norm.weight, eps)
+            STATE.norm_link = (normed, (residual, attn_out), post_norm.weight, eps)
+        else:
+            hidden_states = residual + attn_out
+            normed = post_norm(hidden_states)
+        residual = hidden_states
+        hidden_states = self.mlp(normed)
+        return residual + hidden_states
+
+    decoder_layer._skc = True
+    layer_cls.forward = decoder_layer
 
     dropout_forward = torch.nn.Dropout.forward
 

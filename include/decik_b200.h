@@ -219,6 +219,26 @@ DECIK_API int decik_rmsnorm_bwd(const float* dy, const float* x, const void* w, 
                       const float* rstd, float* dx, int64_t n_rows, int n_cols, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * The decoder's residual add + post-attention RMSNorm, one pass each way.
+ * Replaces AddRMSNormFn (solution/rmsnorm.py:108-144) as the patched Qwen2DecoderLayer.forward
+ * calls it (solution/varlen.py:323-337).
+ *   forward:  h = residual + f32(delta) (one fp32 rounding), y = w * (h * rsqrt(mean(h^2) + eps));
+ *             writes h, y (fp32) and rstd [n_rows] (may be NULL).
+ *   backward: h rebuilt from residual and delta (not kept), dx = grad_h + norm_bwd(dy, h) in fp32
+ *             (grad_h may be NULL: dx = norm_bwd), and dx16 = dx in delta's type (may be NULL).
+ * residual, h, y, dy, grad_h, dx: fp32 [n_rows, n_cols] contiguous, 16-byte aligned; delta and
+ * dx16 of delta_dtype (F32, F16 or BF16), 8-byte aligned (16 for F32); w of w_dtype (F32 or F16).
+ * y and the norm gradient equal decik_rmsnorm_fwd / _bwd applied to the same h bit for bit.
+ * n_cols % 4 == 0, <= 8192.
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int decik_add_rmsnorm_fwd(const float* residual, const void* delta, int delta_dtype, const void* w,
+                      int w_dtype, float* h, float* y, float* rstd, int64_t n_rows, int n_cols, float eps,
+                      void* stream);
+DECIK_API int decik_add_rmsnorm_bwd(const float* dy, const float* grad_h, const float* residual,
+                      const void* delta, int delta_dtype, const void* w, int w_dtype, const float* rstd,
+                      float* dx, void* dx16, int64_t n_rows, int n_cols, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Packed (padding-free) varlen causal GQA attention.
  * Replaces VarlenSDPA (solution/varlen.py:134-168), i.e. aten::_efficient_attention_forward /
  * _backward over cu_seqlens with the 6x GQA expansion (_expand_kv, :124-131) and the

@@ -20,6 +20,10 @@ Fixtures written (numpy .npz):
                       dev/test_cpu_sdpa.py:24)
 - lora_golden.npz     solution/attn.py pack_keep, _lora_inputs, LoRAPairFromNorm and
                       solution/rmsnorm.py RMSNormFn (sizes of dev/test_cpu_norm_link.py:32-45)
+- addnorm_golden.npz  solution/rmsnorm.py AddRMSNormFn (the decoder's residual add + post-attention
+                      norm, solution/varlen.py:323-337) forward and backward, fp16 delta
+
+``python tests/golden/make_golden.py <reference> addnorm`` writes only the named fixture files.
 """
 
 from __future__ import annotations
@@ -211,19 +215,37 @@ def lora_fixtures(attn, rmsnorm) -> dict:
                 eps=np.float32(eps), **norm)
 
 
-def main(reference: str) -> None:
+def addnorm_fixtures(rmsnorm) -> dict:
+    torch.manual_seed(0)
+    T, H = 29, 256
+    eps = 1e-6
+    residual = (torch.randn(1, T, H) * 3).requires_grad_(True)
+    delta = (torch.randn(1, T, H) * 2).half().requires_grad_(True)  # the fp16 attention output
+    w = torch.rand(H) + 0.5
+    grad_h = torch.randn(1, T, H)
+    grad_y = torch.randn(1, T, H)
+    h, y = rmsnorm.AddRMSNormFn.apply(residual, delta, w, eps)
+    torch.autograd.backward([h, y], [grad_h, grad_y])
+    return dict(residual=residual.detach().numpy(), delta=delta.detach().numpy(), w=w.numpy(),
+                grad_h=grad_h.numpy(), grad_y=grad_y.numpy(), h=h.detach().numpy(), y=y.detach().numpy(),
+                d_residual=residual.grad.numpy(), d_delta=delta.grad.numpy(), eps=np.float32(eps))
+
+
+def main(reference: str, only=None) -> None:
     sys.path.insert(0, reference)
     import solution._state as st
     from solution import attn, nf4, rmsnorm, varlen
 
     for m in (st, attn, nf4, rmsnorm, varlen):
         m.on_gpu = lambda t: True
-    np.savez_compressed(os.path.join(HERE, "nf4_golden.npz"), **nf4_fixtures(nf4))
-    np.savez_compressed(os.path.join(HERE, "rope_golden.npz"), **rope_fixtures(attn))
-    np.savez_compressed(os.path.join(HERE, "sdpa_golden.npz"), **sdpa_fixtures(varlen))
-    np.savez_compressed(os.path.join(HERE, "lora_golden.npz"), **lora_fixtures(attn, rmsnorm))
+    makers = {"nf4": lambda: nf4_fixtures(nf4), "rope": lambda: rope_fixtures(attn),
+              "sdpa": lambda: sdpa_fixtures(varlen), "lora": lambda: lora_fixtures(attn, rmsnorm),
+              "addnorm": lambda: addnorm_fixtures(rmsnorm)}
+    for name, make in makers.items():
+        if only is None or name in only:
+            np.savez_compressed(os.path.join(HERE, f"{name}_golden.npz"), **make())
     print("fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "../reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else "../reference", sys.argv[2:] or None)

@@ -18,6 +18,7 @@ def patched_classes():
     from transformers.models.qwen2 import modeling_qwen2 as mq
 
     saved = [(mq.Qwen2Model, "forward", mq.Qwen2Model.forward),
+             (mq.Qwen2DecoderLayer, "forward", mq.Qwen2DecoderLayer.forward),
              (mq.Qwen2Attention, "forward", mq.Qwen2Attention.forward),
              (mq.Qwen2RMSNorm, "forward", mq.Qwen2RMSNorm.forward),
              (torch.nn.Dropout, "forward", torch.nn.Dropout.forward),

@@ -219,6 +219,68 @@ def test_rmsnorm_vs_oracle(cuda_lib):
     assert torch.equal(y, y2)  # the recompute is bit-identical
 
 
+def test_add_rmsnorm_golden(cuda_lib):
+    """The fused residual add + norm against the reference's AddRMSNormFn fixture (fp16 delta):
+    h bit-exact, y and the input gradients within fp32 rounding, the fp16 gradient within one ulp."""
+    ops = _ops()
+    g = golden("addnorm_golden.npz")
+    eps = float(g["eps"])
+    r = torch.from_numpy(g["residual"][0]).to(DEV)
+    d = torch.from_numpy(g["delta"][0]).to(DEV)
+    w = torch.from_numpy(g["w"]).to(DEV)
+    h, y, rstd = ops.add_rmsnorm_fwd(r, d, w, eps)
+    assert np.array_equal(h.cpu().numpy(), g["h"][0])
+    np.testing.assert_allclose(y.cpu().numpy(), g["y"][0], rtol=1e-5, atol=1e-5)
+    dx, dx16 = ops.add_rmsnorm_bwd(torch.from_numpy(g["grad_y"][0]).to(DEV), torch.from_numpy(g["grad_h"][0]).to(DEV),
+                                   r, d, w, rstd)
+    np.testing.assert_allclose(dx.cpu().numpy(), g["d_residual"][0], rtol=1e-4, atol=1e-5)
+    ref16 = g["d_delta"][0].astype(np.float32)
+    ulp = np.spacing(np.abs(g["d_delta"][0])).astype(np.float32)
+    assert dx16.dtype == torch.float16 and np.all(np.abs(dx16.cpu().float().numpy() - ref16) <= ulp)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 256), (37, 1536), (1000, 1536), (5, 8192)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_add_rmsnorm_equals_unfused_kernels(cuda_lib, rows, cols, dtype):
+    """One pass each way equals the composition it replaces bit for bit: torch's fp32 + 16-bit add,
+    decik_rmsnorm_fwd on h, decik_rmsnorm_bwd plus grad_h, and the cast of the sum; also without
+    grad_h, and within tolerance of the fp64 oracle."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(rows + cols)
+    r = (torch.randn(rows, cols, generator=g) * 3).to(DEV)
+    d = (torch.randn(rows, cols, generator=g) * 2).to(dtype).to(DEV)
+    w = (torch.rand(cols, generator=g) + 0.5).to(DEV)
+    dy = torch.randn(rows, cols, generator=g).to(DEV)
+    gh = torch.randn(rows, cols, generator=g).to(DEV)
+    eps = 1e-6
+    h, y, rstd = ops.add_rmsnorm_fwd(r, d, w, eps)
+    h_ref = r + d.float()
+    assert torch.equal(h, h_ref)
+    y_ref, rstd_ref = ops.rmsnorm_fwd(h_ref, w, eps)
+    assert torch.equal(y, y_ref) and torch.equal(rstd, rstd_ref)
+    dx, dx16 = ops.add_rmsnorm_bwd(dy, gh, r, d, w, rstd)
+    dx_ref = gh + ops.rmsnorm_bwd(dy, h_ref, w, rstd_ref)
+    assert torch.equal(dx, dx_ref)
+    assert dx16.dtype == dtype and torch.equal(dx16, dx_ref.to(dtype))
+    dx_n, _ = ops.add_rmsnorm_bwd(dy, None, r, d, w, rstd, want_dx16=False)
+    assert torch.equal(dx_n, ops.rmsnorm_bwd(dy, h_ref, w, rstd_ref))
+    yo, _ = o_norm.forward(h_ref.cpu().numpy(), w.cpu().numpy(), eps)
+    np.testing.assert_allclose(y.cpu().numpy(), yo, rtol=1e-5, atol=1e-5)
+    tot, _ = o_norm.add_backward(gh.cpu().numpy(), dy.cpu().numpy(), r.cpu().numpy(), d.cpu().float().numpy(),
+                                 w.cpu().numpy(), eps)
+    np.testing.assert_allclose(dx.cpu().numpy(), tot, rtol=1e-4, atol=1e-4)
+
+
+def test_add_rmsnorm_rejects_bad_arguments(cuda_lib):
+    ops = _ops()
+    r = torch.randn(4, 6, device=DEV)
+    with pytest.raises(RuntimeError, match="n_cols"):
+        ops.add_rmsnorm_fwd(r, r.half(), torch.ones(6, device=DEV), 1e-6)
+    with pytest.raises(RuntimeError, match="same shape"):
+        ops.add_rmsnorm_fwd(torch.randn(4, 8, device=DEV), torch.randn(4, 4, device=DEV).half(),
+                            torch.ones(8, device=DEV), 1e-6)
+
+
 # ---------------------------------------------------------------------------------------- attention
 def _attn_case(lengths, HQ, HK, dtype, seed=0, layout="token"):
     torch.manual_seed(seed)

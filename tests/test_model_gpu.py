@@ -82,6 +82,7 @@ def patched_classes():
     from transformers.models.qwen2 import modeling_qwen2 as mq
 
     saved = [(mq.Qwen2Model, "forward", mq.Qwen2Model.forward),
+             (mq.Qwen2DecoderLayer, "forward", mq.Qwen2DecoderLayer.forward),
              (mq.Qwen2Attention, "forward", mq.Qwen2Attention.forward),
              (mq.Qwen2RMSNorm, "forward", mq.Qwen2RMSNorm.forward),
              (torch.nn.Dropout, "forward", torch.nn.Dropout.forward),
@@ -99,7 +100,7 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     """With LoRA dropout the packed path draws its keep-masks with the base's op on the base's
     [B, S, H] shape (solution/varlen.py:42-63), so the same seed gives the same masks."""
     from decik_b200 import solution
-    from decik_b200.solution import _state, attn, varlen
+    from decik_b200.solution import _state, attn, rmsnorm, varlen
 
     dtype = torch.bfloat16
     base = _model("cuda", dtype, lora_dropout)
@@ -110,7 +111,7 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     model = _model("cuda", dtype, lora_dropout)    # same seeds: identical weights
     solution.apply(linear4bit_cls=Linear4bit, lora_classes=(LoraLayer,))
     fns = (("rope", attn.FusedQKRope), ("varlen", varlen.VarlenSDPA), ("pair", attn.LoRAPairFromNorm),
-           ("fused", attn.FusedAttentionBlock))
+           ("fused", attn.FusedAttentionBlock), ("addnorm", rmsnorm.AddRMSNormFn))
     calls = {n: 0 for n, _ in fns}
     orig = {n: getattr(c, "forward") for n, c in fns}
 
@@ -131,7 +132,8 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     n_layers = len(model.model.layers)
     # without LoRA dropout every layer runs as one fused node; with it, the reference's chain
     chain = n_layers if lora_dropout > 0 else 0
-    assert calls == {"rope": chain, "varlen": chain, "pair": chain, "fused": n_layers - chain}, calls
+    assert calls == {"rope": chain, "varlen": chain, "pair": chain, "fused": n_layers - chain,
+                     "addnorm": n_layers}, calls
     print(f"loss {l0.item():.6f} -> {l1.item():.6f}")
     assert abs(l1.item() - l0.item()) / abs(l0.item()) < 2e-3, (l1.item(), l0.item())
     assert set(g1) == set(g0)

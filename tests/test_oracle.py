@@ -162,3 +162,20 @@ def test_packing_plan():
     empty = mask.copy()
     empty[3, 0] = 0                             # an empty row
     assert packing.plan(empty) is None
+
+
+def test_add_rmsnorm_oracle_matches_reference_fixture():
+    """oracle.rmsnorm.add_forward / add_backward against the reference's AddRMSNormFn
+    (solution/rmsnorm.py:108-144, run by tests/golden/make_golden.py): h bit-exact, y and the input
+    gradients within fp32 rounding of the reference's Triton kernels."""
+    g = golden("addnorm_golden.npz")
+    eps = float(g["eps"])
+    h, y, _ = rmsnorm.add_forward(g["residual"], g["delta"], g["w"], eps)
+    assert np.array_equal(h, g["h"])
+    assert np.abs(y - g["y"]).max() <= 1e-5 * max(1.0, np.abs(g["y"]).max())
+    total, total16 = rmsnorm.add_backward(g["grad_h"], g["grad_y"], g["residual"], g["delta"], g["w"], eps)
+    assert np.abs(total - g["d_residual"]).max() <= 1e-4 * max(1.0, np.abs(g["d_residual"]).max())
+    assert total16.dtype == np.float16
+    ref16 = g["d_delta"].astype(np.float32)
+    # one fp16 ulp at most (the fp32 sums differ by rounding before the cast)
+    assert np.all(np.abs(total16.astype(np.float32) - ref16) <= np.spacing(np.abs(ref16).astype(np.float16)).astype(np.float32))
