@@ -235,6 +235,34 @@ def add_rmsnorm_bwd(dy, grad_h, residual, delta, w, rstd, want_dx16: bool = True
     return dx.view(residual.shape), None if dx16 is None else dx16.view(delta.shape)
 
 
+def swiglu_fwd(gu: torch.Tensor, inter: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(gate) * up of gu = [gate | up] ([T, 2 * inter], 16-bit, rows 16-byte aligned) -> [T, inter]."""
+    _cuda(gu)
+    if gu.dim() != 2 or gu.stride(1) != 1 or gu.shape[1] < 2 * inter:
+        raise RuntimeError("decik_b200 swiglu_fwd: gu must be [T, >= 2 * inter] with unit column stride")
+    if out is None:
+        out = torch.empty((gu.shape[0], inter), dtype=gu.dtype, device=gu.device)
+    with _timed("swiglu_fwd", 1):
+        rc = _lib.lib().decik_swiglu_fwd(_p(gu), gu.stride(0), _p(out), out.stride(0), gu.shape[0], inter, _dt(gu),
+                                         _stream(gu))
+    _lib.check(rc, "swiglu_fwd")
+    return out
+
+
+def swiglu_bwd(grad: torch.Tensor, gu: torch.Tensor, inter: int, dgu: torch.Tensor | None = None) -> torch.Tensor:
+    """[dgate | dup] ([T, 2 * inter], laid out like gu) from grad [T, inter] and gu."""
+    _cuda(grad, gu)
+    if grad.stride(1) != 1:
+        grad = grad.contiguous()
+    if dgu is None:
+        dgu = torch.empty((gu.shape[0], 2 * inter), dtype=gu.dtype, device=gu.device)
+    with _timed("swiglu_bwd", 1):
+        rc = _lib.lib().decik_swiglu_bwd(_p(grad), grad.stride(0), _p(gu), gu.stride(0), _p(dgu), dgu.stride(0),
+                                         gu.shape[0], inter, _dt(gu), _stream(gu))
+    _lib.check(rc, "swiglu_bwd")
+    return dgu
+
+
 # ------------------------------------------------------------------------------------------------
 # varlen attention
 # ------------------------------------------------------------------------------------------------

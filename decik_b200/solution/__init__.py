@@ -4,12 +4,13 @@
 ``SKC_<NAME>=0`` switches:
 - ``SKC_NF4``         bitsandbytes Linear4bit forward -> sm_100a NF4 dequant + linear (nf4.py)
 - ``SKC_RMSNORM``     Qwen2RMSNorm -> sm_100a RMSNorm, recorded as the LoRA input link (rmsnorm.py)
+- ``SKC_MLP``         Qwen2MLP with NF4 gate/up/down -> one node: one gate|up GEMM, sm_100a SwiGLU (mlp.py)
 - ``SKC_VARLEN``      padding-free decoder + varlen attention (varlen.py); ``SKC_VARLEN_ATTN``;
                       ``SKC_ADDNORM`` (residual add + post-attention norm as one node)
 - ``SKC_ATTN``        Qwen2Attention forward: LoRA + RoPE + varlen attention (attn.py);
                       ``SKC_LORA_RECOMPUTE``; ``SKC_FUSED_BLOCK`` (this build's addition: LoRA
                       without dropout runs as one fused projection + attention node)
-The reference's MLP, head, embedding and warm-up patches are outside this build's scope.
+The reference's head, embedding and warm-up patches are outside this build's scope.
 Patches whose third-party library is not installed (bitsandbytes, peft) are skipped with a
 warning; an eligible input never falls back to a CPU or per-row path.
 """
@@ -23,7 +24,7 @@ def _enabled(name):
 
 
 def apply(linear4bit_cls=None, lora_classes=None):
-    from . import attn, nf4, rmsnorm, varlen
+    from . import attn, mlp, nf4, rmsnorm, varlen
 
     def _try(fn, what, *args, **kw):
         try:
@@ -35,6 +36,8 @@ def apply(linear4bit_cls=None, lora_classes=None):
         _try(nf4.patch, "Linear4bit", linear4bit_cls)
     if _enabled("RMSNORM"):
         _try(rmsnorm.patch, "Qwen2RMSNorm")
+    if _enabled("MLP"):
+        _try(mlp.patch, "Qwen2MLP", linear4bit_cls)
     if _enabled("VARLEN"):
         _try(varlen.patch, "Qwen2Model", varlen_attention=_enabled("VARLEN_ATTN"),
              fuse_residual=_enabled("ADDNORM"))

@@ -1,0 +1,113 @@
+"""Qwen2 MLP with NF4 gate / up / down as one autograd node on the B200 kernels (solution/mlp.py).
+
+The reference (solution/mlp.py:62-163, ``RecomputedMLP``) feeds the three NF4 projections a 16-bit
+input and keeps gate and up in 16 bits, since their values are exactly 16-bit matmul outputs. It
+runs SwiGLU, returns the 16-bit output, and recomputes gate and up in backward to save memory.
+The bitsandbytes base path it replaces casts every projection's output back to the fp32 input
+dtype and runs SwiGLU in fp32.
+
+Here, with 180 GB of HBM per GPU, the node:
+- dequantises W_gate, W_up (into one [2 * inter, hidden] matrix) and W_down in one launch;
+- computes gate | up as ONE GEMM;
+- runs SwiGLU on the sm_100a kernel (``decik_swiglu_fwd``), fp32 arithmetic rounded once;
+- keeps the dequantised weights and gate | up for the backward: no recompute, no second dequant;
+- computes the input gradient as one GEMM over [dgate | dup] with fp32 output. That sums the two
+  projections' input gradients in fp32 inside the GEMM, where the reference casts each to fp32
+  and adds.
+
+The output is in the projections' compute dtype, as the reference's node returns fp16.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .. import ops
+from ._state import on_gpu
+from .nf4 import dequantize_nf4_many, supported
+
+
+class FusedMLP(torch.autograd.Function):
+    """down(silu(gate(x)) * up(x)) with frozen dequantised weights: ``w_gu`` [2 * inter, hidden]
+    (W_gate rows then W_up rows) and ``w_down`` [hidden, inter] in the compute dtype; optional
+    frozen biases ``b_gu`` / ``b_down``. Gradient only for x (returned in x's dtype)."""
+
+    @staticmethod
+    def forward(ctx, x, w_gu, w_down, b_gu, b_down):
+        inter = w_down.shape[1]
+        shape = x.shape
+        x16 = x.reshape(-1, shape[-1]).to(w_gu.dtype)
+        gu = F.linear(x16, w_gu, b_gu)                     # [T, 2 * inter]
+        hidden = ops.swiglu_fwd(gu, inter)                 # [T, inter]
+        out = F.linear(hidden, w_down, b_down)             # [T, hidden]
+        ctx.save_for_backward(gu, w_gu, w_down)
+        ctx.in_dtype, ctx.shape, ctx.inter = x.dtype, shape, inter
+        return out.view(*shape[:-1], out.shape[-1])
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        gu, w_gu, w_down = ctx.saved_tensors
+        g16 = grad_out.reshape(-1, grad_out.shape[-1]).to(w_down.dtype)
+        grad_hidden = torch.mm(g16, w_down)                # [T, inter]
+        dgu = ops.swiglu_bwd(grad_hidden, gu, ctx.inter)   # [T, 2 * inter] = [dgate | dup]
+        dx = torch.mm(dgu, w_gu, out_dtype=torch.float32)  # both input gradients summed in fp32
+        return dx.to(ctx.in_dtype).view(ctx.shape), None, None, None, None
+
+
+def mlp_weights(gate_proj, up_proj, down_proj, dtype):
+    """(w_gu, w_down, b_gu, b_down): this step's dequantised weights, one dequant launch."""
+    gq, uq, dq = (p.weight.quant_state for p in (gate_proj, up_proj, down_proj))
+    inter, hidden = gq.shape
+    dev = gate_proj.weight.device
+    w_gu = torch.empty((2 * inter, hidden), dtype=dtype, device=dev)
+    w_down = torch.empty(tuple(dq.shape), dtype=dtype, device=dev)
+    dequantize_nf4_many([(gate_proj.weight.data, gq, w_gu[:inter]), (up_proj.weight.data, uq, w_gu[inter:]),
+                         (down_proj.weight.data, dq, w_down)], dtype)
+    b_gu = None
+    if gate_proj.bias is not None or up_proj.bias is not None:
+        zeros = torch.zeros(inter, device=dev)
+        b_gu = torch.cat([zeros if p.bias is None else p.bias.float() for p in (gate_proj, up_proj)]).to(dtype)
+    b_down = None if down_proj.bias is None else down_proj.bias.to(dtype)
+    return w_gu, w_down, b_gu, b_down
+
+
+def patch(linear4bit_cls=None):
+    """Patch Qwen2MLP.forward (solution/mlp.py:113-163). Eligible: an input on the GPU, the silu
+    activation, and three NF4 Linear4bit projections with one 16-bit compute dtype, frozen
+    weights and biases. Anything else runs the original forward."""
+    from transformers.models.qwen2 import modeling_qwen2
+
+    if linear4bit_cls is None:
+        import bitsandbytes as bnb
+        linear4bit_cls = bnb.nn.Linear4bit
+    cls = modeling_qwen2.Qwen2MLP
+    if getattr(cls.forward, "_skc", False):
+        return
+    original = cls.forward
+
+    def nf4_projection(module, n_in, dtype):
+        weight = getattr(module, "weight", None)
+        bias = getattr(module, "bias", None)
+        return (isinstance(module, linear4bit_cls) and getattr(module, "compute_dtype", None) == dtype
+                and weight is not None and on_gpu(weight) and weight.dtype == torch.uint8
+                and not weight.requires_grad and (bias is None or not bias.requires_grad)
+                and supported(getattr(weight, "quant_state", None), n_in))
+
+    def forward(self, x):
+        config = getattr(self, "config", None)
+        gate, up, down = (getattr(self, n, None) for n in ("gate_proj", "up_proj", "down_proj"))
+        dtype = getattr(gate, "compute_dtype", None)
+        if not (isinstance(x, torch.Tensor) and on_gpu(x) and x.numel() > 0
+                and x.dtype in (torch.float32, torch.float16, torch.bfloat16)
+                and getattr(config, "hidden_act", None) == "silu" and dtype in (torch.float16, torch.bfloat16)
+                and nf4_projection(gate, x.shape[-1], dtype) and nf4_projection(up, x.shape[-1], dtype)
+                and gate.weight.quant_state.shape == up.weight.quant_state.shape
+                and nf4_projection(down, gate.weight.quant_state.shape[0], dtype)
+                and gate.weight.quant_state.shape[0] % 8 == 0):
+            return original(self, x)
+        w_gu, w_down, b_gu, b_down = mlp_weights(gate, up, down, dtype)
+        return FusedMLP.apply(x, w_gu, w_down, b_gu, b_down)
+
+    forward._skc = True
+    cls.forward = forward

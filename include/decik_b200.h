@@ -239,6 +239,20 @@ DECIK_API int decik_add_rmsnorm_bwd(const float* dy, const float* grad_h, const 
                       float* dx, void* dx16, int64_t n_rows, int n_cols, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * SwiGLU of the Qwen2 MLP, for the fused MLP node.
+ * Replaces the SwiGLU of RecomputedMLP (solution/mlp.py:36-59, kernels solution/swiglu.py:15-37):
+ * gu = [gate | up] is one [n_rows, 2*inter] projection output (row stride ld) in dtype (F16/BF16);
+ *   forward:  out[r, c] = g * sigmoid(g) * u in fp32, rounded to dtype (row stride ldo)
+ *   backward: dup = grad * g * s, dgate = grad * u * s * (1 + g (1 - s)), s = sigmoid(g), written
+ *             as dgu = [dgate | dup] laid out like gu (row stride ldd); grad row stride ldg.
+ * inter % 8 == 0; every row start 16-byte aligned.
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int decik_swiglu_fwd(const void* gu, int64_t ld, void* out, int64_t ldo, int64_t n_rows, int inter,
+                      int dtype, void* stream);
+DECIK_API int decik_swiglu_bwd(const void* grad, int64_t ldg, const void* gu, int64_t ld, void* dgu, int64_t ldd,
+                      int64_t n_rows, int inter, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Packed (padding-free) varlen causal GQA attention.
  * Replaces VarlenSDPA (solution/varlen.py:134-168), i.e. aten::_efficient_attention_forward /
  * _backward over cu_seqlens with the 6x GQA expansion (_expand_kv, :124-131) and the

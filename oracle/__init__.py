@@ -11,7 +11,10 @@ and block compositions), the reference's algorithm for the hot path:
                        dev/test_cpu_attn.py:21-24);
 - ``oracle.lora``      keep-mask packing, masked LoRA inputs, LoRA input gradient
                        (solution/attn.py:130-180) and the LoRA pair math (solution/attn.py:206-273);
-- ``oracle.rmsnorm``   Qwen2RMSNorm (solution/rmsnorm.py:17-45);
+- ``oracle.rmsnorm``   Qwen2RMSNorm (solution/rmsnorm.py:17-45) and the residual add + norm
+                       (AddRMSNormFn, :108-144);
+- ``oracle.mlp``       the MLP with NF4 gate / up / down and SwiGLU (solution/mlp.py:62-110,
+                       solution/swiglu.py:15-37), fp16 rounding points;
 - ``oracle.packing``   padding-free packing plan (solution/varlen.py:23-40, :191-226);
 - ``oracle.attention`` per-row causal GQA attention, forward (out, logsumexp) and backward
                        (solution/varlen.py:76-121, PackedSDPA);

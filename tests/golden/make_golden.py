@@ -20,6 +20,8 @@ Fixtures written (numpy .npz):
                       dev/test_cpu_sdpa.py:24)
 - lora_golden.npz     solution/attn.py pack_keep, _lora_inputs, LoRAPairFromNorm and
                       solution/rmsnorm.py RMSNormFn (sizes of dev/test_cpu_norm_link.py:32-45)
+- mlp_golden.npz      solution/swiglu.py SwiGLU kernels (fp16) and solution/mlp.py RecomputedMLP
+                      forward and backward over three NF4 projections (fp32 input, fp16 compute)
 - addnorm_golden.npz  solution/rmsnorm.py AddRMSNormFn (the decoder's residual add + post-attention
                       norm, solution/varlen.py:323-337) forward and backward, fp16 delta
 
@@ -231,16 +233,55 @@ def addnorm_fixtures(rmsnorm) -> dict:
                 d_residual=residual.grad.numpy(), d_delta=delta.grad.numpy(), eps=np.float32(eps))
 
 
+class _Proj(torch.nn.Module):
+    """The fields of a bitsandbytes Linear4bit that solution/mlp.py reads (weight.quant_state, bias)."""
+
+    def __init__(self, st):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.from_numpy(st["packed"]), requires_grad=False)
+        self.weight.quant_state = _quant_state(st)
+        self.bias = None
+
+
+def mlp_fixtures(mlp) -> dict:
+    from oracle.nf4 import quantize_nf4
+
+    from solution import swiglu
+
+    torch.manual_seed(0)
+    T, H, I = 23, 128, 256
+    gate = (torch.randn(T, I) * 3).half()
+    up = (torch.randn(T, I) * 2).half()
+    grad = torch.randn(T, I).half()
+    hidden = swiglu.SwiGLU.apply(gate, up)
+    dgate, dup = swiglu.SwiGLU.backward(type("Ctx", (), {"saved_tensors": (gate, up)})(), grad)
+    rng = np.random.default_rng(0)
+    states = {n: quantize_nf4((rng.standard_normal(shape) * 0.05).astype(np.float32))
+              for n, shape in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I)))}
+    x = torch.randn(1, T, H).requires_grad_(True)
+    gout = torch.randn(1, T, H).half()
+    out = mlp.RecomputedMLP.apply(x, _Proj(states["gate"]), _Proj(states["up"]), _Proj(states["down"]))
+    out.backward(gout)
+    res = dict(sw_gate=gate.numpy(), sw_up=up.numpy(), sw_grad=grad.numpy(), sw_out=hidden.numpy(),
+               sw_dgate=dgate.numpy(), sw_dup=dup.numpy(), x=x.detach().numpy(), gout=gout.numpy(),
+               out=out.detach().numpy(), dx=x.grad.numpy(), dims=np.array([T, H, I]))
+    for n, st in states.items():
+        for k in ("packed", "absmax", "code", "absmax2", "code2"):
+            res[f"{n}_{k}"] = st[k]
+        res[f"{n}_offset"] = np.float32(st["offset"])
+    return res
+
+
 def main(reference: str, only=None) -> None:
     sys.path.insert(0, reference)
     import solution._state as st
-    from solution import attn, nf4, rmsnorm, varlen
+    from solution import attn, mlp, nf4, rmsnorm, varlen
 
-    for m in (st, attn, nf4, rmsnorm, varlen):
+    for m in (st, attn, mlp, nf4, rmsnorm, varlen):
         m.on_gpu = lambda t: True
     makers = {"nf4": lambda: nf4_fixtures(nf4), "rope": lambda: rope_fixtures(attn),
               "sdpa": lambda: sdpa_fixtures(varlen), "lora": lambda: lora_fixtures(attn, rmsnorm),
-              "addnorm": lambda: addnorm_fixtures(rmsnorm)}
+              "addnorm": lambda: addnorm_fixtures(rmsnorm), "mlp": lambda: mlp_fixtures(mlp)}
     for name, make in makers.items():
         if only is None or name in only:
             np.savez_compressed(os.path.join(HERE, f"{name}_golden.npz"), **make())

@@ -19,6 +19,7 @@ def patched_classes():
 
     saved = [(mq.Qwen2Model, "forward", mq.Qwen2Model.forward),
              (mq.Qwen2DecoderLayer, "forward", mq.Qwen2DecoderLayer.forward),
+             (mq.Qwen2MLP, "forward", mq.Qwen2MLP.forward),
              (mq.Qwen2Attention, "forward", mq.Qwen2Attention.forward),
              (mq.Qwen2RMSNorm, "forward", mq.Qwen2RMSNorm.forward),
              (torch.nn.Dropout, "forward", torch.nn.Dropout.forward),

@@ -29,6 +29,10 @@ def _model(device, dtype, lora_dropout):
         a.k_proj = Linear4bit(a.k_proj, dtype, device)
         a.v_proj = LoraLayer(Linear4bit(a.v_proj, dtype, device), 16, 32, lora_dropout, device)
         a.o_proj = Linear4bit(a.o_proj, dtype, device)
+        m = layer.mlp
+        m.gate_proj = Linear4bit(m.gate_proj, dtype, device)
+        m.up_proj = Linear4bit(m.up_proj, dtype, device)
+        m.down_proj = Linear4bit(m.down_proj, dtype, device)
     for name, p in model.named_parameters():
         p.requires_grad_("lora_" in name)
     model.train()
@@ -83,6 +87,7 @@ def patched_classes():
 
     saved = [(mq.Qwen2Model, "forward", mq.Qwen2Model.forward),
              (mq.Qwen2DecoderLayer, "forward", mq.Qwen2DecoderLayer.forward),
+             (mq.Qwen2MLP, "forward", mq.Qwen2MLP.forward),
              (mq.Qwen2Attention, "forward", mq.Qwen2Attention.forward),
              (mq.Qwen2RMSNorm, "forward", mq.Qwen2RMSNorm.forward),
              (torch.nn.Dropout, "forward", torch.nn.Dropout.forward),
@@ -100,7 +105,7 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     """With LoRA dropout the packed path draws its keep-masks with the base's op on the base's
     [B, S, H] shape (solution/varlen.py:42-63), so the same seed gives the same masks."""
     from decik_b200 import solution
-    from decik_b200.solution import _state, attn, rmsnorm, varlen
+    from decik_b200.solution import _state, attn, mlp, rmsnorm, varlen
 
     dtype = torch.bfloat16
     base = _model("cuda", dtype, lora_dropout)
@@ -111,7 +116,7 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     model = _model("cuda", dtype, lora_dropout)    # same seeds: identical weights
     solution.apply(linear4bit_cls=Linear4bit, lora_classes=(LoraLayer,))
     fns = (("rope", attn.FusedQKRope), ("varlen", varlen.VarlenSDPA), ("pair", attn.LoRAPairFromNorm),
-           ("fused", attn.FusedAttentionBlock), ("addnorm", rmsnorm.AddRMSNormFn))
+           ("fused", attn.FusedAttentionBlock), ("addnorm", rmsnorm.AddRMSNormFn), ("mlp", mlp.FusedMLP))
     calls = {n: 0 for n, _ in fns}
     orig = {n: getattr(c, "forward") for n, c in fns}
 
@@ -133,7 +138,7 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     # without LoRA dropout every layer runs as one fused node; with it, the reference's chain
     chain = n_layers if lora_dropout > 0 else 0
     assert calls == {"rope": chain, "varlen": chain, "pair": chain, "fused": n_layers - chain,
-                     "addnorm": n_layers}, calls
+                     "addnorm": n_layers, "mlp": n_layers}, calls
     print(f"loss {l0.item():.6f} -> {l1.item():.6f}")
     assert abs(l1.item() - l0.item()) / abs(l0.item()) < 2e-3, (l1.item(), l0.item())
     assert set(g1) == set(g0)

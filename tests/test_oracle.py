@@ -179,3 +179,37 @@ def test_add_rmsnorm_oracle_matches_reference_fixture():
     ref16 = g["d_delta"].astype(np.float32)
     # one fp16 ulp at most (the fp32 sums differ by rounding before the cast)
     assert np.all(np.abs(total16.astype(np.float32) - ref16) <= np.spacing(np.abs(ref16).astype(np.float16)).astype(np.float32))
+
+
+def _mlp_states(g):
+    return {n: dict(packed=g[f"{n}_packed"], absmax=g[f"{n}_absmax"], code=g[f"{n}_code"], absmax2=g[f"{n}_absmax2"],
+                    code2=g[f"{n}_code2"], offset=np.float32(g[f"{n}_offset"]), blocksize=64, blocksize2=256,
+                    nested=True, shape=shape)
+            for n, shape in (("gate", (int(g["dims"][2]), int(g["dims"][1]))),
+                             ("up", (int(g["dims"][2]), int(g["dims"][1]))),
+                             ("down", (int(g["dims"][1]), int(g["dims"][2]))))}
+
+
+def _ulps16(a, ref):
+    a = np.asarray(a, dtype=np.float32)
+    ref16 = np.asarray(ref, dtype=np.float16)
+    return np.abs(a - ref16.astype(np.float32)) / np.spacing(np.abs(ref16)).astype(np.float32)
+
+
+def test_mlp_oracle_matches_reference_fixture():
+    """oracle.mlp against the reference's SwiGLU kernels and RecomputedMLP (solution/mlp.py:62-110,
+    solution/swiglu.py:15-37, run by tests/golden/make_golden.py): SwiGLU within one fp16 ulp (the
+    exponential's implementations differ), the whole node within fp16 rounding of its products."""
+    from oracle import mlp
+
+    g = golden("mlp_golden.npz")
+    assert _ulps16(mlp.swiglu_fwd(g["sw_gate"], g["sw_up"]), g["sw_out"]).max() <= 1
+    dgate, dup = mlp.swiglu_bwd(g["sw_grad"], g["sw_gate"], g["sw_up"])
+    assert _ulps16(dgate, g["sw_dgate"]).max() <= 1 and _ulps16(dup, g["sw_dup"]).max() <= 1
+    T, H, _ = (int(v) for v in g["dims"])
+    out, saved = mlp.mlp_forward(g["x"].reshape(T, H), _mlp_states(g))
+    ref = g["out"].reshape(T, H).astype(np.float32)
+    assert np.linalg.norm(out.astype(np.float32) - ref) / np.linalg.norm(ref) < 2e-3
+    dx = mlp.mlp_backward(g["gout"].reshape(T, H), saved)
+    dref = g["dx"].reshape(T, H)
+    assert np.linalg.norm(dx - dref) / np.linalg.norm(dref) < 2e-3
