@@ -57,6 +57,8 @@ SIGNATURES = {
     "decik_swiglu_fwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p]),
     "decik_swiglu_bwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
                                  c_void_p]),
+    "decik_head_stats": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                 c_int, c_int, c_void_p]),
     "decik_varlen_attn_fwd": (c_int, [Tensor3, Tensor3, Tensor3, Tensor3, c_void_p, c_void_p, c_int, c_int,
                                       c_int64, c_int, c_int, c_int, c_float, c_int, c_void_p]),
     "decik_varlen_attn_bwd_workspace": (c_int64, [c_int64, c_int, c_int]),

@@ -7,7 +7,8 @@
 //   backward  dup = grad * g * s, dgate = grad * u * s * (1 + g * (1 - s))
 // (the same expressions and order as the reference). dgate and dup are written into one
 // [T, 2 * inter] buffer laid out like gu, the operand of one dX = dgu . [W_gate; W_up] GEMM.
-// HBM-bound: 8 elements (16 bytes) per thread and step, grid-stride over rows x 8-column groups.
+// HBM-bound: 8 elements (16 bytes) per load, grid-stride over rows x 8-column groups (the forward
+// takes two groups per step so that four loads are in flight per thread).
 #include "common.cuh"
 
 namespace decik {
@@ -35,16 +36,27 @@ __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const T* __restrict__ g
                                                           int64_t ldo, int64_t n_rows, int inter) {
   const int groups = inter / 8;
   const int64_t total = n_rows * groups;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = i / groups;
-    const int c = static_cast<int>(i - row * groups) * 8;
-    float g[8], u[8], o[8];
-    load8<T>(gu + row * ld + c, g);
-    load8<T>(gu + row * ld + inter + c, u);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  // two 8-column groups per step, their four loads issued before any arithmetic
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += 2 * stride) {
+    const int64_t j = i + stride;
+    const bool two = j < total;
+    const int64_t row0 = i / groups, row1 = two ? j / groups : row0;
+    const int c0 = static_cast<int>(i - row0 * groups) * 8;
+    const int c1 = two ? static_cast<int>(j - row1 * groups) * 8 : c0;
+    float g0[8], u0[8], g1[8], u1[8], o[8];
+    load8<T>(gu + row0 * ld + c0, g0);
+    load8<T>(gu + row0 * ld + inter + c0, u0);
+    load8<T>(gu + row1 * ld + c1, g1);
+    load8<T>(gu + row1 * ld + inter + c1, u1);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = g[e] * sigmoidf(g[e]) * u[e];
-    store8<T>(out + row * ldo + c, o);
+    for (int e = 0; e < 8; ++e) o[e] = g0[e] * sigmoidf(g0[e]) * u0[e];
+    store8<T>(out + row0 * ldo + c0, o);
+    if (two) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = g1[e] * sigmoidf(g1[e]) * u1[e];
+      store8<T>(out + row1 * ldo + c1, o);
+    }
   }
 }
 

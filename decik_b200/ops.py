@@ -263,6 +263,24 @@ def swiglu_bwd(grad: torch.Tensor, gu: torch.Tensor, inter: int, dgu: torch.Tens
     return dgu
 
 
+def head_stats(logits: torch.Tensor, target: torch.Tensor):
+    """(lse, entropy, token_loss, hit) of each row of 16-bit logits [rows, vocab]; labelled rows'
+    logits are replaced by softmax - onehot (in place)."""
+    _cuda(logits, target)
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise RuntimeError("decik_b200 head_stats: logits must be [rows, vocab] with unit column stride")
+    n = logits.shape[0]
+    target = target.to(torch.int64).contiguous()
+    f = lambda: torch.empty(n, dtype=torch.float32, device=logits.device)
+    lse, entropy, loss = f(), f(), f()
+    hit = torch.empty(n, dtype=torch.int32, device=logits.device)
+    with _timed("head_stats", 1):
+        rc = _lib.lib().decik_head_stats(_p(logits), logits.stride(0), _p(target), _p(lse), _p(entropy), _p(loss),
+                                         _p(hit), n, logits.shape[1], _dt(logits), _stream(logits))
+    _lib.check(rc, "head_stats")
+    return lse, entropy, loss, hit
+
+
 # ------------------------------------------------------------------------------------------------
 # varlen attention
 # ------------------------------------------------------------------------------------------------

@@ -213,11 +213,13 @@ def padded_batch(lengths, vocab, seed, device):
     return ids.to(device), mask.to(device), labels.to(device)
 
 
-def qlora_train_step(model, ids, mask, labels, dtype=torch.bfloat16, n_labels=None):
+def qlora_train_step(model, ids, mask, labels, dtype=torch.bfloat16, n_labels=None, fused_head=True):
     """Forward (packed path requested) + loss + backward of one step; returns the loss (a device
     scalar). The loss is the summed cross entropy of the real tokens' shifted labels divided by
-    ``n_labels`` (this step's labelled-token count, or the global count under data parallelism:
-    solution/head.py:157-163), so per-rank losses and gradients sum to the one-process values."""
+    ``n_labels``: this step's labelled-token count, or the global count under data parallelism
+    (solution/head.py:157-163). Per-rank losses and gradients then sum to the one-process values.
+    On the GPU with ``fused_head`` the head and loss run chunked through ``solution.head.run_head``
+    (no [tokens x vocab] fp32 logits); otherwise as lm_head + cross_entropy."""
     from .solution._state import STATE
 
     STATE.request, STATE.packing = True, None
@@ -225,19 +227,26 @@ def qlora_train_step(model, ids, mask, labels, dtype=torch.bfloat16, n_labels=No
         with torch.autocast("cuda", dtype=dtype, enabled=ids.is_cuda):
             hidden = model.model(input_ids=ids, attention_mask=mask, use_cache=False).last_hidden_state
             packing = STATE.packing
-            flat = hidden.reshape(-1, hidden.shape[-1])
-            if packing is not None:
-                positions = packing.index
+            if fused_head and ids.is_cuda:
+                from .solution.head import run_head
+
+                if n_labels is None:
+                    n_labels = (F.pad(labels, (0, 1), value=-100)[..., 1:] != -100).sum().float()
+                loss = run_head(model, hidden, labels, mask, n_labels, packing, dtype)
             else:
-                positions = mask.reshape(-1).nonzero().squeeze(1)
-                flat = flat.index_select(0, positions)
-            targets = F.pad(labels, (0, 1), value=-100)[..., 1:].reshape(-1).index_select(0, positions)
-            logits = model.lm_head(flat)
+                flat = hidden.reshape(-1, hidden.shape[-1])
+                if packing is not None:
+                    positions = packing.index
+                else:
+                    positions = mask.reshape(-1).nonzero().squeeze(1)
+                    flat = flat.index_select(0, positions)
+                targets = F.pad(labels, (0, 1), value=-100)[..., 1:].reshape(-1).index_select(0, positions)
+                logits = model.lm_head(flat)
+                if n_labels is None:
+                    n_labels = (targets != -100).sum()
+                loss = F.cross_entropy(logits.float(), targets, ignore_index=-100, reduction="sum") / n_labels
     finally:
         STATE.request, STATE.packing = False, None
-    if n_labels is None:
-        n_labels = (targets != -100).sum()
-    loss = F.cross_entropy(logits.float(), targets, ignore_index=-100, reduction="sum") / n_labels
     loss.backward()
     return loss.detach()
 

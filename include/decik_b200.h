@@ -253,6 +253,17 @@ DECIK_API int decik_swiglu_bwd(const void* grad, int64_t ldg, const void* gu, in
                       int64_t n_rows, int inter, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * LM-head cross entropy over one chunk of logits (the chunked fused head + loss).
+ * Replaces skc_head_stats_kernel (solution/head.py:39-85): per row of logits ([n_rows, n_vocab],
+ * 16-bit of dtype, row stride ld) lse, entropy = lse - sum(p z), token_loss = lse - z[target]
+ * (0 for target < 0, NaN for target >= n_vocab), hit = (argmax == target, first maximal index);
+ * then, for rows with a label, softmax - onehot written over the logits in place (the operand of
+ * the hidden-state gradient matmul). target int64 [n_rows]; n_vocab, ld multiples of 8.
+ * ------------------------------------------------------------------------------------------- */
+DECIK_API int decik_head_stats(void* logits, int64_t ld, const int64_t* target, float* lse, float* entropy,
+                      float* token_loss, int* hit, int64_t n_rows, int n_vocab, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Packed (padding-free) varlen causal GQA attention.
  * Replaces VarlenSDPA (solution/varlen.py:134-168), i.e. aten::_efficient_attention_forward /
  * _backward over cu_seqlens with the 6x GQA expansion (_expand_kv, :124-131) and the

@@ -22,6 +22,8 @@ Fixtures written (numpy .npz):
                       solution/rmsnorm.py RMSNormFn (sizes of dev/test_cpu_norm_link.py:32-45)
 - mlp_golden.npz      solution/swiglu.py SwiGLU kernels (fp16) and solution/mlp.py RecomputedMLP
                       forward and backward over three NF4 projections (fp32 input, fp16 compute)
+- head_golden.npz     solution/head.py FusedHeadLoss (skc_head_stats_kernel + the gradient matmul)
+                      forward and backward, fp16 head, some targets ignored, a tie for the argmax
 - addnorm_golden.npz  solution/rmsnorm.py AddRMSNormFn (the decoder's residual add + post-attention
                       norm, solution/varlen.py:323-337) forward and backward, fp16 delta
 
@@ -272,16 +274,36 @@ def mlp_fixtures(mlp) -> dict:
     return res
 
 
+def head_fixtures(head) -> dict:
+    torch.manual_seed(0)
+    T, H, V = 37, 64, 1000
+    hidden = (torch.randn(T, H) * 2).requires_grad_(True)
+    weight16 = (torch.randn(V, H) * 0.5).half()
+    weight16[7] = weight16[3]  # two identical rows: equal logits, the argmax takes the first
+    targets = torch.randint(0, V, (T,))
+    targets[::5] = -100
+    targets[1] = 3
+    with torch.no_grad():
+        hidden[1] = weight16[3].float() * 4  # rows 3 and 7 tie for the maximum of token 1
+    denominator = torch.tensor(float((targets != -100).sum()))
+    loss, entropy, token_loss, hit = head.FusedHeadLoss.apply(hidden, weight16, targets, denominator)
+    loss.backward()
+    return dict(hidden=hidden.detach().numpy(), weight16=weight16.numpy(), targets=targets.numpy(),
+                denominator=denominator.numpy(), loss=loss.detach().numpy(), entropy=entropy.numpy(),
+                token_loss=token_loss.numpy(), hit=hit.numpy(), dhidden=hidden.grad.numpy())
+
+
 def main(reference: str, only=None) -> None:
     sys.path.insert(0, reference)
     import solution._state as st
-    from solution import attn, mlp, nf4, rmsnorm, varlen
+    from solution import attn, head, mlp, nf4, rmsnorm, varlen
 
-    for m in (st, attn, mlp, nf4, rmsnorm, varlen):
+    for m in (st, attn, head, mlp, nf4, rmsnorm, varlen):
         m.on_gpu = lambda t: True
     makers = {"nf4": lambda: nf4_fixtures(nf4), "rope": lambda: rope_fixtures(attn),
               "sdpa": lambda: sdpa_fixtures(varlen), "lora": lambda: lora_fixtures(attn, rmsnorm),
-              "addnorm": lambda: addnorm_fixtures(rmsnorm), "mlp": lambda: mlp_fixtures(mlp)}
+              "addnorm": lambda: addnorm_fixtures(rmsnorm), "mlp": lambda: mlp_fixtures(mlp),
+              "head": lambda: head_fixtures(head)}
     for name, make in makers.items():
         if only is None or name in only:
             np.savez_compressed(os.path.join(HERE, f"{name}_golden.npz"), **make())

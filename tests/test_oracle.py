@@ -213,3 +213,18 @@ def test_mlp_oracle_matches_reference_fixture():
     dx = mlp.mlp_backward(g["gout"].reshape(T, H), saved)
     dref = g["dx"].reshape(T, H)
     assert np.linalg.norm(dx - dref) / np.linalg.norm(dref) < 2e-3
+
+
+def test_head_oracle_matches_reference_fixture():
+    """oracle.head against the reference's FusedHeadLoss (solution/head.py:88-139): loss, entropy
+    and per-token loss within fp32 rounding, the argmax hits equal (with a tie resolved to the first
+    index), the hidden-state gradient within the fp16 rounding of its products."""
+    from oracle import head
+
+    g = golden("head_golden.npz")
+    loss, entropy, token_loss, hit, dh = head.head_loss(g["hidden"], g["weight16"], g["targets"], g["denominator"])
+    assert abs(loss - float(g["loss"])) <= 1e-4 * abs(float(g["loss"]))
+    np.testing.assert_allclose(entropy, g["entropy"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(token_loss, g["token_loss"], rtol=1e-4, atol=1e-4)
+    assert np.array_equal(hit, g["hit"]) and hit[1] == 1
+    assert np.linalg.norm(dh - g["dhidden"]) / np.linalg.norm(g["dhidden"]) < 2e-3
