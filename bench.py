@@ -558,11 +558,13 @@ def run_full_step(args, world, rank, local):
     if args.profile and world == 1:  # one GPU only: a step would all-reduce with ranks that have left
         from torch.profiler import ProfilerActivity, profile
 
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
             step(ids, mask, labels)
             torch.cuda.synchronize()
-        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=60),
-              file=sys.stderr, flush=True)
+        avg = prof.key_averages()
+        print(avg.table(sort_by="self_cuda_time_total", row_limit=30, max_name_column_width=60), file=sys.stderr)
+        print(avg.table(sort_by="self_cpu_time_total", row_limit=40, max_name_column_width=60), file=sys.stderr,
+              flush=True)
 
 
 def run_reference_full(args, world, rank):
@@ -638,7 +640,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="full-step workloads, one GPU: after the JSON line, one more step under torch.profiler; "
-                         "its device-time table goes to stderr")
+                         "its device-time and host-time tables go to stderr")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(FULL_STEP), default="config3",
                     help="config3: the 1.5B block over 16,384 tokens (default); config4: the 7B block over "
                          "131,072; config2 / config5: the full 28-layer QLoRA train step over ~830 / "
