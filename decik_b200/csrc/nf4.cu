@@ -57,6 +57,8 @@ struct Nf4Args {
   int64_t n_bytes;
   int blocksize;
   int blocksize2;
+  int bs_shift;   // log2(blocksize) when both block sizes are powers of two (the POW2 kernels)
+  int bs2_shift;  // log2(blocksize2)
 };
 
 // Up to kMaxJobs weights in one launch: grid y = job. All of a launch's jobs share the template
@@ -67,19 +69,27 @@ struct Nf4Batch {
   void* out[kMaxJobs];
 };
 
-template <bool NESTED>
+// Block indices: weight i is in absmax block i / blocksize and that block's absmax2 entry is
+// block / blocksize2. 64-bit divisions by run-time values are long instruction sequences, so the
+// POW2 kernels (both sizes powers of two, as bitsandbytes uses: 64 and 256) shift instead.
+template <bool POW2>
+__device__ __forceinline__ int64_t div_bs(const Nf4Args& a, int64_t i) { return POW2 ? (i >> a.bs_shift) : i / a.blocksize; }
+template <bool POW2>
+__device__ __forceinline__ int64_t div_bs2(const Nf4Args& a, int64_t b) { return POW2 ? (b >> a.bs2_shift) : b / a.blocksize2; }
+
+template <bool NESTED, bool POW2>
 __device__ __forceinline__ float block_scale(const Nf4Args& a, const float* s_code2, float offset,
                                              int64_t block) {
   if (NESTED) {
     const uint8_t q = __ldg(reinterpret_cast<const uint8_t*>(a.absmax) + block);
-    const float s = __fmul_rn(s_code2[q], __ldg(a.absmax2 + block / a.blocksize2));
+    const float s = __fmul_rn(s_code2[q], __ldg(a.absmax2 + div_bs2<POW2>(a, block)));
     return __fadd_rn(s, offset);
   }
   return __ldg(reinterpret_cast<const float*>(a.absmax) + block);
 }
 
 // VEC: 16 bytes per step (needs 16-byte aligned packed and out). Otherwise one byte per step.
-template <typename OutT, bool NESTED, bool VEC>
+template <typename OutT, bool NESTED, bool VEC, bool POW2>
 __global__ void __launch_bounds__(256) nf4_dequant_kernel(const __grid_constant__ Nf4Batch bt) {
   const Nf4Args& a = bt.a[blockIdx.y];
   OutT* __restrict__ out = static_cast<OutT*>(bt.out[blockIdx.y]);
@@ -97,10 +107,10 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const __grid_constant_
       const uint4 raw = ldg16(a.packed + (c << 4));
       const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
       float w[32];
-      const int64_t first = (c << 5) / a.blocksize;         // block of weight 32c
-      const int64_t last = ((c << 5) + 31) / a.blocksize;   // block of weight 32c + 31
+      const int64_t first = div_bs<POW2>(a, c << 5);         // block of weight 32c
+      const int64_t last = div_bs<POW2>(a, (c << 5) + 31);   // block of weight 32c + 31
       if (first == last) {  // the whole chunk in one absmax block (blocksize >= 32)
-        const float scale = block_scale<NESTED>(a, s_code2, offset, first);
+        const float scale = block_scale<NESTED, POW2>(a, s_code2, offset, first);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const uint32_t b = (words[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
@@ -110,8 +120,8 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const __grid_constant_
       } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int64_t block = (((c << 4) + j) * 2) / a.blocksize;
-          const float scale = block_scale<NESTED>(a, s_code2, offset, block);
+          const int64_t block = div_bs<POW2>(a, ((c << 4) + j) * 2);
+          const float scale = block_scale<NESTED, POW2>(a, s_code2, offset, block);
           const uint32_t b = (words[j >> 2] >> ((j & 3) * 8)) & 0xFFu;
           w[2 * j] = __fmul_rn(s_code[b >> 4], scale);
           w[2 * j + 1] = __fmul_rn(s_code[b & 15u], scale);
@@ -123,14 +133,14 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const __grid_constant_
     const int64_t tail0 = n_chunks << 4;
     for (int64_t i = tail0 + tid; i < a.n_bytes; i += stride) {
       const uint32_t b = a.packed[i];
-      const float scale = block_scale<NESTED>(a, s_code2, offset, (i * 2) / a.blocksize);
+      const float scale = block_scale<NESTED, POW2>(a, s_code2, offset, div_bs<POW2>(a, i * 2));
       out[2 * i] = cvt_out<OutT>(__fmul_rn(s_code[b >> 4], scale));
       out[2 * i + 1] = cvt_out<OutT>(__fmul_rn(s_code[b & 15u], scale));
     }
   } else {
     for (int64_t i = tid; i < a.n_bytes; i += stride) {
       const uint32_t b = a.packed[i];
-      const float scale = block_scale<NESTED>(a, s_code2, offset, (i * 2) / a.blocksize);
+      const float scale = block_scale<NESTED, POW2>(a, s_code2, offset, div_bs<POW2>(a, i * 2));
       out[2 * i] = cvt_out<OutT>(__fmul_rn(s_code[b >> 4], scale));
       out[2 * i + 1] = cvt_out<OutT>(__fmul_rn(s_code[b & 15u], scale));
     }
@@ -144,14 +154,34 @@ int launch(const Nf4Batch& bt, int n, bool nested, bool vec, cudaStream_t stream
   const int64_t want = (work + 255) / 256;
   const int64_t cap = std::max<int64_t>(1, static_cast<int64_t>(sm_count()) * 8 / n);
   const dim3 grid(static_cast<unsigned>(want < cap ? (want > 0 ? want : 1) : cap), static_cast<unsigned>(n));
+  bool pow2 = true;
+  for (int j = 0; j < n; ++j) pow2 = pow2 && bt.a[j].bs_shift >= 0 && (!nested || bt.a[j].bs2_shift >= 0);
   if (nested) {
-    if (vec) nf4_dequant_kernel<OutT, true, true><<<grid, 256, 0, stream>>>(bt);
-    else nf4_dequant_kernel<OutT, true, false><<<grid, 256, 0, stream>>>(bt);
+    if (vec) {
+      if (pow2) nf4_dequant_kernel<OutT, true, true, true><<<grid, 256, 0, stream>>>(bt);
+      else nf4_dequant_kernel<OutT, true, true, false><<<grid, 256, 0, stream>>>(bt);
+    } else {
+      if (pow2) nf4_dequant_kernel<OutT, true, false, true><<<grid, 256, 0, stream>>>(bt);
+      else nf4_dequant_kernel<OutT, true, false, false><<<grid, 256, 0, stream>>>(bt);
+    }
   } else {
-    if (vec) nf4_dequant_kernel<OutT, false, true><<<grid, 256, 0, stream>>>(bt);
-    else nf4_dequant_kernel<OutT, false, false><<<grid, 256, 0, stream>>>(bt);
+    if (vec) {
+      if (pow2) nf4_dequant_kernel<OutT, false, true, true><<<grid, 256, 0, stream>>>(bt);
+      else nf4_dequant_kernel<OutT, false, true, false><<<grid, 256, 0, stream>>>(bt);
+    } else {
+      if (pow2) nf4_dequant_kernel<OutT, false, false, true><<<grid, 256, 0, stream>>>(bt);
+      else nf4_dequant_kernel<OutT, false, false, false><<<grid, 256, 0, stream>>>(bt);
+    }
   }
   return check_launch("nf4_dequant");
+}
+
+// log2(v) when v is a power of two, else -1
+int log2_exact(int v) {
+  if (v <= 0 || (v & (v - 1)) != 0) return -1;
+  int k = 0;
+  while ((1 << k) < v) ++k;
+  return k;
 }
 
 int check_job(const decik_nf4_job& j) {
@@ -181,7 +211,7 @@ int run_jobs(const decik_nf4_job* jobs, int n_jobs, int out_dtype, cudaStream_t 
       const decik_nf4_job& jb = jobs[j];
       if (jb.n_bytes == 0 || (jb.nested != 0) != nested || (aligned16(jb.packed) && aligned16(jb.out)) != vec) continue;
       bt.a[n] = Nf4Args{jb.packed, jb.absmax, jb.absmax2, jb.code2, jb.offset, jb.code, jb.n_bytes, jb.blocksize,
-                        jb.blocksize2};
+                        jb.blocksize2, log2_exact(jb.blocksize), nested ? log2_exact(jb.blocksize2) : 0};
       bt.out[n] = jb.out;
       if (++n == kMaxJobs || j == n_jobs - 1) {
         int rc = DECIK_OK;

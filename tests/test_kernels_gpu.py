@@ -69,7 +69,8 @@ def test_nf4_reference_shapes_hash(cuda_lib, i):
 
 @pytest.mark.parametrize("shape,nested,bs", [((1536, 1536), True, 64), ((256, 1536), False, 64),
                                              ((8960, 1536), True, 64), ((96, 64), True, 32),
-                                             ((128, 256), True, 128), ((7, 18), False, 2)])
+                                             ((128, 256), True, 128), ((7, 18), False, 2),
+                                             ((48, 96), True, 96), ((10, 36), False, 6)])
 @pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
 def test_nf4_vs_oracle_bit_exact(cuda_lib, shape, nested, bs, dtype):
     rng = np.random.default_rng(hash((shape, nested, bs)) % 2**32)
