@@ -53,11 +53,15 @@ class FusedAttentionBlock(torch.autograd.Function):
     ``w_cat`` [(Hq+2Hk)*D + 2r, H] holds this step's dequantised W_q, W_k, W_v in its first rows;
     decik_lora_pack writes A_q, A_v (as dt) into the last 2r rows and the lora_B fragments of both
     epilogues in the same launch. The matrix is kept for backward, where the reference dequantises
-    again (solution/nf4.py:99-104)."""
+    again (solution/nf4.py:99-104).
+
+    With ``w_o`` (the dequantised NF4 o_proj weight [H, Hq*D], optional bias ``b_o``) the node
+    also applies o_proj (solution/attn.py:418) and returns [T, H]: the same F.linear the
+    reference's NF4Linear runs, with the weight kept for backward instead of dequantised again."""
 
     @staticmethod
     def forward(ctx, x, a_q, b_q, a_v, b_v, w_cat, bias_cat, cos, sin, cu_seqlens, max_len, n_heads,
-                n_kv, scaling, scale):
+                n_kv, scaling, scale, w_o=None, b_o=None):
         dt = w_cat.dtype
         D = cos.shape[-1]
         r = a_q.shape[0]
@@ -68,14 +72,18 @@ class FusedAttentionBlock(torch.autograd.Function):
         q, k, v, u = ops.qkv_epilogue_fwd(y, y[:, n_proj:], frag, scaling, cos, sin, n_heads, n_kv, want_u=True)
         del y
         out, lse = ops.varlen_attn_fwd(q.transpose(0, 1), k.transpose(0, 1), v, cu_seqlens, max_len, scale)
-        ctx.save_for_backward(x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu_seqlens)
+        ctx.save_for_backward(x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu_seqlens, w_o)
         ctx.meta = (int(max_len), n_heads, n_kv, float(scaling), float(scale), r)
+        if w_o is not None:
+            return F.linear(out.view(out.shape[0], -1), w_o, b_o)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu = ctx.saved_tensors
+        x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu, w_o = ctx.saved_tensors
         max_len, n_heads, n_kv, scaling, scale, r = ctx.meta
+        if w_o is not None:  # through o_proj first: the attention output's gradient
+            grad_out = torch.mm(grad_out.reshape(-1, grad_out.shape[-1]).to(w_o.dtype), w_o).view(out.shape)
         T, D = x16.shape[0], cos.shape[-1]
         n_q, n_kvd = n_heads * D, n_kv * D
         n_proj = n_q + 2 * n_kvd
@@ -91,7 +99,7 @@ class FusedAttentionBlock(torch.autograd.Function):
         db = torch.mm(dy[:, :n_proj].t(), u, out_dtype=torch.float32)
         d_bq = db[:n_q, :r] * scaling
         d_bv = db[n_q + n_kvd:, r:] * scaling
-        return (dx, da[:r], d_bq, da[r:], d_bv) + (None,) * 10
+        return (dx, da[:r], d_bq, da[r:], d_bv) + (None,) * 12
 
 
 def pack_keep(keep_q, keep_v):
@@ -254,10 +262,11 @@ def _nf4_parts(module, n_in, dtype):
     return weight.data, qs, bias
 
 
-def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim):
-    """The attention output [1, T, Hq*D] through FusedAttentionBlock, or None when this layer does not
+def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim, o_nf4=False):
+    """(output, o_proj applied) through FusedAttentionBlock, or None when this layer does not
     qualify: both LoRA branches without dropout, rank 16 and one scaling; q, k, v NF4 linears of the
-    compute dtype; the varlen attention switched on; head_dim 128."""
+    compute dtype; the varlen attention switched on; head_dim 128. With ``o_nf4`` (o_proj is a plain
+    NF4 Linear4bit of the compute dtype) o_proj joins the node: the output is then [1, T, H]."""
     from .nf4 import dequantize_nf4_many
 
     pq, pv = _lora_parts(self.q_proj, q_name), _lora_parts(self.v_proj, v_name)
@@ -280,13 +289,19 @@ def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_k
         items.append((packed, qs, w_cat[r0:r0 + nr]))
         biases.append(bias.float() if bias is not None else torch.zeros(nr, device=x.device))
         r0 += nr
-    dequantize_nf4_many(items, dtype)  # W_q, W_k, W_v into their rows, one launch
+    w_o = b_o = None
+    po = _nf4_parts(self.o_proj, n_heads * head_dim, dtype) if o_nf4 else None
+    if po is not None:
+        w_o = torch.empty(tuple(po[1].shape), dtype=dtype, device=x.device)
+        items.append((po[0], po[1], w_o))
+        b_o = None if po[2] is None else po[2].to(dtype)
+    dequantize_nf4_many(items, dtype)  # W_q, W_k, W_v into their rows (and W_o), one launch
     bias_cat = torch.cat(biases + [torch.zeros(32, device=x.device)]).to(dtype)
     out = FusedAttentionBlock.apply(x.reshape(n_tok, hidden), pq[0], pq[1], pv[0], pv[1], w_cat, bias_cat,
                                     cos.reshape(n_tok, -1), sin.reshape(n_tok, -1),
                                     packing.cu_seqlens(x.device), packing.max_len, n_heads, n_kv, pq[2],
-                                    self.scaling)
-    return out.reshape(1, n_tok, -1)
+                                    self.scaling, w_o, b_o)
+    return out.reshape(1, n_tok, -1), w_o is not None
 
 
 def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None, fused_block=True):
@@ -339,9 +354,11 @@ def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None, fused_blo
         n_kv = self.config.num_key_value_heads
         x = hidden_states
         if fused_block:
-            out = _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim)
-            if out is not None:
-                return self.o_proj(out), None
+            res = _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim,
+                               o_nf4=nf4_linear(getattr(self, "o_proj", None)))
+            if res is not None:
+                out, o_done = res
+                return (out if o_done else self.o_proj(out)), None
         link = STATE.norm_link
         parts_q = parts_v = None
         if (recompute_lora and link is not None and link[0] is x

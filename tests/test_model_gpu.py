@@ -105,7 +105,7 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     """With LoRA dropout the packed path draws its keep-masks with the base's op on the base's
     [B, S, H] shape (solution/varlen.py:42-63), so the same seed gives the same masks."""
     from decik_b200 import solution
-    from decik_b200.solution import _state, attn, mlp, rmsnorm, varlen
+    from decik_b200.solution import _state, attn, mlp, nf4, rmsnorm, varlen
 
     dtype = torch.bfloat16
     base = _model("cuda", dtype, lora_dropout)
@@ -116,7 +116,8 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     model = _model("cuda", dtype, lora_dropout)    # same seeds: identical weights
     solution.apply(linear4bit_cls=Linear4bit, lora_classes=(LoraLayer,))
     fns = (("rope", attn.FusedQKRope), ("varlen", varlen.VarlenSDPA), ("pair", attn.LoRAPairFromNorm),
-           ("fused", attn.FusedAttentionBlock), ("addnorm", rmsnorm.AddRMSNormFn), ("mlp", mlp.FusedMLP))
+           ("fused", attn.FusedAttentionBlock), ("addnorm", rmsnorm.AddRMSNormFn), ("mlp", mlp.FusedMLP),
+           ("nf4linear", nf4.NF4Linear))
     calls = {n: 0 for n, _ in fns}
     orig = {n: getattr(c, "forward") for n, c in fns}
 
@@ -135,10 +136,11 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
             c.forward = orig[n]
     assert packed1
     n_layers = len(model.model.layers)
-    # without LoRA dropout every layer runs as one fused node; with it, the reference's chain
+    # without LoRA dropout every layer runs as one fused node (o_proj included); with it, the
+    # reference's chain, whose q, k, v and o projections are NF4Linear calls
     chain = n_layers if lora_dropout > 0 else 0
     assert calls == {"rope": chain, "varlen": chain, "pair": chain, "fused": n_layers - chain,
-                     "addnorm": n_layers, "mlp": n_layers}, calls
+                     "addnorm": n_layers, "mlp": n_layers, "nf4linear": 4 * chain}, calls
     print(f"loss {l0.item():.6f} -> {l1.item():.6f}")
     assert abs(l1.item() - l0.item()) / abs(l0.item()) < 2e-3, (l1.item(), l0.item())
     assert set(g1) == set(g0)
