@@ -581,18 +581,12 @@ int bwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor
   const dim3 grid = p.rows_outer ? dim3(static_cast<unsigned>(n_kb), static_cast<unsigned>(rkv), 1)
                                  : dim3(static_cast<unsigned>(rkv), static_cast<unsigned>(n_kb), 1);
   if (dtype == DECIK_BF16) {
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(attn_bwd_sm100_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-      set = true;
-    }
+    static unsigned long long set = 0;
+    if (int rc = ensure_dyn_smem(attn_bwd_sm100_kernel<__nv_bfloat16>, kSmem, set, "attn_bwd_sm100")) return rc;
     attn_bwd_sm100_kernel<__nv_bfloat16><<<grid, NTHREADS, kSmem, stream>>>(p);
   } else {
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(attn_bwd_sm100_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-      set = true;
-    }
+    static unsigned long long set = 0;
+    if (int rc = ensure_dyn_smem(attn_bwd_sm100_kernel<__half>, kSmem, set, "attn_bwd_sm100")) return rc;
     attn_bwd_sm100_kernel<__half><<<grid, NTHREADS, kSmem, stream>>>(p);
   }
   return check_launch("attn_bwd_sm100");

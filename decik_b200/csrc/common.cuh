@@ -27,6 +27,22 @@ inline int check_launch(const char* what) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current device, once per device:
+// the setting belongs to each device's context. `done` is the call site's bitmask of devices
+// already set (devices 0-63).
+template <typename Kernel>
+inline int ensure_dyn_smem(Kernel kernel, int bytes, unsigned long long& done, const char* what) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done & bit) return DECIK_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return set_error(DECIK_ERR_CUDA, "%s: dynamic shared memory %d bytes: %s", what, bytes,
+                                         cudaGetErrorString(e));
+  done |= bit;
+  return DECIK_OK;
+}
+
 inline int sm_count() {
   static int n = 0;
   if (n == 0) {
