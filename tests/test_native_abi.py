@@ -71,3 +71,29 @@ def test_workspace_size():
     lib = _lib.lib()
     n = lib.decik_varlen_attn_bwd_workspace(1000, 12, 128)
     assert n >= 1000 * 12 * 128 * 4 + 1000 * 12 * 4 and n % 256 == 0
+
+
+def test_step_kernels_reject_bad_arguments_before_any_cuda_call(built):
+    """The entry points around the block (residual add + norm, SwiGLU, head statistics) check their
+    sizes and pointers first; empty inputs are no-ops."""
+    lib = _lib.lib()
+    # add + norm: null pointers, then a width that is not a multiple of 4
+    rc = lib.decik_add_rmsnorm_fwd(None, None, 0, None, 2, None, None, None, 4, 1536, 1e-6, None)
+    assert rc == 1 and b"null" in lib.decik_last_error()
+    p = ctypes.c_void_p(16)  # never dereferenced: the size check fails first
+    rc = lib.decik_add_rmsnorm_fwd(p, p, 0, p, 2, p, p, None, 4, 1538, 1e-6, None)
+    assert rc == 1 and b"n_cols" in lib.decik_last_error()
+    rc = lib.decik_add_rmsnorm_bwd(p, None, p, p, 1, p, 7, p, p, None, 4, 1536, None)
+    assert rc == 1 and b"w_dtype" in lib.decik_last_error()
+    # SwiGLU: inter not a multiple of 8, rows narrower than [gate | up]
+    rc = lib.decik_swiglu_fwd(p, 24, p, 12, 4, 12, 1, None)
+    assert rc == 1 and b"multiple of 8" in lib.decik_last_error()
+    rc = lib.decik_swiglu_bwd(p, 16, p, 24, p, 32, 4, 16, 1, None)
+    assert rc == 1 and b"ld" in lib.decik_last_error()
+    # head statistics: vocabulary not a multiple of 8
+    rc = lib.decik_head_stats(p, 1004, p, p, p, p, p, 2, 1002, 1, None)
+    assert rc == 1 and b"n_vocab" in lib.decik_last_error()
+    # empty inputs
+    assert lib.decik_add_rmsnorm_fwd(None, None, 0, None, 2, None, None, None, 0, 1536, 1e-6, None) == 0
+    assert lib.decik_swiglu_fwd(None, 0, None, 0, 0, 8960, 1, None) == 0
+    assert lib.decik_head_stats(None, 0, None, None, None, None, None, 0, 151936, 1, None) == 0
