@@ -581,11 +581,11 @@ int bwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor
   const dim3 grid = p.rows_outer ? dim3(static_cast<unsigned>(n_kb), static_cast<unsigned>(rkv), 1)
                                  : dim3(static_cast<unsigned>(rkv), static_cast<unsigned>(n_kb), 1);
   if (dtype == DECIK_BF16) {
-    static unsigned long long set = 0;
+    static std::atomic<unsigned long long> set{0};
     if (int rc = ensure_dyn_smem(attn_bwd_sm100_kernel<__nv_bfloat16>, kSmem, set, "attn_bwd_sm100")) return rc;
     attn_bwd_sm100_kernel<__nv_bfloat16><<<grid, NTHREADS, kSmem, stream>>>(p);
   } else {
-    static unsigned long long set = 0;
+    static std::atomic<unsigned long long> set{0};
     if (int rc = ensure_dyn_smem(attn_bwd_sm100_kernel<__half>, kSmem, set, "attn_bwd_sm100")) return rc;
     attn_bwd_sm100_kernel<__half><<<grid, NTHREADS, kSmem, stream>>>(p);
   }

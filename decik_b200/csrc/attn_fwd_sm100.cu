@@ -561,11 +561,11 @@ int fwd_sm100(const decik_tensor3& q, const decik_tensor3& k, const decik_tensor
   p.slot = static_cast<int>(g_next_slot.fetch_add(1u) % kSlots);
   const dim3 grid(static_cast<unsigned>(p.persistent ? std::min<uint64_t>(sm_count(), tickets) : tickets));
   if (dtype == DECIK_BF16) {
-    static unsigned long long set = 0;
+    static std::atomic<unsigned long long> set{0};
     if (int rc = ensure_dyn_smem(attn_fwd_sm100_kernel<__nv_bfloat16>, kSmem, set, "attn_fwd_sm100")) return rc;
     attn_fwd_sm100_kernel<__nv_bfloat16><<<grid, NTHREADS, kSmem, stream>>>(p);
   } else {
-    static unsigned long long set = 0;
+    static std::atomic<unsigned long long> set{0};
     if (int rc = ensure_dyn_smem(attn_fwd_sm100_kernel<__half>, kSmem, set, "attn_fwd_sm100")) return rc;
     attn_fwd_sm100_kernel<__half><<<grid, NTHREADS, kSmem, stream>>>(p);
   }

@@ -12,7 +12,11 @@
 // - The array exists on every GPU that loads this library and stays allocated until the process
 //   exits (about 8.5 MB per GPU).
 // - The first call on a device looks the array's address up (cudaGetSymbolAddress, with that
-//   device current) and caches it; make that first call before any stream capture.
+//   device current) and caches it. The library is built as separate device modules and CUDA loads
+//   modules lazily by default, so that first lookup is also when the driver loads this file's
+//   module and reserves the 8.5 MB on the device: make the first call at start-up, before the
+//   caller's pool claims the device memory and before any stream capture. A call with zero tokens
+//   does only this set-up (no kernel runs), so it serves as the start-up call.
 // - All calls share the one array. The kernels zero the dq accumulator and rewrite the delta
 //   values at the start of every call, so stale contents from an earlier call do not matter, but
 //   two calls whose kernels overlap on the GPU (different streams, no ordering) race on the array.
@@ -73,7 +77,6 @@ extern "C" int decik_varlen_attn_bwd_noalloc(decik_tensor3 dout, decik_tensor3 q
                                              int max_len, int64_t n_tok, int n_heads, int n_kv, int head_dim,
                                              float scale, int dtype, void* stream) {
   using namespace decik;
-  if (n_rows == 0 || n_tok == 0 || max_len == 0) return DECIK_OK;
   if (n_tok < 0 || n_heads <= 0)
     return set_error(DECIK_ERR_INVALID, "varlen_attn_bwd_noalloc: bad sizes (T=%lld, heads %d)", (long long)n_tok, n_heads);
   if (n_tok * n_heads > kNoAllocTokenHeads)
@@ -86,6 +89,7 @@ extern "C" int decik_varlen_attn_bwd_noalloc(decik_tensor3 dout, decik_tensor3 q
   void* scratch = nullptr;
   const int rc = scratch_address(&scratch);
   if (rc) return rc;
+  if (n_rows == 0 || n_tok == 0 || max_len == 0) return DECIK_OK;  // set-up only
   // one head subset per key block: dK / dV stay on chip, so the scratch holds only dq and delta
   return attn::varlen_attn_bwd_impl(dout, q, k, v, out, lse, dq, dk, dv, cu_seqlens, n_rows, max_len, n_tok, n_heads,
                                     n_kv, head_dim, scale, dtype, scratch, false, as_stream(stream));

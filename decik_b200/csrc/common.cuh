@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -29,17 +30,18 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // Raises a kernel's dynamic shared-memory limit to `bytes` on the current device, once per device:
 // the setting belongs to each device's context. `done` is the call site's bitmask of devices
-// already set (devices 0-63).
+// already set (devices 0-63); host threads driving different devices may call concurrently (a
+// device set twice by two racing threads is harmless: the attribute call is idempotent).
 template <typename Kernel>
-inline int ensure_dyn_smem(Kernel kernel, int bytes, unsigned long long& done, const char* what) {
+inline int ensure_dyn_smem(Kernel kernel, int bytes, std::atomic<unsigned long long>& done, const char* what) {
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
-  if (done & bit) return DECIK_OK;
+  if (done.load(std::memory_order_acquire) & bit) return DECIK_OK;
   const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return set_error(DECIK_ERR_CUDA, "%s: dynamic shared memory %d bytes: %s", what, bytes,
                                          cudaGetErrorString(e));
-  done |= bit;
+  done.fetch_or(bit, std::memory_order_acq_rel);
   return DECIK_OK;
 }
 

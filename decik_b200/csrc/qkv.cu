@@ -572,11 +572,11 @@ extern "C" int decik_qkv_epilogue_fwd(const void* y, int64_t ldy, const void* u,
                   static_cast<unsigned>((n_heads + 2 * n_kv + kFwdWarps - 1) / kFwdWarps));
   const int smem = kCsBytes + kFwdWarps * 2 * kTile * 2;
   if (dtype == DECIK_BF16) {
-    static unsigned long long set = 0;
+    static std::atomic<unsigned long long> set{0};
     if (int rc = ensure_dyn_smem(qkv_fwd_kernel<__nv_bfloat16>, smem, set, "qkv_epilogue_fwd")) return rc;
     qkv_fwd_kernel<__nv_bfloat16><<<grid, kFwdWarps * 32, smem, as_stream(stream)>>>(p);
   } else {
-    static unsigned long long set = 0;
+    static std::atomic<unsigned long long> set{0};
     if (int rc = ensure_dyn_smem(qkv_fwd_kernel<__half>, smem, set, "qkv_epilogue_fwd")) return rc;
     qkv_fwd_kernel<__half><<<grid, kFwdWarps * 32, smem, as_stream(stream)>>>(p);
   }
@@ -589,11 +589,11 @@ int qkv_bwd_launch(const QkvBwdParams& p, int dtype, cudaStream_t stream) {
   const int smem = kCsBytes + kWarps * kTile * 2;  // >= the du partials [warps][2][16][16] fp32
   static_assert(kWarps * kTile * 2 >= kWarps * 2 * 256 * 4, "du partials must fit in the tiles' space");
   if (dtype == DECIK_BF16) {
-    static unsigned long long set = 0;
+    static std::atomic<unsigned long long> set{0};
     if (int rc = ensure_dyn_smem(qkv_bwd_kernel<__nv_bfloat16>, smem, set, "qkv_epilogue_bwd")) return rc;
     qkv_bwd_kernel<__nv_bfloat16><<<grid, kWarps * 32, smem, stream>>>(p);
   } else {
-    static unsigned long long set = 0;
+    static std::atomic<unsigned long long> set{0};
     if (int rc = ensure_dyn_smem(qkv_bwd_kernel<__half>, smem, set, "qkv_epilogue_bwd")) return rc;
     qkv_bwd_kernel<__half><<<grid, kWarps * 32, smem, stream>>>(p);
   }

@@ -63,16 +63,21 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with the given parity to complete; false (and *err set) if it never does.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+// Waits for the phase with the given parity to complete within `limit` cycles; false (and *err
+// set to `code`) if it does not.
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, int* err, int code, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = cycles();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (cycles() - t0 > kWaitLimitCycles) break;
+    if (cycles() - t0 > limit) break;
   }
   report(err, code);
   return false;
+}
+// The kernels' wait: gives up after kWaitLimitCycles.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
+  return mbar_wait_limit(bar, parity, err, code, kWaitLimitCycles);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -2,6 +2,8 @@
 // error word that bounded waits write when they give up.
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "attn_common.cuh"
 
 namespace decik {
@@ -12,29 +14,34 @@ static __device__ int g_kernel_error = 0;
 
 namespace attn {
 
+// The device address of g_kernel_error on the current device, looked up once per device behind a
+// mutex (host threads may drive different devices concurrently).
 int* attn_error_word() {
-  static int* ptr = nullptr;
-  static int dev_cached = -1;
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static int* cached[kMaxDevices] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (ptr == nullptr || dev != dev_cached) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_kernel_error) != cudaSuccess) return nullptr;
-    ptr = static_cast<int*>(p);
-    dev_cached = dev;
+    cached[dev] = static_cast<int*>(p);
   }
-  return ptr;
+  return cached[dev];
 }
 
+// cuTensorMapEncodeTiled from the driver (process-wide; the function-local static is initialised
+// once, thread-safely).
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    return nullptr;
+  }();
   return fn;
 }
 

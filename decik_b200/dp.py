@@ -99,6 +99,24 @@ class GradBucket:
             if p.grad is None or p.grad.data_ptr() != v.data_ptr():
                 raise RuntimeError("a gradient left the bucket (was .grad reassigned?)")
 
+    def check_layout(self, group=None):
+        """Raise ValueError on every rank unless all ranks hold buckets of the same layout (the
+        same number of parameters with the same sizes). Run once before the first all_reduce: a
+        rank whose bucket differs would otherwise sum unrelated gradients or wait for a collective
+        of another size. Cost: one all-gather of a few integers."""
+        import torch.distributed as dist
+
+        if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
+            return
+        sizes = [p.numel() for p in self.params]
+        sig = torch.tensor([len(sizes), self.flat.numel(), hash(tuple(sizes)) & 0x7FFFFFFF], dtype=torch.int64,
+                           device=self.flat.device)
+        every = [torch.empty_like(sig) for _ in range(dist.get_world_size(group))]
+        dist.all_gather(every, sig, group=group)
+        if any(not torch.equal(e, sig) for e in every):
+            rows = ", ".join(f"rank {r}: {int(e[0])} params / {int(e[1])} values" for r, e in enumerate(every))
+            raise ValueError(f"GradBucket layouts differ across ranks ({rows})")
+
     def all_reduce(self, group=None, average: bool = False, async_op: bool = False):
         import torch.distributed as dist
 

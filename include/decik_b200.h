@@ -48,6 +48,13 @@ DECIK_API int decik_abi_version(void);
  * wait on mbarriers never spin forever: they record a code here and return. */
 DECIK_API int decik_kernel_error(int reset);
 
+/* Failure-path self-test (no counterpart in the reference, whose Triton kernels have no bounded
+ * waits): launches one warp that holds 32 TMEM columns and waits on an mbarrier nothing arrives
+ * on, giving up after limit_cycles (at most 4e9) exactly as the attention kernels give up after
+ * theirs. It then records 901 in the error word read by decik_kernel_error(), frees its TMEM and
+ * returns; *done (device int) becomes 2 when the wait ran out (1 if it had completed). */
+DECIK_API int decik_wait_limit_selftest(long long limit_cycles, int* done, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * NF4 double-quant dequant.
  * Replaces solution/nf4.py:66-85 (dequantize_nf4) and its kernel skc_nf4_dequant_kernel
@@ -304,9 +311,13 @@ DECIK_API int decik_varlen_attn_bwd(decik_tensor3 dout, decik_tensor3 q, decik_t
  * held on every GPU that loads the library until the process exits). Larger inputs return
  * DECIK_ERR_INVALID with a message. It is meant for callers whose device memory is owned by a
  * host framework's pool that forbids raw allocations, or that run where an allocation could
- * block or fail. The first call on a device looks up the array's address (make it before any
- * stream capture); every call reuses the same array, so calls whose kernels overlap on the GPU
- * race with each other. Nothing is allocated or freed.
+ * block or fail. The first call on a device looks up the array's address; under CUDA's default
+ * lazy module loading that is also when the driver loads the array's module and reserves its
+ * 8.5 MB on that device. So make the first call on each device at start-up, before the host's
+ * pool takes the device memory and before any stream capture: a call with n_tok = 0 does only
+ * this set-up (no kernel runs). Every call reuses the same array, so calls whose kernels overlap
+ * on the GPU (different streams with no ordering) race with each other: order them on one stream
+ * or with events. This entry point itself allocates and frees nothing.
  * ------------------------------------------------------------------------------------------- */
 DECIK_API int decik_varlen_attn_bwd_noalloc(decik_tensor3 dout, decik_tensor3 q, decik_tensor3 k, decik_tensor3 v,
                           decik_tensor3 out, const float* lse, decik_tensor3_mut dq,

@@ -28,16 +28,23 @@ def _case(dtype, lengths=LENGTHS, seed=0, hidden=1536, n_heads=12, n_kv=2):
     return block, packing, cos, sin, x, dout
 
 
-def _oracle(block, packing, cos, sin, x, dout):
-    from oracle.block import block_step
+def _oracle(block, packing, cos, sin, x, dout, rounded=True):
+    """oracle.block's fp32 step. With ``rounded`` it gets the inputs the kernels get: x, the
+    biases and the LoRA matrices rounded to the block's 16-bit dtype, and W_q, W_k, W_v dequantised
+    to that dtype (the reference's NF4Linear multiplies x16 by the fp16 dequantised weight,
+    solution/nf4.py:93-97), so the comparison measures the kernels' error and not the rounding of
+    their inputs."""
+    from oracle.block import block_step, dequant_torch
 
-    cpu = lambda t: t.detach().float().cpu()
-    inputs = {"x": x, "b_q": cpu(block.bias["q"]), "b_k": cpu(block.bias["k"]), "b_v": cpu(block.bias["v"]),
-              "a_q": cpu(block.lora["a_q"]), "bb_q": cpu(block.lora["b_q"]), "a_v": cpu(block.lora["a_v"]),
-              "bb_v": cpu(block.lora["b_v"]), "cos": cpu(cos), "sin": cpu(sin),
+    dt = block.dtype if rounded else torch.float32
+    cpu = lambda t: t.detach().float().cpu().to(dt).float()
+    inputs = {"x": x.to(dt).float(), "b_q": cpu(block.bias["q"]), "b_k": cpu(block.bias["k"]),
+              "b_v": cpu(block.bias["v"]), "a_q": cpu(block.lora["a_q"]), "bb_q": cpu(block.lora["b_q"]),
+              "a_v": cpu(block.lora["a_v"]), "bb_v": cpu(block.lora["b_v"]), "cos": cos.cpu(), "sin": sin.cpu(),
               "nf4_q": block.nf4_states["q"], "nf4_k": block.nf4_states["k"], "nf4_v": block.nf4_states["v"],
               "spans": packing.spans, "n_heads": block.n_heads, "n_kv": block.n_kv, "scaling": block.scaling}
-    return block_step(inputs, dout.float())
+    weights = {f"w_{n}": dequant_torch(block.nf4_states[n]).to(dt).float() for n in ("q", "k", "v")}
+    return block_step(inputs, dout.float(), weights)
 
 
 def _run(block, packing, cos, sin, x, dout, fused):
@@ -50,13 +57,10 @@ def _run(block, packing, cos, sin, x, dout, fused):
     return (out.detach().float().cpu(), xg.grad.cpu()) + tuple(p.grad.cpu() for p in block.lora_params())
 
 
-# The stated bar (rel-L2 5e-3, max-abs 2e-2 against fp32) is met in fp16, the reference's compute
-# dtype, with a wide margin (dA_q 8e-4). bf16 keeps 8 significant bits against fp16's 11, and at the
-# block level the rounding of its own inputs already spends the bar: x16 = bf16(x) is off by 1.7e-3,
-# q/k/v after the projection and RoPE by 3.3e-3, and attention turns that into dq 5.8e-3 although the
-# attention kernels on the same rounded inputs add only 2.5e-3 (their own 5e-3 tests run on rounded
-# inputs). The bf16 block gradients are therefore held to twice the bar (measured: <= 6.7e-3).
-BLOCK_REL_L2 = {torch.float16: 5e-3, torch.bfloat16: 1e-2}
+# The stated bar: rel-L2 <= 5e-3 and max-abs <= 2e-2 against the fp32 oracle fed the same 16-bit
+# inputs (tests/tolerance.py), for the output, the input gradient and all four LoRA gradients, in
+# both 16-bit dtypes.
+BLOCK_REL_L2 = {torch.float16: 5e-3, torch.bfloat16: 5e-3}
 
 
 @pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])

@@ -481,3 +481,68 @@ def test_varlen_attention_config4_full_size(cuda_lib):
     s, L = spans[0]
     for name, a, e in (("out", out, ro), ("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
         _close_gpu(a[s:s + L], e[s:s + L], f"{name} of the 32,768-token row")
+
+
+@pytest.mark.parametrize("rank", range(8))
+def test_varlen_attention_bench_packings_every_row(cuda_lib, rank):
+    """The packings bench.py's block step times on ranks 0-7 (bench.lengths_for(1000 + rank): 16,384
+    tokens, rows up to 4,096), 12 / 2 heads, bf16, q and k head-major as the projection epilogue
+    writes them. This runs the launch order the bench runs (the heavy-first persistent forward and
+    the head-split backward with fp32 dK / dV partials). Every row of out, lse, dq, dk and dv is
+    checked against the fp32 restatement: the bar holds for the whole packing and for each row."""
+    from bench import lengths_for
+
+    ops = _ops()
+    lengths = lengths_for(1000 + rank)
+    assert sum(lengths) == 16384
+    spans, cu, q, k, v, do = _attn_case(lengths, 12, 2, torch.bfloat16, seed=50 + rank, layout="ref")
+    scale = 128 ** -0.5
+    out, lse = ops.varlen_attn_fwd(q, k, v, cu, max(lengths), scale)
+    dq, dk, dv = ops.varlen_attn_bwd(do, q, k, v, out, lse, cu, max(lengths), scale)
+    torch.cuda.synchronize()
+    assert cuda_lib.decik_kernel_error(1) == 0
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ro, rl, rdq, rdk, rdv = _attn_fp32_rows(q, k, v, do, spans, scale)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert (lse - rl).abs().max().item() <= 2e-3
+    for name, a, e in (("out", out, ro), ("dq", dq, rdq), ("dk", dk, rdk), ("dv", dv, rdv)):
+        _close_gpu(a, e, name)
+        for i, (s, L) in enumerate(spans):
+            _close_gpu(a[s:s + L], e[s:s + L], f"{name} of row {i} (length {L})")
+
+
+@pytest.mark.parametrize("rank", [0, 3])
+def test_attn_qkv_bwd_bench_packing_every_row(cuda_lib, rank):
+    """The one-call backward the fused block runs (decik_attn_qkv_bwd: attention backward, then the
+    projection epilogue reading its fp32 accumulators) on a bench packing. With cos = 1 and sin = 0
+    RoPE^T is the identity, so dy's q, k and v columns are dq, dk and dv rounded to bf16: every row
+    is checked against the fp32 restatement."""
+    from bench import lengths_for
+
+    ops = _ops()
+    lengths = lengths_for(1000 + rank)
+    T, HQ, HK, D = sum(lengths), 12, 2, 128
+    spans, cu, q, k, v, do = _attn_case(lengths, HQ, HK, torch.bfloat16, seed=70 + rank, layout="ref")
+    scale = D ** -0.5
+    out, lse = ops.varlen_attn_fwd(q, k, v, cu, max(lengths), scale)
+    cos = torch.ones(T, D, device=DEV)
+    sin = torch.zeros(T, D, device=DEV)
+    dy = torch.zeros(T, (HQ + 2 * HK) * D + 32, dtype=torch.bfloat16, device=DEV)
+    ops.attn_qkv_bwd(do, q, k, v, out, lse, cu, max(lengths), scale, cos, sin, None, 1.0, dy)
+    torch.cuda.synchronize()
+    assert cuda_lib.decik_kernel_error(1) == 0
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        _, _, rdq, rdk, rdv = _attn_fp32_rows(q, k, v, do, spans, scale)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    got = {"dq": dy[:, :HQ * D].view(T, HQ, D), "dk": dy[:, HQ * D:(HQ + HK) * D].view(T, HK, D),
+           "dv": dy[:, (HQ + HK) * D:(HQ + 2 * HK) * D].view(T, HK, D)}
+    for name, e in (("dq", rdq), ("dk", rdk), ("dv", rdv)):
+        _close_gpu(got[name], e, name)
+        for i, (s, L) in enumerate(spans):
+            _close_gpu(got[name][s:s + L], e[s:s + L], f"{name} of row {i} (length {L})")
