@@ -39,6 +39,63 @@ def _p(t: torch.Tensor | None) -> int | None:
 
 
 # ------------------------------------------------------------------------------------------------
+# padding-free packing
+# ------------------------------------------------------------------------------------------------
+_MASK_CODES = {torch.int64: 0, torch.int32: 1, torch.uint8: 2, torch.bool: 2}
+_pinned: dict = {}
+
+
+def _pinned_i32(n: int) -> torch.Tensor:
+    """A reused page-locked int32 host buffer of at least n values (this thread's packing reads)."""
+    buf = _pinned.get("summary")
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(max(n, 1024), dtype=torch.int32, pin_memory=True)
+        _pinned["summary"] = buf
+    return buf
+
+
+def pack_rows(mask: torch.Tensor, input_ids: torch.Tensor | None = None):
+    """The packing of a right-padded [B, S] batch built on the device (decik_pack_rows).
+
+    Returns None when some row is not right-padded, else ``(lengths, cu_seqlens, index,
+    positions, ids)``: the row lengths as host ints, cu_seqlens int32 [B + 1], index / positions
+    int64 [T] and the packed ids int64 [T] (None without ``input_ids``), all on the mask's device.
+    The only host read is the summary of 4 + B int32, copied into pinned memory."""
+    _cuda(mask, input_ids)
+    if mask.dim() != 2:
+        raise RuntimeError("decik_b200 pack_rows: mask must be [batch, seq]")
+    code = _MASK_CODES.get(mask.dtype)
+    if code is None:
+        raise RuntimeError(f"decik_b200 pack_rows: mask dtype {mask.dtype}")
+    mask = mask.contiguous()
+    B, S = mask.shape
+    dev = mask.device
+    if input_ids is not None:
+        if input_ids.shape != mask.shape or input_ids.dtype != torch.int64:
+            raise RuntimeError("decik_b200 pack_rows: input_ids must be int64 [batch, seq]")
+        input_ids = input_ids.contiguous()
+    cu = torch.empty(B + 1, dtype=torch.int32, device=dev)
+    index = torch.empty(B * S, dtype=torch.int64, device=dev)
+    positions = torch.empty(B * S, dtype=torch.int64, device=dev)
+    ids = torch.empty(B * S, dtype=torch.int64, device=dev) if input_ids is not None else None
+    summary = torch.empty(4 + B, dtype=torch.int32, device=dev)
+    rc = _lib.lib().decik_pack_rows(_p(mask), code, _p(input_ids), B, S, _p(cu), _p(index), _p(positions),
+                                    _p(ids), _p(summary), _stream(mask))
+    _lib.check(rc, "pack_rows")
+    host = _pinned_i32(4 + B)[:4 + B]
+    host.copy_(summary, non_blocking=True)
+    done = torch.cuda.Event()
+    done.record(torch.cuda.current_stream(dev))
+    done.synchronize()  # the step's one device -> host read
+    vals = host.tolist()
+    T, right_padded = vals[0], vals[2]
+    if not right_padded:
+        return None
+    lengths = vals[4:4 + B]
+    return lengths, cu, index[:T], positions[:T], (ids[:T] if ids is not None else None)
+
+
+# ------------------------------------------------------------------------------------------------
 # NF4
 # ------------------------------------------------------------------------------------------------
 def nf4_dequant(packed: torch.Tensor, absmax: torch.Tensor, code: torch.Tensor, shape,

@@ -56,6 +56,24 @@ DECIK_API int decik_kernel_error(int reset);
 DECIK_API int decik_wait_limit_selftest(long long limit_cycles, int* done, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Padding-free packing of a right-padded batch, on the device.
+ * Replaces plan() / Packing of solution/varlen.py:191-226 and :23-40 (mask.sum, the right-padding
+ * torch.equal check, lengths.tolist(), mask.nonzero(), the positions and cu_seqlens), which read
+ * the device three times; here the caller reads only `summary` (one copy of 4 + batch int32).
+ *   mask       [batch, seq], contiguous; mask_dtype 0 = int64, 1 = int32, 2 = uint8 / bool
+ *   input_ids  int64 [batch, seq] contiguous, or NULL (then ids_out must be NULL)
+ *   cu_seqlens int32 [batch + 1]: row starts in the packed sequence, then T
+ *   index      int64 [>= T]: b * seq + s of each real token, row-major (capacity batch * seq)
+ *   positions  int64 [>= T]: s (the token's position in its row)
+ *   ids_out    int64 [>= T]: input_ids at index, or NULL
+ *   summary    int32 [4 + batch]: T, max row length, 1 if every row is right-padded (else 0: the
+ *              other outputs are then meaningless), min row length, then the row lengths.
+ * batch <= 8192, seq <= 2^30, batch * seq < 2^31. One kernel on `stream`. */
+DECIK_API int decik_pack_rows(const void* mask, int mask_dtype, const int64_t* input_ids, int64_t batch,
+                              int64_t seq, int32_t* cu_seqlens, int64_t* index, int64_t* positions,
+                              int64_t* ids_out, int32_t* summary, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * NF4 double-quant dequant.
  * Replaces solution/nf4.py:66-85 (dequantize_nf4) and its kernel skc_nf4_dequant_kernel
  * (solution/nf4.py:28-49). Bit-exact: for packed byte i, the high nibble is weight 2i and the low

@@ -228,3 +228,19 @@ def test_head_oracle_matches_reference_fixture():
     np.testing.assert_allclose(token_loss, g["token_loss"], rtol=1e-4, atol=1e-4)
     assert np.array_equal(hit, g["hit"]) and hit[1] == 1
     assert np.linalg.norm(dh - g["dhidden"]) / np.linalg.norm(g["dhidden"]) < 2e-3
+
+
+def test_packing_from_lengths_matches_the_plan():
+    """solution.varlen.packing_from_lengths (device ops, run here on the CPU) gives the positions,
+    cu_seqlens and spans of the oracle's plan for the same rows."""
+    from decik_b200.solution.varlen import packing_from_lengths
+
+    lengths = [401, 77, 512, 3]
+    p = packing_from_lengths(lengths, "cpu")
+    mask = np.zeros((4, 512), dtype=np.int64)
+    for i, L in enumerate(lengths):
+        mask[i, :L] = 1
+    ref = packing.plan(mask)
+    assert p.spans == ref["spans"] and p.max_len == ref["max_len"] and p.n_tokens == ref["n_tokens"]
+    assert np.array_equal(p.positions.numpy(), ref["positions"])
+    assert np.array_equal(p.cu_seqlens("cpu").numpy(), ref["cu_seqlens"])
