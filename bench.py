@@ -99,14 +99,21 @@ def causal_flops(lengths, n_heads=HQ, head_dim=D) -> float:
 
 
 def peaks() -> dict:
+    """Roofline denominators: MEASURED_PEAKS.json (driver-measured on this pool's B200s: bf16 GEMM
+    burst and sustained, HBM copy), else the pool's earlier measurement as a labelled fallback."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             p = json.load(f)
         return {"bf16_tflops": float(p["bf16_tflops"]), "hbm_gbs": float(p["hbm_gbs"]),
-                "source": "MEASURED_PEAKS.json (measured; bf16 burst)"}
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "MEASURED_PEAKS.json (measured; bf16 burst)",
+                "source_sustained": "MEASURED_PEAKS.json (measured; bf16 sustained: the kernels run inside a "
+                                    "long step)"}
     except Exception:
-        return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback (earlier pool measurement)"}
+        return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback (earlier pool measurement)",
+                "source_sustained": "fallback (earlier pool measurement, sustained)"}
 
 
 class ClockSampler:
@@ -196,10 +203,21 @@ def dist_setup():
     return world, rank, local
 
 
+def block_flops(lengths, hidden=HIDDEN, n_heads=HQ, n_kv=HK) -> float:
+    """Algorithmic FLOPs of one attention-block step over these rows: the q/k/v projections'
+    forward and input-gradient GEMMs, the LoRA r16 products (forward, input and parameter
+    gradients) and the causal attention (3 x the forward's 4 . D . Hq . L(L+1)/2)."""
+    T = sum(lengths)
+    proj = hidden * (n_heads + 2 * n_kv) * D
+    lora = 16 * (2 * hidden + (n_heads + n_kv) * D)
+    return 4.0 * proj * T + 6.0 * lora * T + 3.0 * causal_flops(lengths, n_heads=n_heads)
+
+
 def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0, hidden: int = HIDDEN,
                         n_heads: int = HQ, n_kv: int = HK):
     """Times the reference's CPU path (oracle.block, torch fp32) on the first rows of the packing,
-    ``sample_tokens`` tokens (last row truncated). Returns (tokens/s, sample description, threads)."""
+    ``sample_tokens`` tokens (last row truncated). Returns (tokens/s of the whole packing
+    extrapolated from the sample by block_flops, sample description, threads, step times)."""
     from decik_b200.nf4_quant import quantize_nf4
     from oracle import block as ob
 
@@ -237,22 +255,28 @@ def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0
         t0 = time.perf_counter()
         ob.block_step(inputs, grad)
         times.append(time.perf_counter() - t0)
-    desc = f"{len(rows)} rows, {T} tokens (first rows of the packing), fwd+bwd incl. NF4 dequant, fp32"
-    return T / statistics.mean(times), desc, threads, times
+    ratio = block_flops(lengths, hidden, n_heads, n_kv) / block_flops(rows, hidden, n_heads, n_kv)
+    value = sum(lengths) / (statistics.mean(times) * ratio)
+    desc = (f"{len(rows)} rows, {T} tokens (first rows of the packing) timed, fwd+bwd incl. NF4 dequant, fp32 "
+            f"({T / statistics.mean(times):.1f} tokens/s); value = the packing's {sum(lengths)} tokens / (sample "
+            f"step time x FLOP ratio {ratio:.2f}, block_flops)")
+    return value, desc, threads, times
 
 
 REF_BUDGET_S = 90.0  # the reference arm's timed steps, seconds
 
-# DRAM bytes (read + write) of the two attention kernels in one config-3 step, from the ncu capture
-# in profiles/attn_block_fused_config3.md (forward 68.1 + 15.6 MB, backward 412.0 + 186.0 MB)
-ATTN_DRAM_BYTES = {"config3": 681.6e6}
+# DRAM bytes (read + write) of the two attention kernels in one config-3 step (N = 1 packing), from
+# one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum; forward 68.1 + 15.6 MB, backward
+# 412.0 + 186.0 MB). Not measured by this run: the second field says which kernel build it describes.
+ATTN_DRAM_BYTES = {"config3": (681.6e6, "ncu capture of both attention kernels, one step, kernels as of "
+                                        "commit a73d9e0 (the forward has changed since); not this run's")}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    hidden, hq, hk, lengths_of, workload, _ = WORKLOADS[args.workload]
-    lengths = lengths_of(1000)
+    hidden, hq, hk, _, workload, _ = WORKLOADS[args.workload]
+    lengths = block_lengths(args.workload, 1, 0)
     sample = args.ref_tokens
     # warm-up step (untimed), then K timed steps, each one bounded sample of the workload; the
     # sample shrinks (attention is superlinear in it, so it is stated in the line) when K steps of
@@ -274,7 +298,22 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, world, rank, local):
+def block_lengths(workload: str, world: int, rank: int) -> list[int]:
+    """This rank's rows of the block workload. Config 3: one global pool of world x 16,384 tokens
+    (lengths U[64, 4096], seed 1000) split across the ranks by whole rows with dp.partition_rows
+    (balanced by tokens + causal pairs); at N = 1 the pool is lengths_for(1000). Config 4: each
+    rank its own 131,072-token packing (seed 1000 + rank)."""
+    from decik_b200.dp import partition_rows
+
+    if workload != "config3":
+        return WORKLOADS[workload][3](1000 + rank)
+    pool = lengths_for(1000, total=world * TOKENS)
+    return [pool[i] for i in partition_rows(pool, world)[rank]]
+
+
+def measure_block(args, world, rank, local, n_steps, workload=None, e2e=True, cpu=True):
+    """The attention block step (config 3 or 4) on this rank; returns rank 0's JSON line (None on
+    other ranks). ``e2e`` adds the end-to-end leg, ``cpu`` the CPU baseline leg (rank 0, N=1)."""
     from decik_b200 import ops
     from decik_b200.block import QLoRAAttentionBlock, rope_cos_sin
     from decik_b200.dp import GradBucket
@@ -282,10 +321,17 @@ def run_ours(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    hidden, hq, hk, lengths_of, workload, lengths_text = WORKLOADS[args.workload]
+    name = workload or args.workload
+    hidden, hq, hk, _, workload, lengths_text = WORKLOADS[name]
     block = QLoRAAttentionBlock.random(hidden=hidden, n_heads=hq, n_kv=hk, seed=0, device=dev)  # frozen + LoRA
-    lengths = lengths_of(1000 + rank)                                 # each rank its own sequences
+    lengths = block_lengths(name, world, rank)                        # this rank's whole rows
     T = sum(lengths)
+    T_all = T
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([float(T)], device=dev)
+        dist.all_reduce(t)
+        T_all = int(t.item())
     packing = packing_from_lengths(lengths, dev)
     cos, sin = rope_cos_sin(packing.positions, D)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -327,7 +373,7 @@ def run_ours(args, world, rank, local):
     timer = ops.OpTimer()
     ops.install_timer(timer)
     with ClockSampler(local) as clocks:
-        step_ms = timed(args.steps, lambda: step(x, dout))
+        step_ms = timed(n_steps, lambda: step(x, dout))
     ops.install_timer(None)
     op_ms = timer.elapsed_ms()
     launches = timer.launches
@@ -336,114 +382,160 @@ def run_ours(args, world, rank, local):
         t = torch.tensor([total_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
-    value = world * T * args.steps / (total_ms / 1e3)
+    value = T_all * n_steps / (total_ms / 1e3)
 
-    # end to end through the same public API: every step's x and dOut are copied from pinned host
-    # memory and its LoRA gradients read back inside the timed region. As a training loop's input
-    # prefetch would, step i + 1's inputs are copied on a second stream (into the other of two
-    # device buffers) while step i computes. Inputs (151 MB) exceed L2 and are new every step.
-    x_host = x.detach().cpu().pin_memory()
-    d_host = dout.cpu().pin_memory()
-    g_host = torch.empty(bucket.flat.numel(), dtype=torch.float32).pin_memory()
-    bufs = [(torch.empty_like(x.detach()), torch.empty_like(dout)) for _ in range(2)]
-    copy_stream = torch.cuda.Stream(device=dev)
-    compute = torch.cuda.current_stream(dev)
+    e2e_value = None
+    if e2e:
+        # end to end through the same public API: every step's x and dOut are copied from pinned host
+        # memory and its LoRA gradients read back inside the timed region. As a training loop's input
+        # prefetch would, step i + 1's inputs are copied on a second stream (into the other of two
+        # device buffers) while step i computes. Inputs (151 MB) exceed L2 and are new every step.
+        x_host = x.detach().cpu().pin_memory()
+        d_host = dout.cpu().pin_memory()
+        g_host = torch.empty(bucket.flat.numel(), dtype=torch.float32).pin_memory()
+        bufs = [(torch.empty_like(x.detach()), torch.empty_like(dout)) for _ in range(2)]
+        copy_stream = torch.cuda.Stream(device=dev)
+        compute = torch.cuda.current_stream(dev)
 
-    def e2e_run(n):
-        copied = [torch.cuda.Event() for _ in range(2)]
-        consumed = [torch.cuda.Event() for _ in range(2)]
+        def e2e_run(n):
+            copied = [torch.cuda.Event() for _ in range(2)]
+            consumed = [torch.cuda.Event() for _ in range(2)]
 
-        def copy_in(i):
-            b = i % 2
-            with torch.cuda.stream(copy_stream):
-                if i >= 2:
-                    copy_stream.wait_event(consumed[b])  # step i - 2 is done with this buffer
-                bufs[b][0].copy_(x_host, non_blocking=True)
-                bufs[b][1].copy_(d_host, non_blocking=True)
-                copied[b].record(copy_stream)
+            def copy_in(i):
+                b = i % 2
+                with torch.cuda.stream(copy_stream):
+                    if i >= 2:
+                        copy_stream.wait_event(consumed[b])  # step i - 2 is done with this buffer
+                    bufs[b][0].copy_(x_host, non_blocking=True)
+                    bufs[b][1].copy_(d_host, non_blocking=True)
+                    copied[b].record(copy_stream)
 
-        copy_in(0)
-        for i in range(n):
-            b = i % 2
-            if i + 1 < n:
-                copy_in(i + 1)
-            compute.wait_event(copied[b])
-            step(bufs[b][0].detach().requires_grad_(True), bufs[b][1])
-            consumed[b].record(compute)
-            g_host.copy_(bucket.flat, non_blocking=True)
+            copy_in(0)
+            for i in range(n):
+                b = i % 2
+                if i + 1 < n:
+                    copy_in(i + 1)
+                compute.wait_event(copied[b])
+                step(bufs[b][0].detach().requires_grad_(True), bufs[b][1])
+                consumed[b].record(compute)
+                g_host.copy_(bucket.flat, non_blocking=True)
 
-    e2e_run(2)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(compute)
-    e2e_run(args.steps)
-    ev1.record(compute)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e2e_ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+        e2e_run(2)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(compute)
+        e2e_run(n_steps)
+        ev1.record(compute)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e2e_ms = ev0.elapsed_time(ev1)
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e_value = T_all * n_steps / (e2e_ms / 1e3)
 
     if rank != 0:
-        return
+        return None
     pk = peaks()
     f_fwd = causal_flops(lengths, n_heads=hq)
     fwd_ms = statistics.mean(op_ms.get("varlen_attn_fwd", [float("nan")]))
     bwd_ms = statistics.mean(op_ms.get("varlen_attn_bwd", [float("nan")]))
     attn_tflops = 3.0 * f_fwd / ((fwd_ms + bwd_ms) / 1e3) / 1e12
-    kernels = {name: {"ms_mean": round(statistics.mean(v), 4), "calls_per_step": len(v) // max(args.steps, 1)}
+    kernels = {name: {"ms_mean": round(statistics.mean(v), 4), "calls_per_step": len(v) // max(n_steps, 1)}
                for name, v in op_ms.items()}
     kernels["varlen_attn_fwd"]["tflops"] = round(f_fwd / (fwd_ms / 1e3) / 1e12, 2)
     kernels["varlen_attn_bwd"]["tflops"] = round(2 * f_fwd / (bwd_ms / 1e3) / 1e12, 2)
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
+        "steps": n_steps, "warmup": args.warmup, "ms_per_step": round(total_ms / n_steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded lengths, N(0,1) activations, random-init NF4/LoRA weights)",
-        "config": {"workload": workload, "tokens_per_gpu": T, "rows_rank0": len(lengths),
-                   "lengths": f"{lengths_text}, numpy default_rng(1000 + rank)", "hidden": hidden,
+        "config": {"workload": workload, "tokens_per_gpu": T, "tokens_all_ranks": T_all, "rows_rank0": len(lengths),
+                   "lengths": f"{lengths_text}; " + ("one pool of N x 16,384 tokens (seed 1000) split by "
+                                                     "dp.partition_rows" if name == "config3" else
+                                                     "numpy default_rng(1000 + rank)"), "hidden": hidden,
                    "heads": f"{hq}/{hk}", "head_dim": D, "lora": "r16 alpha32 q,v", "nf4": "bs64, double quant bs256",
                    "l2": "flushed between timed steps (256 MiB write, untimed)", "parallelism": f"dp{world}"},
         "roofline": {"bound": "tensor", "kernel": "varlen attention fwd+bwd (decik_varlen_attn_fwd/bwd)",
                      "achieved": round(attn_tflops, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": round(attn_tflops / pk["bf16_tflops"], 4),
-                     "traffic": ATTN_DRAM_BYTES.get(args.workload),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of both kernels, one step"
-                     if args.workload in ATTN_DRAM_BYTES else None,
+                     "traffic": ATTN_DRAM_BYTES.get(name, (None, None))[0],
+                     "traffic_source": ATTN_DRAM_BYTES.get(name, (None, None))[1],
                      "flops_per_step": 3.0 * f_fwd, "peak_source": pk["source"]},
         "attn_tflops": round(attn_tflops, 2),
         "kernels": kernels,
         "gpu_launches": launches,
         "clocks": clocks.summary(),
-        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": x_host.numel() * 4 + d_host.numel() * 2,
-                "d2h_bytes_per_step": g_host.numel() * 4,
-                "pipelining": "step i+1's inputs copied on a second stream while step i computes"},
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if e2e:
+        line["e2e"] = {"value": round(e2e_value, 1), "unit": "tokens/s",
+                       "h2d_bytes_per_step": x_host.numel() * 4 + d_host.numel() * 2,
+                       "d2h_bytes_per_step": g_host.numel() * 4,
+                       "pipelining": "step i+1's inputs copied on a second stream while step i computes"}
+    if cpu and world == 1 and not args.no_cpu_baseline:
         cv, desc, threads, _ = cpu_reference_steps(lengths, 1, args.ref_tokens, hidden=hidden, n_heads=hq, n_kv=hk)
         line["cpu_baseline"] = {"value": round(cv, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
                                 "sample": desc}
-    print(json.dumps(line), flush=True)
+    return line
 
 
-def full_step_lengths(workload: str, rank: int) -> list[int]:
+def run_ours(args, world, rank, local):
+    line = measure_block(args, world, rank, local, args.steps)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def full_step_attn_weight(cfg=None) -> float:
+    """Causal score pairs -> token-equivalents for dp.partition_rows on the full step: attention
+    FLOPs per score pair over the linear-layer FLOPs per token of the 28-layer model (its 7 NF4
+    linears per layer and the head), doubled because the attention kernels run at about half the
+    GEMMs' fraction of peak."""
+    from decik_b200.qlora_model import QWEN25_15B
+
+    c = cfg or QWEN25_15B
+    h, hq, hk, inter, vocab = c["hidden"], c["heads"], c["kv_heads"], c["intermediate"], c["vocab"]
+    per_token = c["layers"] * h * ((hq + 2 * hk) * D + hq * D + 3 * inter) + h * vocab
+    per_pair = c["layers"] * 2 * hq * D
+    return 2.0 * per_pair / per_token
+
+
+def full_step_lengths(workload: str, world: int, rank: int) -> list[int]:
+    """This rank's rows of a full-step workload: one global pool of world x (tokens per GPU) rows
+    (log-normal lengths, seed 1000) split across the ranks by whole rows with dp.partition_rows."""
+    from decik_b200.dp import partition_rows
     from decik_b200.qlora_model import lognormal_lengths
 
     total, median, lo, hi, _ = FULL_STEP[workload]
-    return lognormal_lengths(1000 + rank, total, median, lo, hi)
+    pool = lognormal_lengths(1000, world * total, median, lo, hi)
+    if world == 1:
+        return pool
+    return [pool[i] for i in partition_rows(pool, world, attn_weight=full_step_attn_weight())[rank]]
+
+
+def full_step_flops(lengths, cfg=None) -> float:
+    """Algorithmic FLOPs of one QLoRA train step over these rows: the frozen linears' forward and
+    input-gradient GEMMs (2 x 2 x MACs per token), the head's the same, the LoRA r16 products
+    (forward, input and parameter gradients) and the causal attention (3 x the forward's
+    4 . D . Hq . L(L+1)/2 per layer). The basis of the CPU arm's extrapolation from its sample."""
+    from decik_b200.qlora_model import QWEN25_15B
+
+    c = cfg or QWEN25_15B
+    h, hq, hk, inter, vocab, layers = c["hidden"], c["heads"], c["kv_heads"], c["intermediate"], c["vocab"], c["layers"]
+    T = sum(lengths)
+    lin = layers * h * ((hq + 2 * hk) * D + hq * D + 3 * inter) + h * vocab
+    lora = layers * 16 * (2 * h + (hq + hk) * D)
+    return 4.0 * lin * T + 6.0 * lora * T + layers * 3.0 * causal_flops(lengths, n_heads=hq)
 
 
 def run_full_step(args, world, rank, local):
     """The whole QLoRA train step of the 28-layer model through the reference-facing surface:
-    solution.apply() patches the model; each step is forward + loss + backward (+ the LoRA-grad
-    all-reduce on N > 1) + AdamW."""
+    solution.apply() patches the model; each step is forward + loss + backward + the LoRA-grad
+    all-reduce (N > 1) + AdamW. The rows of one global pool are split across the ranks by
+    dp.partition_rows; the loss is normalised by the global labelled-token count."""
     from decik_b200 import ops, solution
     from decik_b200.dp import GradBucket, global_count
     from decik_b200.qlora_model import (QWEN25_15B, Linear4bit, LoraLinear, build_qlora_qwen2,
@@ -455,19 +547,31 @@ def run_full_step(args, world, rank, local):
     model = build_qlora_qwen2(device=dev, seed=0)
     solution.apply(linear4bit_cls=Linear4bit, lora_classes=(LoraLinear,))
     n_layers = QWEN25_15B["layers"]
-    lengths = full_step_lengths(args.workload, rank)
+    lengths = full_step_lengths(args.workload, world, rank)
     T = sum(lengths)
     ids, mask, labels = padded_batch(lengths, QWEN25_15B["vocab"], 2000 + rank, dev)
     params = lora_parameters(model)
     bucket = GradBucket(params)
+    bucket.check_layout()
     opt = torch.optim.AdamW(params, lr=2e-4)
     # labelled tokens of this step over all ranks (each row's last token has no next-token label)
     n_labels = global_count(torch.tensor(float(T - len(lengths)), device=dev)).to(dev)
+    T_all = int(global_count(torch.tensor(float(T), device=dev)).item())
+    if world > 1:
+        import torch.distributed as dist
+    ar_events = []  # (start, end) around the LoRA-gradient all-reduce of each timed step
 
-    def step(i_ids, i_mask, i_labels):
+    def step(i_ids, i_mask, i_labels, time_ar=False):
         bucket.zero_()
         loss = qlora_train_step(model, i_ids, i_mask, i_labels, n_labels=n_labels)
-        bucket.all_reduce()
+        if time_ar:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            bucket.all_reduce()
+            b.record()
+            ar_events.append((a, b))
+        else:
+            bucket.all_reduce()
         opt.step()
         return loss
 
@@ -475,7 +579,6 @@ def run_full_step(args, world, rank, local):
         step(ids, mask, labels)
     torch.cuda.synchronize()
     if world > 1:
-        import torch.distributed as dist
         dist.barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -484,18 +587,24 @@ def run_full_step(args, world, rank, local):
     with ClockSampler(local) as clocks:
         for i in range(args.steps):
             starts[i].record()
-            step(ids, mask, labels)
+            step(ids, mask, labels, time_ar=True)
             ends[i].record()
         torch.cuda.synchronize()
     ops.install_timer(None)
     op_ms = timer.elapsed_ms()
     step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    ar_ms = statistics.mean(a.elapsed_time(b) for a, b in ar_events) if ar_events else 0.0
     total_ms = sum(step_ms)
+    rank_ms = [total_ms / args.steps]
     if world > 1:
-        t = torch.tensor([total_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
-    value = world * T * args.steps / (total_ms / 1e3)
+        every = [torch.zeros(2, device=dev) for _ in range(world)]
+        dist.all_gather(every, torch.tensor([total_ms / args.steps, ar_ms], device=dev))
+        rank_ms = [float(e[0]) for e in every]
+        rank_ar = [float(e[1]) for e in every]
+        total_ms = max(rank_ms) * args.steps
+    else:
+        rank_ar = [ar_ms]
+    value = T_all * args.steps / (total_ms / 1e3)
 
     # end to end: each step's token ids, mask and labels copied from pinned host memory and its loss
     # read back into pinned host memory, all inside the timed region
@@ -520,7 +629,13 @@ def run_full_step(args, world, rank, local):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+    e2e_value = T_all * args.steps / (e2e_ms / 1e3)
+
+    # the block step of config 3 (the path alone, L2 flushed between steps), as an extra key
+    block = None
+    if not args.no_block:
+        block = measure_block(args, world, rank, local, min(args.steps, 20), workload="config3", e2e=False,
+                              cpu=False)
     if rank != 0:
         return
     pk = peaks()
@@ -535,17 +650,22 @@ def run_full_step(args, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded log-normal lengths, uniform token ids, random-init NF4 weights and LoRA)",
-        "config": {"workload": workload, "tokens_per_gpu": T, "rows_rank0": len(lengths),
-                   "lengths": f"log-normal median {median} sigma 1 in [{lo},{hi}], numpy default_rng(1000 + rank)",
+        "config": {"workload": workload, "tokens_per_gpu": T, "tokens_all_ranks": T_all, "rows_rank0": len(lengths),
+                   "lengths": f"log-normal median {median} sigma 1 in [{lo},{hi}]: one pool of N x {total} tokens "
+                              "(numpy default_rng(1000)) split across ranks by dp.partition_rows",
                    "model": "Qwen2.5-1.5B shape: 28 layers, hidden 1536, inter 8960, 12/2 heads, vocab 151936",
                    "lora": "r16 alpha32 q,v", "nf4": "bs64, double quant bs256 (all 7 linears per layer)",
                    "l2": "not flushed: each step streams the 0.7 GB of NF4 weights and the 0.9 GB embedding (> L2)",
                    "parallelism": f"dp{world}"},
         "roofline": {"bound": "tensor", "kernel": "varlen attention fwd+bwd of the 28 layers (decik_varlen_attn_fwd/bwd)",
-                     "achieved": round(attn_tflops, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": round(attn_tflops / pk["bf16_tflops"], 4), "traffic": None,
-                     "flops_per_step": 3.0 * f_fwd, "peak_source": pk["source"]},
+                     "achieved": round(attn_tflops, 2), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": round(attn_tflops / pk["bf16_tflops_sustained"], 4), "traffic": None,
+                     "flops_per_step": 3.0 * f_fwd,
+                     "peak_source": pk["source_sustained"]},
         "attn_tflops": round(attn_tflops, 2),
+        "rank_ms_per_step": [round(v, 3) for v in rank_ms],
+        "allreduce_ms_per_step": [round(v, 4) for v in rank_ar],
+        "allreduce_bytes": bucket.nbytes,
         "kernels": kernels,
         "gpu_launches": timer.launches,
         "clocks": clocks.summary(),
@@ -554,6 +674,12 @@ def run_full_step(args, world, rank, local):
                 "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (h_ids, h_mask, h_labels)),
                 "d2h_bytes_per_step": 4},
     }
+    if block is not None:
+        line["block_config3"] = {k: block[k] for k in ("value", "ms_per_step", "roofline", "kernels", "config")}
+    if world == 1 and not args.no_cpu_baseline:
+        cv, cv_sample, desc, threads, _ = cpu_full_step(args.workload, lengths, 2, args.full_ref_tokens)
+        line["cpu_baseline"] = {"value": round(cv, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": desc, "sample_value": round(cv_sample, 3)}
     print(json.dumps(line), flush=True)
     if args.profile and world == 1:  # one GPU only: a step would all-reduce with ranks that have left
         from torch.profiler import ProfilerActivity, profile
@@ -567,68 +693,109 @@ def run_full_step(args, world, rank, local):
               flush=True)
 
 
-def run_reference_full(args, world, rank):
-    """The reference's CPU path for the full step: the same model on the host in fp32 with the
-    original transformers code (no patches), NF4 weights dequantised by the torch restatement of
-    solution/nf4.py:36-48 each call; a bounded sample of the first rows of the workload."""
-    if rank != 0:
-        return
+def cpu_full_step(workload, lengths, n_steps, sample_tokens, warmup=0, budget_s=None):
+    """The reference's CPU path for the full step, timed on bounded samples: the same model on the
+    host in fp32 with the original transformers code (no patches), NF4 weights dequantised by the
+    torch restatement of solution/nf4.py:36-48 on every call, over the first rows of ``lengths``
+    cut to a sample. The timed steps alternate between two samples (``sample_tokens`` / 4 and
+    ``sample_tokens``) so that the step time can be split into a part fixed per step (the NF4
+    dequant of every linear call, the optimizer) and a part proportional to the step's FLOPs
+    (full_step_flops); that affine fit extrapolates the step time to ``lengths``. ``budget_s``
+    stops the timed steps early (at least two) once their time would pass it.
+    Returns (tokens/s of ``lengths`` extrapolated, tokens/s of the larger sample, description,
+    threads, step times)."""
     from decik_b200.qlora_model import (QWEN25_15B, Linear4bit, build_qlora_qwen2, lora_parameters,
                                         padded_batch, qlora_train_step)
     from oracle.block import dequant_torch_qs
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    *_, workload = FULL_STEP[args.workload]
     t_build = time.perf_counter()
     model = build_qlora_qwen2(device="cpu", seed=0, share_layer_weights=True)
     build_s = time.perf_counter() - t_build
+    original = Linear4bit.forward
 
     def cpu_forward(self, x):
         w = dequant_torch_qs(self.weight.data, self.weight.quant_state)
         return torch.nn.functional.linear(x.float(), w, None if self.bias is None else self.bias.float())
 
-    Linear4bit.forward = cpu_forward
-    lengths = full_step_lengths(args.workload, 0)
-    opt = torch.optim.AdamW(lora_parameters(model), lr=2e-4)
-
-    def run(sample_tokens, n):
+    def first_rows(n_tok):
         rows, t = [], 0
         for L in lengths:
-            if t >= sample_tokens:
+            if t >= n_tok:
                 break
-            rows.append(min(L, sample_tokens - t))
+            rows.append(min(L, n_tok - t))
             t += rows[-1]
-        ids, mask, labels = padded_batch(rows, QWEN25_15B["vocab"], 2000, "cpu")
-        times = []
-        for _ in range(n):
+        return rows
+
+    samples = [first_rows(max(8, sample_tokens // 4)), first_rows(sample_tokens)]
+    batches = [padded_batch(rows, QWEN25_15B["vocab"], 2000, "cpu") for rows in samples]
+    Linear4bit.forward = cpu_forward
+    times = {0: [], 1: []}
+    all_times = []
+    try:
+        opt = torch.optim.AdamW(lora_parameters(model), lr=2e-4)
+        n_run = 0
+        for i in range(warmup + max(n_steps, 2)):
+            which = i % 2
             t0 = time.perf_counter()
             model.zero_grad(set_to_none=True)
-            qlora_train_step(model, ids, mask, labels)
+            qlora_train_step(model, *batches[which])
             opt.step()
-            times.append(time.perf_counter() - t0)
-        return rows, times
+            dt = time.perf_counter() - t0
+            if i >= warmup:
+                times[which].append(dt)
+                all_times.append(dt)
+                n_run += 1
+                if (budget_s is not None and n_run >= 2 and n_run < n_steps
+                        and sum(all_times) * (n_run + 1) / n_run > budget_s):
+                    break
+    finally:
+        Linear4bit.forward = original
+    t_small, t_large = statistics.mean(times[0]), statistics.mean(times[1])
+    f_small, f_large, f_full = (full_step_flops(r) for r in (samples[0], samples[1], lengths))
+    per_flop = (t_large - t_small) / (f_large - f_small) if f_large > f_small else 0.0
+    if per_flop > 0:
+        fixed = max(0.0, t_large - per_flop * f_large)
+        full_s = fixed + per_flop * f_full
+        how = (f"affine fit over the two samples: {fixed:.2f} s per step fixed + {per_flop * 1e12:.2f} s per "
+               f"TFLOP x {f_full / 1e12:.1f} TFLOP (full_step_flops of the workload)")
+    else:  # the two samples did not separate: proportional to FLOPs from the larger one
+        full_s = t_large * f_full / f_large
+        how = f"larger sample's step time x FLOP ratio {f_full / f_large:.1f} (full_step_flops)"
+    value = sum(lengths) / full_s
+    sample_value = sum(samples[1]) / t_large
+    desc = (f"two samples of the workload's first rows timed alternately ({sum(samples[0])} tokens: "
+            f"{t_small:.2f} s/step, {sum(samples[1])} tokens: {t_large:.2f} s/step; {len(all_times)} steps): full "
+            f"28-layer step fwd+bwd+AdamW in fp32 with NF4 dequant per call, frozen NF4 weights shared by the "
+            f"layers (model build {build_s:.0f} s, untimed); value = the workload's {sum(lengths)} tokens / "
+            f"{full_s:.1f} s, the step time extrapolated by an {how}")
+    return value, sample_value, desc, threads, all_times
 
-    sample = min(args.ref_tokens, 256)
-    if args.warmup:
-        _, warm = run(sample, 1)
-        if args.steps * warm[0] > REF_BUDGET_S:
-            sample = max(16, int(sample * REF_BUDGET_S / (args.steps * warm[0])))
-    rows, times = run(sample, args.steps)
-    value = sum(rows) / statistics.mean(times)
-    desc = (f"{len(rows)} rows, {sum(rows)} tokens (first rows of the packing), full 28-layer step fwd+bwd+AdamW, "
-            f"fp32, frozen NF4 weights shared by the layers (model build {build_s:.0f} s, untimed)")
-    line = {"metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "impl": "reference",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+
+def run_reference_full(args, world, rank):
+    """The reference arm for the full step: the reference's CPU path (cpu_full_step) on rank 0,
+    with the value extrapolated from its timed sample to this configuration's rows by FLOPs."""
+    if rank != 0:
+        return
+    *_, workload = FULL_STEP[args.workload]
+    lengths = full_step_lengths(args.workload, 1, 0)
+    value, sample_value, desc, threads, times = cpu_full_step(args.workload, lengths, args.steps,
+                                                              args.full_ref_tokens, warmup=min(args.warmup, 1),
+                                                              budget_s=REF_BUDGET_S)
+    line = {"metric": METRIC, "value": round(value, 4), "unit": "tokens/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": len(times), "warmup": min(args.warmup, 1),
+            "steps_note": f"{len(times)} of the {args.steps} requested timed CPU steps ran (stopped at the "
+                          f"{REF_BUDGET_S:.0f} s CPU budget, at least 2); one warm-up step",
             "ms_per_step": round(1e3 * statistics.mean(times), 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": workload.replace("through solution.apply()",
-                                                    "on the original transformers code with torch NF4 dequant")
-                       + " (bounded CPU sample)", "tokens_per_gpu": sum(lengths), "sample": desc,
-                       "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                                                    "on the original transformers code with torch NF4 dequant"),
+                       "tokens_per_gpu": sum(lengths), "sample": desc, "parallelism": "cpu",
+                       "extrapolated": True, "sample_value": round(sample_value, 3)},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": desc},
-            "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -639,19 +806,22 @@ def main():
     ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 10; 1 with --impl reference)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ref-tokens", type=int, default=4096, help="tokens of the bounded CPU sample")
+    ap.add_argument("--full-ref-tokens", type=int, default=128,
+                    help="tokens of the bounded CPU sample of the full step (cpu_baseline and --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-block", action="store_true", help="full step: skip the extra config-3 block measurement")
     ap.add_argument("--profile", action="store_true",
                     help="full-step workloads, one GPU: after the JSON line, one more step under torch.profiler; "
                          "its device-time and host-time tables go to stderr")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(FULL_STEP), default="config3",
-                    help="config3: the 1.5B block over 16,384 tokens (default); config4: the 7B block over "
-                         "131,072; config2 / config5: the full 28-layer QLoRA train step over ~830 / "
-                         "16,384 tokens per GPU")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(FULL_STEP), default="config5",
+                    help="config5: the full 28-layer QLoRA train step over 16,384 tokens per GPU (default, "
+                         "with the config-3 block step as an extra key); config2: the same over ~830 tokens; "
+                         "config3: the 1.5B attention block over 16,384 tokens; config4: the 7B block over 131,072")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 10 if args.impl == "reference" else 100
+        args.steps = 10 if args.impl == "reference" else (20 if args.workload in FULL_STEP else 100)
     if args.warmup is None:
-        args.warmup = 1 if args.impl == "reference" else 10
+        args.warmup = 1 if args.impl == "reference" else (5 if args.workload in FULL_STEP else 10)
     world, rank, local = dist_setup()
     try:
         if args.workload in FULL_STEP:

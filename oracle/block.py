@@ -46,18 +46,23 @@ def dequant_torch(state: dict) -> torch.Tensor:
 
 def dequant_torch_qs(packed: torch.Tensor, qs) -> torch.Tensor:
     """fp32 [N, K] weights from packed uint8 bytes and a QuantState-like object (fields absmax,
-    code, blocksize, shape, nested, state2.{absmax, code, blocksize}, offset), the same torch ops
-    as dequant_torch (solution/nf4.py:36-48)."""
+    code, blocksize, shape, nested, state2.{absmax, code, blocksize}, offset): the arithmetic of
+    dequant_torch (solution/nf4.py:36-48: per block scale = code2[absmax] * absmax2, then
+    + offset; each weight code[nibble] * scale in fp32, high nibble first), vectorised per byte
+    and per block as a CPU dequant would be: a 256-entry table gives each byte's two codes, and one
+    scale per block multiplies its bytes."""
     p = packed.reshape(-1).to(torch.int64)
     bs = int(qs.blocksize)
-    block = (torch.arange(p.numel(), dtype=torch.int64, device=p.device) * 2) // bs
+    n_blocks = (p.numel() * 2) // bs
+    byte = torch.arange(256, device=p.device)
+    pair = torch.stack((qs.code[byte >> 4], qs.code[byte & 15]), dim=1)  # [256, 2]: (hi, lo)
     if qs.nested:
-        q = qs.absmax.to(torch.int64)
-        scale = qs.state2.code[q[block]] * qs.state2.absmax[block // int(qs.state2.blocksize)]
+        blk = torch.arange(n_blocks, device=p.device)
+        scale = qs.state2.code[qs.absmax.to(torch.int64)] * qs.state2.absmax[blk // int(qs.state2.blocksize)]
         scale = scale + qs.offset.reshape(-1)[0]
     else:
-        scale = qs.absmax[block]
-    w = torch.stack((qs.code[p >> 4] * scale, qs.code[p & 15] * scale), dim=1)
+        scale = qs.absmax
+    w = pair[p].view(n_blocks, bs // 2, 2) * scale.view(n_blocks, 1, 1)
     return w.reshape(qs.shape)
 
 

@@ -483,18 +483,19 @@ def test_varlen_attention_config4_full_size(cuda_lib):
         _close_gpu(a[s:s + L], e[s:s + L], f"{name} of the 32,768-token row")
 
 
-@pytest.mark.parametrize("rank", range(8))
-def test_varlen_attention_bench_packings_every_row(cuda_lib, rank):
-    """The packings bench.py's block step times on ranks 0-7 (bench.lengths_for(1000 + rank): 16,384
-    tokens, rows up to 4,096), 12 / 2 heads, bf16, q and k head-major as the projection epilogue
-    writes them. This runs the launch order the bench runs (the heavy-first persistent forward and
-    the head-split backward with fp32 dK / dV partials). Every row of out, lse, dq, dk and dv is
+@pytest.mark.parametrize("world,rank", [(1, 0)] + [(8, r) for r in range(8)])
+def test_varlen_attention_bench_packings_every_row(cuda_lib, world, rank):
+    """The packings bench.py's config-3 block step times: at N = 1 and on each of the 8 ranks at
+    N = 8 (bench.block_lengths: one pool of N x 16,384 tokens, rows U[64, 4096], split by
+    dp.partition_rows), 12 / 2 heads, bf16, q and k head-major as the projection epilogue writes
+    them. This runs the launch order the bench runs (the heavy-first persistent forward and the
+    head-split backward with fp32 dK / dV partials). Every row of out, lse, dq, dk and dv is
     checked against the fp32 restatement: the bar holds for the whole packing and for each row."""
-    from bench import lengths_for
+    from bench import block_lengths
 
     ops = _ops()
-    lengths = lengths_for(1000 + rank)
-    assert sum(lengths) == 16384
+    lengths = block_lengths("config3", world, rank)
+    assert abs(sum(lengths) - 16384) < 4096
     spans, cu, q, k, v, do = _attn_case(lengths, 12, 2, torch.bfloat16, seed=50 + rank, layout="ref")
     scale = 128 ** -0.5
     out, lse = ops.varlen_attn_fwd(q, k, v, cu, max(lengths), scale)
@@ -514,16 +515,16 @@ def test_varlen_attention_bench_packings_every_row(cuda_lib, rank):
             _close_gpu(a[s:s + L], e[s:s + L], f"{name} of row {i} (length {L})")
 
 
-@pytest.mark.parametrize("rank", [0, 3])
-def test_attn_qkv_bwd_bench_packing_every_row(cuda_lib, rank):
+@pytest.mark.parametrize("world,rank", [(1, 0), (8, 3)])
+def test_attn_qkv_bwd_bench_packing_every_row(cuda_lib, world, rank):
     """The one-call backward the fused block runs (decik_attn_qkv_bwd: attention backward, then the
     projection epilogue reading its fp32 accumulators) on a bench packing. With cos = 1 and sin = 0
     RoPE^T is the identity, so dy's q, k and v columns are dq, dk and dv rounded to bf16: every row
     is checked against the fp32 restatement."""
-    from bench import lengths_for
+    from bench import block_lengths
 
     ops = _ops()
-    lengths = lengths_for(1000 + rank)
+    lengths = block_lengths("config3", world, rank)
     T, HQ, HK, D = sum(lengths), 12, 2, 128
     spans, cu, q, k, v, do = _attn_case(lengths, HQ, HK, torch.bfloat16, seed=70 + rank, layout="ref")
     scale = D ** -0.5
