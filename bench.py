@@ -806,7 +806,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=None, help="untimed steps (default 10; 1 with --impl reference)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ref-tokens", type=int, default=4096, help="tokens of the bounded CPU sample")
-    ap.add_argument("--full-ref-tokens", type=int, default=128,
+    ap.add_argument("--full-ref-tokens", type=int, default=512,
                     help="tokens of the bounded CPU sample of the full step (cpu_baseline and --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-block", action="store_true", help="full step: skip the extra config-3 block measurement")
