@@ -1,0 +1,712 @@
+// The projection GEMMs of the attention block on the 5th-generation tensor cores (tcgen05 + TMEM,
+// operands staged by TMA), with the work around them fused in. They replace the cuBLAS calls of
+// the block: the forward's q|k|v|LoRA-down F.linear and the backward's dX / dA / dB products
+// (the three NF4Linear GEMMs of the reference, solution/nf4.py:93-104, and the LoRA branch's
+// matmuls, solution/attn.py:217-273).
+//
+// Forward, two kernels:
+// 1. x_cast_lora_down_kernel: x fp32 [T, H] -> x16 = dt(x) [T, H] and u = dt(x16 [A_q; A_v]^T)
+//    [T, 32] (the reference's lora_A products, solution/attn.py:225-227) in one pass over x: the
+//    cast has to read x anyway, and the rank-32 product rides along on mma.sync.
+// 2. proj_gemm_kernel<EPI_QKV>: y = x16 [W_q; W_k; W_v]^T on tcgen05, tile 128 tokens x 256
+//    outputs (two heads), K-major A and B from TMA, fp32 accumulators in TMEM (two buffers, so a
+//    tile's epilogue overlaps the next tile's MMAs). The epilogue is the projection epilogue
+//    of qkv.cu applied straight to the accumulators: + bias rounded to dt (F.linear with bias),
+//    LoRA-up dt(dt(u B16^T) * scaling) on q and v, v = dt(base + lora), RoPE with separate
+//    roundings and no FMA (solution/attn.py:39-60) on q and k, and the head-major q / k and
+//    token-major v tiles leave through shared memory by TMA stores. y never reaches HBM.
+// Backward:
+// 3. proj_gemm_kernel<EPI_F32>: dx = dy W_cat (dy [T, 2080] K-major, W_cat [2080, H] read
+//    MN-major), fp32 out by TMA stores: the three NF4Linear input gradients and both LoRA input
+//    gradients summed in one product (K = 2080, the tail zero-filled by TMA).
+// 4. lora_grad_kernel: dA = du^T x16 [32, H] and dB = scaling g^T u [(Hq + Hk) 128, 16] as
+//    token-chunked mma.sync products reduced into fp32 outputs (red.global.add).
+//
+// GEMM kernel roles (12 warps, one CTA per SM, persistent over tiles in n-fastest order so the
+// CTAs running together share their A row tiles in L2): warp 0 TMA producer (one thread), warp 1
+// TMEM allocation and the single-thread tcgen05.mma issue, warps 2-3 idle, warps 4-11 the
+// epilogue (warp w reads TMEM lanes 32 (w % 4) .. + 31; warps 4-7 take the first half of the
+// tile's columns, 8-11 the second). Every mbarrier wait is bounded (sm100::mbar_wait): one that
+// gives up records a code in the error word and the CTA winds down.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <type_traits>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "sm100.cuh"
+
+namespace decik {
+namespace attn {
+int* attn_error_word();
+int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
+                  int n_heads, int dtype, int* order, int box_rows);
+int make_map_2d(CUtensorMap* map, const void* ptr, int dtype, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                uint32_t box_inner, uint32_t box_outer);
+}  // namespace attn
+
+namespace proj {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BK = 64, NTHREADS = 384, kEpiWarps = 8, kD = 128, kR = 16;
+enum { EPI_QKV = 0, EPI_F32 = 1 };
+
+template <int EPI> struct Cfg;
+template <> struct Cfg<EPI_QKV> {  // two heads per tile
+  static constexpr int BN = 256, STAGES = 3;
+  static constexpr bool B_MN = false;
+};
+template <> struct Cfg<EPI_F32> {  // 1536 / 192 = 8 column tiles: 1024 tiles at 16,384 tokens = 6.9 waves
+  static constexpr int BN = 192, STAGES = 4;
+  static constexpr bool B_MN = true;
+};
+
+template <int EPI>
+struct Layout {
+  static constexpr int BN = Cfg<EPI>::BN, S = Cfg<EPI>::STAGES;
+  static constexpr int A_BYTES = BM * BK * 2;  // 128 rows x 128 B, 128-byte swizzle
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = S * A_BYTES;
+  static constexpr int OFF_STG = OFF_B + S * B_BYTES;  // per epilogue warp: two 4 KB staging tiles
+  static constexpr int STG_WARP = 8192;
+  static constexpr int OFF_B16 = OFF_STG + kEpiWarps * STG_WARP;  // QKV: lora_B rows of the tile's 2 heads
+  static constexpr int B16_BYTES = EPI == EPI_QKV ? 2 * kD * kR * 2 : 0;
+  static constexpr int OFF_BIAS = OFF_B16 + B16_BYTES;  // QKV: fp32 bias of the tile's 2 heads
+  static constexpr int BIAS_BYTES = EPI == EPI_QKV ? 2 * kD * 4 : 0;
+  static constexpr int OFF_BAR = OFF_BIAS + BIAS_BYTES;
+  static constexpr int N_BAR = 2 * S + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], done
+  static constexpr int OFF_TMEM = OFF_BAR + 8 * N_BAR;
+  static constexpr int SMEM = OFF_TMEM + 16 + 1024;  // + slack for the 1024-byte alignment
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+  static_assert(OFF_STG % 1024 == 0, "staging tiles need the swizzle atom's alignment");
+};
+
+struct Params {
+  CUtensorMap ta, tb;     // A [M, K] K-major; B [N, K] K-major or [K, N] (MN-major)
+  CUtensorMap to[3];      // EPI_QKV: q, k, v tile maps; EPI_F32: the fp32 output
+  int order[3];           // tile-map coordinate order of q, k, v (0: d, tok, head; 1: d, head, tok)
+  int64_t M;
+  int N, K, n_tiles_n, n_tiles;
+  const void* bias;       // EPI_QKV: 16-bit [N]
+  const void* u;          // EPI_QKV: 16-bit [M, 32] (u_q | u_v), NULL without LoRA
+  int64_t ldu;
+  const void* b16;        // EPI_QKV: 16-bit [(hq + hk) * 128, 16]: lora_B of q then v
+  float scaling;
+  const float* cosp;
+  const float* sinp;
+  int hq, hk;
+  int* err;
+};
+
+template <typename T>
+__device__ __forceinline__ float rnd(float x) {
+  return Dt<T>::to_f(Dt<T>::from_f(x));
+}
+
+// dt(dt(u . B[d]) * scaling): the LoRA-up value of output column d (B rows staged in shared memory)
+template <typename T>
+__device__ __forceinline__ float lora_up(const float (&u)[kR], const uint4* brow, float scaling) {
+  const uint4 w0 = brow[0], w1 = brow[1];
+  float b[16];
+  unpack8<T>(w0, *reinterpret_cast<float(*)[8]>(&b[0]));
+  unpack8<T>(w1, *reinterpret_cast<float(*)[8]>(&b[8]));
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < kR; ++j) acc = fmaf(u[j], b[j], acc);
+  return rnd<T>(__fmul_rn(rnd<T>(acc), scaling));
+}
+
+template <typename T, int EPI>
+__global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_constant__ Params p) {
+  using L = Layout<EPI>;
+  constexpr int BN = L::BN, S = L::S;
+  constexpr bool BMN = Cfg<EPI>::B_MN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const auto full = [&](int s) { return sb + L::OFF_BAR + 8 * s; };
+  const auto empty = [&](int s) { return sb + L::OFF_BAR + 8 * (S + s); };
+  const auto acc_full = [&](int b) { return sb + L::OFF_BAR + 8 * (2 * S + b); };
+  const auto acc_empty = [&](int b) { return sb + L::OFF_BAR + 8 * (2 * S + 2 + b); };
+  const uint32_t done = sb + L::OFF_BAR + 8 * (2 * S + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), kEpiWarps);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(sb + L::OFF_TMEM, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::OFF_TMEM);
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&p.ta);
+      prefetch_tmap(&p.tb);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / p.n_tiles_n) * BM, n0 = (tile % p.n_tiles_n) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = static_cast<int>(it % S);
+          if (it >= static_cast<uint32_t>(S) && !(ok = mbar_wait(empty(s), ((it / S) - 1) & 1, p.err, 301))) break;
+          mbar_expect_tx(full(s), L::A_BYTES + L::B_BYTES);
+          tma_load_2d(sb + L::OFF_A + s * L::A_BYTES, &p.ta, full(s), kb * BK, m0);
+          if constexpr (!BMN) {
+            tma_load_2d(sb + L::OFF_B + s * L::B_BYTES, &p.tb, full(s), kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + L::OFF_B + s * L::B_BYTES + j * (64 * BK * 2), &p.tb, full(s), n0 + 64 * j, kb * BK);
+          }
+        }
+      }
+      // wind down: the loads in flight land before the CTA leaves
+      for (uint32_t j = it > static_cast<uint32_t>(S) ? it - S : 0; j < it; ++j)
+        mbar_wait(full(static_cast<int>(j % S)), (j / S) & 1, p.err, 302);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issue (one thread)
+    if (lane == 0) {
+      constexpr int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      const uint32_t idesc = idesc_f16(ab, BM, BN, 0, BMN ? 1 : 0);
+      uint32_t it = 0;
+      int i = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !(ok = mbar_wait(acc_empty(b), ((i >> 1) - 1) & 1, p.err, 311))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * 256;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = static_cast<int>(it % S);
+          if (!(ok = mbar_wait(full(s), (it / S) & 1, p.err, 312))) break;
+          tc_fence_after();
+          const uint32_t a = sb + L::OFF_A + s * L::A_BYTES, bb = sb + L::OFF_B + s * L::B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(a + kk * 32, 16, 1024);
+            const uint64_t bd = BMN ? smem_desc_sw128(bb + kk * 2048, 64 * BK * 2, 1024)
+                                    : smem_desc_sw128(bb + kk * 32, 16, 1024);
+            umma_ss(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(empty(s));
+        }
+        if (!ok) break;
+        umma_commit(acc_full(b));
+      }
+      // every MMA this thread issued has completed before TMEM is freed
+      umma_commit(done);
+      mbar_wait(done, 0, p.err, 313);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int ew = warp - 4, wg = ew >> 2, q4 = warp & 3;
+    uint8_t* stg = smem + L::OFF_STG + ew * L::STG_WARP;
+    const uint32_t stg_s = sb + L::OFF_STG + ew * L::STG_WARP;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * q4) << 16;
+    uint32_t n_chunks = 0;  // EPI_F32: staging tiles used so far (double buffer)
+    int i = 0;
+    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++i) {
+      const int m0 = (tile / p.n_tiles_n) * BM, n0 = (tile % p.n_tiles_n) * BN;
+      const int b = i & 1;
+      bool ok = mbar_wait(acc_full(b), (i >> 1) & 1, p.err, 321);
+      // EPI_QKV: the warpgroup leaves together (it meets at named barriers below), and this barrier
+      // also orders the previous tile's reads of bias_s / b16_s before they are rewritten
+      if constexpr (EPI == EPI_QKV) ok = named_bar_and(1 + wg, 128, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem + lane_base + b * 256;
+      const int64_t row0 = m0 + 32 * q4;
+      const int64_t r = row0 + lane;
+      if constexpr (EPI == EPI_F32) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32, ++n_chunks) {
+          const int col = wg * (BN / 2) + c;
+          uint32_t v[32];
+          tmem_ld32(tacc + col, v);
+          tmem_ld_wait();
+          if (lane == 0) bulk_wait_read1();  // the store that last used this buffer has read it
+          __syncwarp();
+          uint8_t* row = stg + (n_chunks & 1) * 4096 + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < p.M && n0 + col < p.N)
+              tma_store_2d(&p.to[0], stg_s + (n_chunks & 1) * 4096, n0 + col, static_cast<int>(row0));
+            bulk_commit();  // one group per chunk, stored or not: the wait above counts groups
+          }
+        }
+      } else {
+        const int hh = n0 / kD + wg;  // head of this warpgroup: q heads, then k, then v
+        const int kind = hh < p.hq ? 0 : (hh < p.hq + p.hk ? 1 : 2);
+        const bool lora = p.b16 != nullptr && kind != 1;
+        const bool rope = kind != 2;
+        const int tid = threadIdx.x - 128 - 128 * wg;  // 0..127 in the warpgroup
+        float* bias_s = reinterpret_cast<float*>(smem + L::OFF_BIAS) + wg * kD;
+        uint4* b16_s = reinterpret_cast<uint4*>(smem + L::OFF_B16 + wg * kD * kR * 2);
+        bias_s[tid] = Dt<T>::to_f(static_cast<const T*>(p.bias)[hh * kD + tid]);
+        if (lora) {
+          const int slot = kind == 0 ? hh : p.hq + (hh - p.hq - p.hk);
+          const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.b16) + (slot * kD + tid) * kR);
+          b16_s[2 * tid] = __ldg(src);
+          b16_s[2 * tid + 1] = __ldg(src + 1);
+        }
+        named_bar(1 + wg, 128);
+        float u[kR];
+#pragma unroll
+        for (int j = 0; j < kR; ++j) u[j] = 0.f;
+        if (lora && r < p.M) {
+          const uint4* up = reinterpret_cast<const uint4*>(static_cast<const T*>(p.u) + r * p.ldu + (kind == 2 ? kR : 0));
+          unpack8<T>(__ldg(up), *reinterpret_cast<float(*)[8]>(&u[0]));
+          unpack8<T>(__ldg(up + 1), *reinterpret_cast<float(*)[8]>(&u[8]));
+        }
+        const int64_t rc = r < p.M ? r : p.M - 1;  // cos / sin row (rows past the end are not stored)
+        const float* cs = p.cosp + rc * kD;
+        const float* sn = p.sinp + rc * kD;
+        if (lane == 0) bulk_wait_read0();  // this warp's previous stores have read the staging tiles
+        __syncwarp();
+#pragma unroll 1
+        for (int c = 0; c < kD / 2; c += 16) {
+          uint32_t alo[16], ahi[16];
+          tmem_ld16(tacc + wg * kD + c, alo);
+          tmem_ld16(tacc + wg * kD + c + kD / 2, ahi);
+          tmem_ld_wait();
+          float olo[16], ohi[16];
+#pragma unroll
+          for (int e4 = 0; e4 < 16; e4 += 4) {
+            float4 cl = make_float4(0.f, 0.f, 0.f, 0.f), ch = cl, sl = cl, sh = cl;
+            if (rope) {
+              cl = __ldg(reinterpret_cast<const float4*>(cs + c + e4));
+              ch = __ldg(reinterpret_cast<const float4*>(cs + c + e4 + kD / 2));
+              sl = __ldg(reinterpret_cast<const float4*>(sn + c + e4));
+              sh = __ldg(reinterpret_cast<const float4*>(sn + c + e4 + kD / 2));
+            }
+            const float cla[4] = {cl.x, cl.y, cl.z, cl.w}, cha[4] = {ch.x, ch.y, ch.z, ch.w};
+            const float sla[4] = {sl.x, sl.y, sl.z, sl.w}, sha[4] = {sh.x, sh.y, sh.z, sh.w};
+#pragma unroll
+            for (int e1 = 0; e1 < 4; ++e1) {
+              const int e = e4 + e1, d = c + e;
+              float lo = rnd<T>(__fadd_rn(__uint_as_float(alo[e]), bias_s[d]));
+              float hi = rnd<T>(__fadd_rn(__uint_as_float(ahi[e]), bias_s[d + kD / 2]));
+              if (lora) {
+                lo = __fadd_rn(lo, lora_up<T>(u, b16_s + 2 * d, p.scaling));
+                hi = __fadd_rn(hi, lora_up<T>(u, b16_s + 2 * (d + kD / 2), p.scaling));
+              }
+              if (rope) {
+                // d < D/2: x[d] cos[d] + (-x[d + D/2]) sin[d];  d + D/2: x[d + D/2] cos + x[d] sin
+                olo[e] = __fadd_rn(__fmul_rn(lo, cla[e1]), __fmul_rn(-hi, sla[e1]));
+                ohi[e] = __fadd_rn(__fmul_rn(hi, cha[e1]), __fmul_rn(lo, sha[e1]));
+              } else {
+                olo[e] = lo;
+                ohi[e] = hi;
+              }
+            }
+          }
+          // this row's 16 + 16 values into the two [32 rows x 64] halves (128-byte swizzle)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int chunk = c / 8 + j;
+            const int off = lane * 128 + ((chunk ^ (lane & 7)) << 4);
+            *reinterpret_cast<uint4*>(stg + off) = pack8<T>(*reinterpret_cast<const float(*)[8]>(&olo[8 * j]));
+            *reinterpret_cast<uint4*>(stg + 4096 + off) = pack8<T>(*reinterpret_cast<const float(*)[8]>(&ohi[8 * j]));
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0 && row0 < p.M) {
+          const int head = kind == 0 ? hh : (kind == 1 ? hh - p.hq : hh - p.hq - p.hk);
+          const CUtensorMap* map = &p.to[kind];
+          const int t = static_cast<int>(row0);
+          if (p.order[kind] == 0) {
+            tma_store_3d(map, stg_s, 0, t, head);
+            tma_store_3d(map, stg_s + 4096, kD / 2, t, head);
+          } else {
+            tma_store_3d(map, stg_s, 0, head, t);
+            tma_store_3d(map, stg_s + 4096, kD / 2, head, t);
+          }
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(b));
+    }
+    if (lane == 0) bulk_wait0();  // the stores have finished before the CTA leaves
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// x fp32 -> x16, u = dt(x16 [A_q; A_v]^T)
+// ------------------------------------------------------------------------------------------------
+constexpr int kCastTok = 64, kCastThreads = 256, kCastLd = 64 + 8;  // padded shared rows (16-bit)
+
+template <typename T>
+__global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const float* __restrict__ x, int64_t ldx,
+                                                                        const T* __restrict__ a16, int64_t lda,
+                                                                        T* __restrict__ x16, int64_t ldx16,
+                                                                        T* __restrict__ u, int64_t n_tok, int hidden) {
+  __shared__ __align__(16) T xs[kCastTok * kCastLd];
+  __shared__ __align__(16) T as[2 * kR * kCastLd];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kCastTok;
+  const bool lora = u != nullptr;
+  // each thread moves 4 float4 per 64-column chunk: rows (tid >> 4) + 16 i, columns 4 (tid & 15)
+  const int cc = 4 * (tid & 15), rr = tid >> 4;
+  float4 cur[4], nxt[4];
+  auto load = [&](int k0, float4 (&dst)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t t = t0 + rr + 16 * i;
+      dst[i] = t < n_tok ? __ldg(reinterpret_cast<const float4*>(x + t * ldx + k0 + cc)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  float acc[2][4];
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+  load(0, cur);
+  for (int k0 = 0; k0 < hidden; k0 += 64) {
+    if (k0 + 64 < hidden) load(k0 + 64, nxt);
+    if (lora) {  // A rows of this chunk: 32 rows x 64 columns, one 16-byte piece per thread
+      const int ar = tid >> 3, ac = 8 * (tid & 7);
+      ptx::cp_async16(ptx::smem_u32(as + ar * kCastLd + ac), a16 + ar * lda + k0 + ac, true);
+      ptx::cp_async_commit();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t t = t0 + rr + 16 * i;
+      const uint2 v = make_uint2(Dt<T>::pack2(cur[i].x, cur[i].y), Dt<T>::pack2(cur[i].z, cur[i].w));
+      if (t < n_tok) *reinterpret_cast<uint2*>(x16 + t * ldx16 + k0 + cc) = v;
+      *reinterpret_cast<uint2*>(xs + (rr + 16 * i) * kCastLd + cc) = v;
+    }
+    if (lora) {
+      ptx::cp_async_wait<0>();
+      __syncthreads();
+      // warp w: tokens 16 (w & 3) .. + 15, u columns 16 (w >> 2) .. + 15 (two n8 tiles)
+      const int mt = warp & 3, nh = warp >> 2;
+#pragma unroll
+      for (int kk = 0; kk < 64; kk += 16) {
+        uint32_t a[4], b0, b1, b2, b3;
+        const T* ap = xs + (16 * mt + (lane & 15)) * kCastLd + kk + 8 * (lane >> 4);
+        ptx::ldsm_x4(ptx::smem_u32(ap), a[0], a[1], a[2], a[3]);
+        // B (n x k, k contiguous): matrices (n 0-7, k 0-7), (n 0-7, k 8-15), (n 8-15, k 0-7), (n 8-15, k 8-15)
+        const T* bp = as + (16 * nh + (lane & 7) + 8 * (lane >> 4)) * kCastLd + kk + 8 * ((lane >> 3) & 1);
+        ptx::ldsm_x4(ptx::smem_u32(bp), b0, b1, b2, b3);
+        ptx::mma16816<T>(acc[0], a, b0, b1);
+        ptx::mma16816<T>(acc[1], a, b2, b3);
+      }
+      __syncthreads();  // xs / as are rewritten by the next chunk
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) cur[i] = nxt[i];
+  }
+  if (lora) {
+    const int mt = warp & 3, nh = warp >> 2;
+    const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const int col = 16 * nh + 8 * n + 2 * tq;
+      const int64_t ta = t0 + 16 * mt + g, tb = ta + 8;
+      if (ta < n_tok) *reinterpret_cast<uint32_t*>(u + ta * 2 * kR + col) = Dt<T>::pack2(acc[n][0], acc[n][1]);
+      if (tb < n_tok) *reinterpret_cast<uint32_t*>(u + tb * 2 * kR + col) = Dt<T>::pack2(acc[n][2], acc[n][3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// dA = du^T x16, dB = scaling g^T u: reductions over the tokens on mma.sync
+// ------------------------------------------------------------------------------------------------
+// Output row block v (blockIdx.y): v < hidden / 128 -> dA^T rows (hidden columns 128 v ..): P = x16,
+// Q = du (32 columns); else dB rows of lora_B head v - hidden / 128 (q heads, then v heads): P = the
+// head's g columns of dy, Q = u_q or u_v (16 columns). out[m][n] += sum_t P[t][m] Q[t][n] over the
+// block's token chunk (blockIdx.x), added into fp32 outputs zeroed by the caller.
+constexpr int kGradTok = 512, kGradStep = 64, kGradThreads = 256, kPLd = 128 + 8, kQLd = 32 + 8;
+
+template <typename T>
+__global__ void __launch_bounds__(kGradThreads) lora_grad_kernel(const T* __restrict__ dy, int64_t ld_dy,
+                                                                 const T* __restrict__ x16, int64_t ldx,
+                                                                 const T* __restrict__ u, float* __restrict__ da,
+                                                                 float* __restrict__ db, float scaling,
+                                                                 int64_t n_tok, int hidden, int hq, int hk) {
+  __shared__ __align__(16) T ps[2][kGradStep * kPLd];
+  __shared__ __align__(16) T qs[2][kGradStep * kQLd];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int vb = blockIdx.y, n_da = hidden / kD;
+  const bool is_a = vb < n_da;
+  const int head = vb - n_da;  // dB: lora_B head slot (q heads, then v heads)
+  const int nq = is_a ? 2 * kR : kR;  // Q columns
+  const T* P;
+  int64_t ldp;
+  const T* Q;
+  int64_t ldq;
+  const int n_proj = (hq + 2 * hk) * kD;
+  if (is_a) {
+    P = x16 + vb * kD;
+    ldp = ldx;
+    Q = dy + n_proj;  // du_q | du_v
+    ldq = ld_dy;
+  } else {
+    const int col = head < hq ? head * kD : (hq + hk + (head - hq)) * kD;
+    P = dy + col;
+    ldp = ld_dy;
+    Q = u + (head < hq ? 0 : kR);
+    ldq = 2 * kR;
+  }
+  const int64_t tb0 = static_cast<int64_t>(blockIdx.x) * kGradTok;
+  auto stage = [&](int buf, int64_t t0) {
+    // P: 64 tokens x 128 columns = 1024 pieces of 16 bytes, 4 per thread
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int piece = tid + kGradThreads * i;
+      const int row = piece >> 4, c = 8 * (piece & 15);
+      const int64_t t = t0 + row;
+      const bool ok = t < n_tok;
+      ptx::cp_async16(ptx::smem_u32(&ps[buf][row * kPLd + c]), ok ? P + t * ldp + c : P, ok);
+    }
+    // Q: 64 tokens x nq columns (nq / 8 pieces per row)
+    const int per_row = nq / 8;
+    if (tid < kGradStep * per_row) {
+      const int row = tid / per_row, c = 8 * (tid % per_row);
+      const int64_t t = t0 + row;
+      const bool ok = t < n_tok;
+      ptx::cp_async16(ptx::smem_u32(&qs[buf][row * kQLd + c]), ok ? Q + t * ldq + c : Q, ok);
+    }
+    ptx::cp_async_commit();
+  };
+  float acc[4][4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+  const int n_steps = kGradTok / kGradStep;
+  stage(0, tb0);
+  for (int st = 0; st < n_steps; ++st) {
+    const int buf = st & 1;
+    if (st + 1 < n_steps) {
+      stage(buf ^ 1, tb0 + (st + 1) * kGradStep);
+      ptx::cp_async_wait<1>();
+    } else {
+      ptx::cp_async_wait<0>();
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k0 = 0; k0 < kGradStep; k0 += 16) {
+      // A (m = P column, k = token) from P[token][column] by transposed loads
+      uint32_t a[4];
+      const int tok = k0 + (lane & 7) + 8 * (lane >> 4);
+      const int m = 16 * warp + 8 * ((lane >> 3) & 1);
+      ptx::ldsm_x4_t(ptx::smem_u32(&ps[buf][tok * kPLd + m]), a[0], a[1], a[2], a[3]);
+#pragma unroll
+      for (int n2 = 0; n2 < 2; ++n2) {
+        if (16 * n2 >= nq) break;
+        uint32_t b0, b1, b2, b3;
+        const int tq = k0 + (lane & 7) + 8 * ((lane >> 3) & 1);
+        const int nn = 16 * n2 + 8 * (lane >> 4);
+        ptx::ldsm_x4_t(ptx::smem_u32(&qs[buf][tq * kQLd + nn]), b0, b1, b2, b3);
+        ptx::mma16816<T>(acc[2 * n2], a, b0, b1);
+        ptx::mma16816<T>(acc[2 * n2 + 1], a, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  // C fragment: rows (m) g / g + 8 of the warp's 16, columns (n) 8 nt + 2 tq .. + 1
+  const int g = lane >> 2, tq = lane & 3;
+  const float mul = is_a ? 1.f : scaling;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    if (8 * nt >= nq) break;
+    const int n = 8 * nt + 2 * tq;
+    const int m = 16 * warp + g;
+    if (is_a) {  // dA [32, hidden]: element (n, hidden column 128 vb + m)
+      float* base = da + vb * kD + m;
+      atomicAdd(base + static_cast<int64_t>(n) * hidden, acc[nt][0]);
+      atomicAdd(base + static_cast<int64_t>(n + 1) * hidden, acc[nt][1]);
+      atomicAdd(base + static_cast<int64_t>(n) * hidden + 8, acc[nt][2]);
+      atomicAdd(base + static_cast<int64_t>(n + 1) * hidden + 8, acc[nt][3]);
+    } else {     // dB [(hq + hk) * 128, 16]: element (128 head + m, n)
+      float* base = db + (static_cast<int64_t>(head) * kD + m) * kR + n;
+      atomicAdd(base, mul * acc[nt][0]);
+      atomicAdd(base + 1, mul * acc[nt][1]);
+      atomicAdd(base + 8 * kR, mul * acc[nt][2]);
+      atomicAdd(base + 8 * kR + 1, mul * acc[nt][3]);
+    }
+  }
+}
+
+template <typename T, int EPI>
+int launch_gemm(const Params& p, cudaStream_t s, const char* what) {
+  static std::atomic<unsigned long long> set{0};
+  if (int rc = ensure_dyn_smem(proj_gemm_kernel<T, EPI>, Layout<EPI>::SMEM, set, what)) return rc;
+  const int grid = p.n_tiles < sm_count() ? p.n_tiles : sm_count();
+  proj_gemm_kernel<T, EPI><<<grid, NTHREADS, Layout<EPI>::SMEM, s>>>(p);
+  return check_launch(what);
+}
+
+}  // namespace
+}  // namespace proj
+}  // namespace decik
+
+using decik::set_error;
+
+extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* bias,
+                                  const void* lora_b, float scaling, const float* cosp, const float* sinp,
+                                  decik_tensor3_mut q, decik_tensor3_mut k, decik_tensor3_mut v, void* x16,
+                                  int64_t ldx16, void* u, int64_t n_tok, int hidden, int n_heads, int n_kv,
+                                  int head_dim, int dtype, void* stream) {
+  using namespace decik;
+  using namespace decik::proj;
+  if (n_tok == 0) return DECIK_OK;
+  if (n_tok < 0 || n_tok > (int64_t(1) << 31) - 1 || head_dim != kD || n_heads <= 0 || n_kv <= 0 ||
+      hidden <= 0 || hidden % 64 != 0 || (n_heads + 2 * n_kv) % 2 != 0)
+    return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: T=%lld hidden %d heads %d/%d head_dim %d (needs head_dim 128, "
+                     "hidden %% 64 == 0, an even head count)", (long long)n_tok, hidden, n_heads, n_kv, head_dim);
+  if (!x || !w_cat || !bias || !cosp || !sinp || !q.ptr || !k.ptr || !v.ptr || !x16 || ((lora_b == nullptr) != (u == nullptr)))
+    return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: NULL pointer (lora_b and u go together)");
+  if (ldx < hidden || ldw < hidden || ldx16 < hidden)
+    return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: row strides shorter than hidden");
+  if (ldx % 4 || ldw % 8 || ldx16 % 8 || !aligned16(x) || !aligned16(w_cat) || !aligned16(x16) ||
+      (u && !aligned16(u)) || (lora_b && !aligned16(lora_b)) || !aligned16(cosp) || !aligned16(sinp))
+    return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: rows and pointers need 16-byte alignment");
+  if (dtype != DECIK_BF16 && dtype != DECIK_F16) return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: dtype %d", dtype);
+  cudaStream_t s = as_stream(stream);
+  const int n_proj = (n_heads + 2 * n_kv) * kD;
+  Params p{};
+  int ord = 0;
+  if (int rc = attn::make_map_2d(&p.ta, x16, dtype, hidden, n_tok, ldx16 * 2, 64, BM)) return rc;
+  if (int rc = attn::make_map_2d(&p.tb, w_cat, dtype, hidden, n_proj, ldw * 2, 64, Cfg<EPI_QKV>::BN)) return rc;
+  const decik_tensor3_mut outs[3] = {q, k, v};
+  const int heads[3] = {n_heads, n_kv, n_kv};
+  for (int j = 0; j < 3; ++j) {
+    if (int rc = attn::make_tile_map(&p.to[j], outs[j].ptr, outs[j].tok_stride, outs[j].head_stride, n_tok, heads[j],
+                                     dtype, &ord, 32))
+      return rc;
+    p.order[j] = ord;
+  }
+  p.M = n_tok;
+  p.N = n_proj;
+  p.K = hidden;
+  p.n_tiles_n = n_proj / Cfg<EPI_QKV>::BN + (n_proj % Cfg<EPI_QKV>::BN ? 1 : 0);
+  const int64_t m_tiles = (n_tok + BM - 1) / BM;
+  p.n_tiles = static_cast<int>(m_tiles * p.n_tiles_n);
+  p.bias = bias;
+  p.u = u;
+  p.ldu = 2 * kR;
+  p.b16 = lora_b;
+  p.scaling = scaling;
+  p.cosp = cosp;
+  p.sinp = sinp;
+  p.hq = n_heads;
+  p.hk = n_kv;
+  p.err = attn::attn_error_word();
+  // x16 and u first (the GEMM's A operand and the LoRA-up input), then the GEMM + epilogue
+  const int grid_cast = static_cast<int>((n_tok + kCastTok - 1) / kCastTok);
+  if (dtype == DECIK_BF16) {
+    using T = __nv_bfloat16;
+    x_cast_lora_down_kernel<T><<<grid_cast, kCastThreads, 0, s>>>(
+        x, ldx, static_cast<const T*>(w_cat) + static_cast<int64_t>(n_proj) * ldw, ldw, static_cast<T*>(x16), ldx16,
+        static_cast<T*>(u), n_tok, hidden);
+    if (int rc = check_launch("x_cast_lora_down")) return rc;
+    return launch_gemm<T, EPI_QKV>(p, s, "qkv_proj_gemm");
+  }
+  using T = __half;
+  x_cast_lora_down_kernel<T><<<grid_cast, kCastThreads, 0, s>>>(
+      x, ldx, static_cast<const T*>(w_cat) + static_cast<int64_t>(n_proj) * ldw, ldw, static_cast<T*>(x16), ldx16,
+      static_cast<T*>(u), n_tok, hidden);
+  if (int rc = check_launch("x_cast_lora_down")) return rc;
+  return launch_gemm<T, EPI_QKV>(p, s, "qkv_proj_gemm");
+}
+
+extern "C" int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const void* w_cat, int64_t ldw, float* dx,
+                             int64_t ld_dx, int64_t n_tok, int hidden, int dtype, void* stream) {
+  using namespace decik;
+  using namespace decik::proj;
+  if (n_tok == 0) return DECIK_OK;
+  if (n_tok < 0 || n_tok > (int64_t(1) << 31) - 1 || hidden <= 0 || hidden % 64 != 0 || k_cols <= 0)
+    return set_error(DECIK_ERR_INVALID, "proj_dx: T=%lld hidden %d K %d", (long long)n_tok, hidden, k_cols);
+  if (!dy || !w_cat || !dx) return set_error(DECIK_ERR_INVALID, "proj_dx: NULL pointer");
+  if (ld_dy < k_cols || ldw < hidden || ld_dx < hidden)
+    return set_error(DECIK_ERR_INVALID, "proj_dx: row strides shorter than the rows");
+  if (ld_dy % 8 || ldw % 8 || ld_dx % 4 || !aligned16(dy) || !aligned16(w_cat) || !aligned16(dx))
+    return set_error(DECIK_ERR_INVALID, "proj_dx: rows and pointers need 16-byte alignment");
+  if (dtype != DECIK_BF16 && dtype != DECIK_F16) return set_error(DECIK_ERR_INVALID, "proj_dx: dtype %d", dtype);
+  Params p{};
+  if (int rc = attn::make_map_2d(&p.ta, dy, dtype, k_cols, n_tok, ld_dy * 2, 64, BM)) return rc;
+  if (int rc = attn::make_map_2d(&p.tb, w_cat, dtype, hidden, k_cols, ldw * 2, 64, 64)) return rc;
+  if (int rc = attn::make_map_2d(&p.to[0], dx, DECIK_F32, hidden, n_tok, ld_dx * 4, 32, 32)) return rc;
+  constexpr int BN = Cfg<EPI_F32>::BN;
+  p.M = n_tok;
+  p.N = hidden;
+  p.K = k_cols;
+  p.n_tiles_n = (hidden + BN - 1) / BN;
+  p.n_tiles = static_cast<int>(((n_tok + BM - 1) / BM) * p.n_tiles_n);
+  p.err = attn::attn_error_word();
+  cudaStream_t s = as_stream(stream);
+  if (dtype == DECIK_BF16) return launch_gemm<__nv_bfloat16, EPI_F32>(p, s, "proj_dx_gemm");
+  return launch_gemm<__half, EPI_F32>(p, s, "proj_dx_gemm");
+}
+
+extern "C" int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, int64_t ldx, const void* u, float* da,
+                                float* db, float scaling, int64_t n_tok, int hidden, int n_heads, int n_kv,
+                                int dtype, void* stream) {
+  using namespace decik;
+  using namespace decik::proj;
+  if (n_tok < 0 || hidden <= 0 || hidden % kD != 0 || n_heads <= 0 || n_kv <= 0)
+    return set_error(DECIK_ERR_INVALID, "lora_grads: T=%lld hidden %d heads %d/%d", (long long)n_tok, hidden, n_heads, n_kv);
+  if (!dy || !x16 || !u || !da || !db) return set_error(DECIK_ERR_INVALID, "lora_grads: NULL pointer");
+  if (ld_dy < static_cast<int64_t>(n_heads + 2 * n_kv) * kD + 2 * kR || ldx < hidden)
+    return set_error(DECIK_ERR_INVALID, "lora_grads: dy rows need (heads + 2 kv heads) x 128 + 32 columns, x16 rows hidden");
+  if (ld_dy % 8 || ldx % 8 || !aligned16(dy) || !aligned16(x16) || !aligned16(u))
+    return set_error(DECIK_ERR_INVALID, "lora_grads: rows and pointers need 16-byte alignment");
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaMemsetAsync(da, 0, sizeof(float) * 2 * kR * hidden, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(db, 0, sizeof(float) * (n_heads + n_kv) * kD * kR, s);
+  if (e != cudaSuccess) return set_error(DECIK_ERR_CUDA, "lora_grads: memset: %s", cudaGetErrorString(e));
+  if (n_tok == 0) return DECIK_OK;
+  const dim3 grid(static_cast<unsigned>((n_tok + kGradTok - 1) / kGradTok), hidden / kD + n_heads + n_kv);
+  if (dtype == DECIK_BF16) {
+    using T = __nv_bfloat16;
+    lora_grad_kernel<T><<<grid, kGradThreads, 0, s>>>(static_cast<const T*>(dy), ld_dy, static_cast<const T*>(x16),
+                                                      ldx, static_cast<const T*>(u), da, db, scaling, n_tok, hidden,
+                                                      n_heads, n_kv);
+  } else if (dtype == DECIK_F16) {
+    using T = __half;
+    lora_grad_kernel<T><<<grid, kGradThreads, 0, s>>>(static_cast<const T*>(dy), ld_dy, static_cast<const T*>(x16),
+                                                      ldx, static_cast<const T*>(u), da, db, scaling, n_tok, hidden,
+                                                      n_heads, n_kv);
+  } else {
+    return set_error(DECIK_ERR_INVALID, "lora_grads: dtype %d", dtype);
+  }
+  return check_launch("lora_grads");
+}

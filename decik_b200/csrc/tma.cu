@@ -80,6 +80,31 @@ int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t
   return DECIK_OK;
 }
 
+// A 2-D tiled map with the 128-byte swizzle over a row-major matrix of `outer` rows x `inner`
+// elements (row stride row_bytes), box box_outer rows x box_inner elements (box_inner x the element
+// size must be 128 bytes: one swizzle row). dtype: DECIK_F16 / DECIK_BF16 / DECIK_F32.
+int make_map_2d(CUtensorMap* map, const void* ptr, int dtype, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return set_error(DECIK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const CUtensorMapDataType dt = dtype == DECIK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : dtype == DECIK_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const uint32_t esize = dtype == DECIK_F32 ? 4 : 2;
+  if (box_inner * esize != 128)
+    return set_error(DECIK_ERR_INVALID, "make_map_2d: box inner %u x %u bytes is not one 128-byte row", box_inner, esize);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer}, estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(DECIK_ERR_INVALID, "cuTensorMapEncodeTiled (2-D) failed (%d): %llu x %llu, row %llu bytes",
+                     static_cast<int>(r), (unsigned long long)outer, (unsigned long long)inner,
+                     (unsigned long long)row_bytes);
+  return DECIK_OK;
+}
+
 // A 3-D map over an fp32 [T, H, 128] tensor (dims ordered d, head, token; head stride 512 B) whose
 // box is box_rows tokens x one head x 128 dims, no swizzle: the target of the dq tile reductions.
 // fp32 [n_tok, n_heads, 128] accumulator (dq, dk, dv) for TMA reduce-add of [box_rows x 16] chunks

@@ -451,6 +451,63 @@ def qkv_epilogue_fwd(y: torch.Tensor, u: torch.Tensor | None, frag: torch.Tensor
     return q, k, v, u_out
 
 
+def qkv_proj_fwd(x: torch.Tensor, w_cat: torch.Tensor, bias_cat: torch.Tensor, lora_b: torch.Tensor | None,
+                 scaling: float, cos: torch.Tensor, sin: torch.Tensor, n_heads: int, n_kv: int):
+    """The block's forward projections on tcgen05 (decik_qkv_proj_fwd): from x fp32 [T, H] and
+    w_cat [(Hq+2Hk)*D + 32, H] (W_q, W_k, W_v rows, then A_q, A_v) returns x16 [T, H], u [T, 32]
+    (None without ``lora_b``), q [Hq, T, D] and k [Hk, T, D] head-major with RoPE, v [T, Hk, D]."""
+    _cuda(x, w_cat, bias_cat, lora_b, cos, sin)
+    T, H = x.shape
+    D = cos.shape[-1]
+    dt, dev = w_cat.dtype, x.device
+    if x.dtype != torch.float32 or x.stride(1) != 1 or w_cat.stride(1) != 1:
+        raise RuntimeError("decik_b200 qkv_proj_fwd: x fp32 and w_cat with contiguous rows")
+    x16 = torch.empty((T, H), dtype=dt, device=dev)
+    u = torch.empty((T, 2 * LORA_RANK), dtype=dt, device=dev) if lora_b is not None else None
+    q = torch.empty((n_heads, T, D), dtype=dt, device=dev)
+    k = torch.empty((n_kv, T, D), dtype=dt, device=dev)
+    v = torch.empty((T, n_kv, D), dtype=dt, device=dev)
+    b16 = lora_b.contiguous() if lora_b is not None else None
+    with _timed("qkv_proj_fwd", 2):
+        rc = _lib.lib().decik_qkv_proj_fwd(
+            _p(x), x.stride(0), _p(w_cat), w_cat.stride(0), _p(bias_cat.contiguous()), _p(b16), float(scaling),
+            _p(cos.contiguous()), _p(sin.contiguous()), _t3any(q.transpose(0, 1)), _t3any(k.transpose(0, 1)),
+            _t3any(v), _p(x16), x16.stride(0), _p(u), T, H, n_heads, n_kv, D, _dt(w_cat), _stream(x))
+    _lib.check(rc, "qkv_proj_fwd")
+    return x16, u, q, k, v
+
+
+def proj_dx(dy: torch.Tensor, w_cat: torch.Tensor, k_cols: int | None = None) -> torch.Tensor:
+    """dx = dy[:, :K] . w_cat[:K] in fp32 [T, H] on tcgen05 (decik_proj_dx)."""
+    _cuda(dy, w_cat)
+    T = dy.shape[0]
+    K = int(k_cols if k_cols is not None else w_cat.shape[0])
+    H = w_cat.shape[1]
+    if dy.stride(1) != 1 or w_cat.stride(1) != 1:
+        raise RuntimeError("decik_b200 proj_dx: dy and w_cat need contiguous rows")
+    dx = torch.empty((T, H), dtype=torch.float32, device=dy.device)
+    with _timed("proj_dx", 1):
+        rc = _lib.lib().decik_proj_dx(_p(dy), dy.stride(0), K, _p(w_cat), w_cat.stride(0), _p(dx), dx.stride(0), T, H,
+                                      _dt(dy), _stream(dy))
+    _lib.check(rc, "proj_dx")
+    return dx
+
+
+def lora_grads(dy: torch.Tensor, x16: torch.Tensor, u: torch.Tensor, scaling: float, n_heads: int, n_kv: int):
+    """(dA [32, H], dB [(Hq+Hk)*D, 16]) fp32 of the fused block (decik_lora_grads): dA = du^T x16 with
+    du = dy's last 32 columns; dB = scaling g^T u over dy's q columns (u_q) and v columns (u_v)."""
+    _cuda(dy, x16, u)
+    T, H = x16.shape
+    D = 128
+    da = torch.empty((2 * LORA_RANK, H), dtype=torch.float32, device=dy.device)
+    db = torch.empty(((n_heads + n_kv) * D, LORA_RANK), dtype=torch.float32, device=dy.device)
+    with _timed("lora_grads", 1):
+        rc = _lib.lib().decik_lora_grads(_p(dy), dy.stride(0), _p(x16), x16.stride(0), _p(u.contiguous()), _p(da),
+                                         _p(db), float(scaling), T, H, n_heads, n_kv, _dt(dy), _stream(dy))
+    _lib.check(rc, "lora_grads")
+    return da, db
+
+
 def qkv_epilogue_bwd(grad_q: torch.Tensor, grad_k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                      frag: torch.Tensor | None, scaling: float, dy: torch.Tensor, n_heads: int,
                      n_kv: int) -> torch.Tensor:

@@ -43,12 +43,13 @@ class FusedAttentionBlock(torch.autograd.Function):
     NF4Linear, LoRAPairFromNorm, FusedQKRope, VarlenSDPA), regrouped so each pass over the tokens
     does as much as it can:
 
-    forward   y = x16 [W_q; W_k; W_v; A_q; A_v]^T + [b; 0]   one GEMM (the three base projections
-              and both lora_A products share x16); decik_qkv_epilogue_fwd (LoRA-up, v add, RoPE,
-              head-major q/k); decik_varlen_attn_fwd.
-    backward  decik_varlen_attn_bwd with dv written straight into dy; decik_qkv_epilogue_bwd
-              (RoPE^T, du); dX = dy . W_cat (one GEMM, fp32 out: the three NF4Linear input
-              gradients and both LoRA input gradients); dA = du^T x16; dB = scaling . g^T u.
+    forward   decik_qkv_proj_fwd: x16 = dt(x) and u = x16 [A_q; A_v]^T in one pass, then one
+              tcgen05 GEMM x16 [W_q; W_k; W_v]^T whose epilogue adds the bias, LoRA-up, the v
+              add and RoPE and writes head-major q / k and v (y never reaches HBM);
+              decik_varlen_attn_fwd.
+    backward  decik_attn_qkv_bwd (attention backward, RoPE^T, du) into dy; decik_proj_dx:
+              dX = dy . W_cat (one tcgen05 GEMM, fp32 out: the three NF4Linear input gradients and
+              both LoRA input gradients); decik_lora_grads: dA = du^T x16, dB = scaling . g^T u.
 
     ``w_cat`` [(Hq+2Hk)*D + 2r, H] holds this step's dequantised W_q, W_k, W_v in its first rows;
     decik_lora_pack writes A_q, A_v (as dt) into the last 2r rows and the lora_B fragments of both
@@ -67,10 +68,9 @@ class FusedAttentionBlock(torch.autograd.Function):
         r = a_q.shape[0]
         n_proj = (n_heads + 2 * n_kv) * D
         frag = ops.lora_pack(a_q, a_v, b_q, b_v, dt, a_out=w_cat[n_proj:])
-        x16 = x.to(dt)
-        y = F.linear(x16, w_cat, bias_cat)
-        q, k, v, u = ops.qkv_epilogue_fwd(y, y[:, n_proj:], frag, scaling, cos, sin, n_heads, n_kv, want_u=True)
-        del y
+        lora_b = torch.cat((b_q, b_v)).to(dt)
+        x32 = x if (x.dtype == torch.float32 and x.stride(-1) == 1) else x.float().contiguous()
+        x16, u, q, k, v = ops.qkv_proj_fwd(x32, w_cat, bias_cat, lora_b, scaling, cos, sin, n_heads, n_kv)
         out, lse = ops.varlen_attn_fwd(q.transpose(0, 1), k.transpose(0, 1), v, cu_seqlens, max_len, scale)
         ctx.save_for_backward(x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu_seqlens, w_o)
         ctx.meta = (int(max_len), n_heads, n_kv, float(scaling), float(scale), r)
@@ -94,12 +94,9 @@ class FusedAttentionBlock(torch.autograd.Function):
         # from their place in dy
         ops.attn_qkv_bwd(g, q.transpose(0, 1), k.transpose(0, 1), v, out, lse, cu, max_len, scale, cos, sin,
                          frag, scaling, dy)
-        dx = torch.mm(dy, w_cat, out_dtype=torch.float32)
-        da = torch.mm(dy[:, n_proj:].t(), x16, out_dtype=torch.float32)
-        db = torch.mm(dy[:, :n_proj].t(), u, out_dtype=torch.float32)
-        d_bq = db[:n_q, :r] * scaling
-        d_bv = db[n_q + n_kvd:, r:] * scaling
-        return (dx, da[:r], d_bq, da[r:], d_bv) + (None,) * 12
+        dx = ops.proj_dx(dy, w_cat)
+        da, db = ops.lora_grads(dy, x16, u, scaling, n_heads, n_kv)
+        return (dx, da[:r], db[:n_q], da[r:], db[n_q:]) + (None,) * 12
 
 
 def pack_keep(keep_q, keep_v):
