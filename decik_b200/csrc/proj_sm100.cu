@@ -71,11 +71,14 @@ struct Layout {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = S * A_BYTES;
-  static constexpr int OFF_STG = OFF_B + S * B_BYTES;  // per epilogue warp: two 4 KB staging tiles
-  static constexpr int STG_WARP = 8192;
-  static constexpr int OFF_B16 = OFF_STG + kEpiWarps * STG_WARP;  // QKV: lora_B rows of the tile's 2 heads
-  static constexpr int B16_BYTES = EPI == EPI_QKV ? 2 * kD * kR * 2 : 0;
-  static constexpr int OFF_BIAS = OFF_B16 + B16_BYTES;  // QKV: fp32 bias of the tile's 2 heads
+  // per epilogue warp: EPI_F32 two 4 KB staging tiles (double buffer); EPI_QKV one 4 KB tile (a
+  // [32 rows x 64] half of a head) and its RoPE tables (cos, sin: 32 rows x 16 fp32, rows padded to
+  // 80 bytes so that each thread's row reads are conflict-free)
+  static constexpr int OFF_STG = OFF_B + S * B_BYTES;
+  static constexpr int STG_WARP = EPI == EPI_QKV ? 4096 : 8192;
+  static constexpr int OFF_TAB = OFF_STG + kEpiWarps * STG_WARP;
+  static constexpr int TAB_WARP = EPI == EPI_QKV ? 2 * 32 * 80 : 0;
+  static constexpr int OFF_BIAS = OFF_TAB + kEpiWarps * TAB_WARP;  // QKV: fp32 bias of the tile's 2 heads
   static constexpr int BIAS_BYTES = EPI == EPI_QKV ? 2 * kD * 4 : 0;
   static constexpr int OFF_BAR = OFF_BIAS + BIAS_BYTES;
   static constexpr int N_BAR = 2 * S + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], done
@@ -87,14 +90,13 @@ struct Layout {
 
 struct Params {
   CUtensorMap ta, tb;     // A [M, K] K-major; B [N, K] K-major or [K, N] (MN-major)
+  CUtensorMap ta2, tb2;   // EPI_QKV with LoRA: one more K block, A = u [M, 64], B = [N, 64] scaled lora_B
   CUtensorMap to[3];      // EPI_QKV: q, k, v tile maps; EPI_F32: the fp32 output
   int order[3];           // tile-map coordinate order of q, k, v (0: d, tok, head; 1: d, head, tok)
   int64_t M;
   int N, K, n_tiles_n, n_tiles;
   const void* bias;       // EPI_QKV: 16-bit [N]
-  const void* u;          // EPI_QKV: 16-bit [M, 32] (u_q | u_v), NULL without LoRA
-  int64_t ldu;
-  const void* b16;        // EPI_QKV: 16-bit [(hq + hk) * 128, 16]: lora_B of q then v
+  int lora;               // EPI_QKV: the extra K block (u x scaled lora_B) is added to the accumulators
   float scaling;
   const float* cosp;
   const float* sinp;
@@ -105,19 +107,6 @@ struct Params {
 template <typename T>
 __device__ __forceinline__ float rnd(float x) {
   return Dt<T>::to_f(Dt<T>::from_f(x));
-}
-
-// dt(dt(u . B[d]) * scaling): the LoRA-up value of output column d (B rows staged in shared memory)
-template <typename T>
-__device__ __forceinline__ float lora_up(const float (&u)[kR], const uint4* brow, float scaling) {
-  const uint4 w0 = brow[0], w1 = brow[1];
-  float b[16];
-  unpack8<T>(w0, *reinterpret_cast<float(*)[8]>(&b[0]));
-  unpack8<T>(w1, *reinterpret_cast<float(*)[8]>(&b[8]));
-  float acc = 0.f;
-#pragma unroll
-  for (int j = 0; j < kR; ++j) acc = fmaf(u[j], b[j], acc);
-  return rnd<T>(__fmul_rn(rnd<T>(acc), scaling));
 }
 
 template <typename T, int EPI>
@@ -156,6 +145,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::OFF_TMEM);
   const int nk = (p.K + BK - 1) / BK;
+  const int nkt = nk + (EPI == EPI_QKV && p.lora ? 1 : 0);  // K blocks per tile, the LoRA one last
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -166,10 +156,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / p.n_tiles_n) * BM, n0 = (tile % p.n_tiles_n) * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = 0; kb < nkt; ++kb, ++it) {
           const int s = static_cast<int>(it % S);
           if (it >= static_cast<uint32_t>(S) && !(ok = mbar_wait(empty(s), ((it / S) - 1) & 1, p.err, 301))) break;
           mbar_expect_tx(full(s), L::A_BYTES + L::B_BYTES);
+          if (kb == nk) {  // the LoRA K block: u [tokens, 64] against the scaled lora_B columns
+            tma_load_2d(sb + L::OFF_A + s * L::A_BYTES, &p.ta2, full(s), 0, m0);
+            tma_load_2d(sb + L::OFF_B + s * L::B_BYTES, &p.tb2, full(s), 0, n0);
+            continue;
+          }
           tma_load_2d(sb + L::OFF_A + s * L::A_BYTES, &p.ta, full(s), kb * BK, m0);
           if constexpr (!BMN) {
             tma_load_2d(sb + L::OFF_B + s * L::B_BYTES, &p.tb, full(s), kb * BK, n0);
@@ -197,7 +192,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
         if (i >= 2 && !(ok = mbar_wait(acc_empty(b), ((i >> 1) - 1) & 1, p.err, 311))) break;
         tc_fence_after();
         const uint32_t d = tmem + b * 256;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = 0; kb < nkt; ++kb, ++it) {
           const int s = static_cast<int>(it % S);
           if (!(ok = mbar_wait(full(s), (it / S) & 1, p.err, 312))) break;
           tc_fence_after();
@@ -263,92 +258,80 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
       } else {
         const int hh = n0 / kD + wg;  // head of this warpgroup: q heads, then k, then v
         const int kind = hh < p.hq ? 0 : (hh < p.hq + p.hk ? 1 : 2);
-        const bool lora = p.b16 != nullptr && kind != 1;
         const bool rope = kind != 2;
         const int tid = threadIdx.x - 128 - 128 * wg;  // 0..127 in the warpgroup
         float* bias_s = reinterpret_cast<float*>(smem + L::OFF_BIAS) + wg * kD;
-        uint4* b16_s = reinterpret_cast<uint4*>(smem + L::OFF_B16 + wg * kD * kR * 2);
         bias_s[tid] = Dt<T>::to_f(static_cast<const T*>(p.bias)[hh * kD + tid]);
-        if (lora) {
-          const int slot = kind == 0 ? hh : p.hq + (hh - p.hq - p.hk);
-          const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.b16) + (slot * kD + tid) * kR);
-          b16_s[2 * tid] = __ldg(src);
-          b16_s[2 * tid + 1] = __ldg(src + 1);
-        }
         named_bar(1 + wg, 128);
-        float u[kR];
+        const int head = kind == 0 ? hh : (kind == 1 ? hh - p.hq : hh - p.hq - p.hk);
+        float* tab = reinterpret_cast<float*>(smem + L::OFF_TAB + ew * L::TAB_WARP);  // [cos | sin][32][20]
+        // the warp's 32 table rows of columns [d0, d0 + 16): 2 tables x 32 rows x 4 pieces of 16 B,
+        // eight coalesced cp.async per lane (rows past the end read the last row; not stored)
+        const auto load_tab = [&](int d0) {
 #pragma unroll
-        for (int j = 0; j < kR; ++j) u[j] = 0.f;
-        if (lora && r < p.M) {
-          const uint4* up = reinterpret_cast<const uint4*>(static_cast<const T*>(p.u) + r * p.ldu + (kind == 2 ? kR : 0));
-          unpack8<T>(__ldg(up), *reinterpret_cast<float(*)[8]>(&u[0]));
-          unpack8<T>(__ldg(up + 1), *reinterpret_cast<float(*)[8]>(&u[8]));
-        }
-        const int64_t rc = r < p.M ? r : p.M - 1;  // cos / sin row (rows past the end are not stored)
-        const float* cs = p.cosp + rc * kD;
-        const float* sn = p.sinp + rc * kD;
-        if (lane == 0) bulk_wait_read0();  // this warp's previous stores have read the staging tiles
-        __syncwarp();
+          for (int i = 0; i < 8; ++i) {
+            const int piece = lane + 32 * i;
+            const int which = piece >> 7, row = (piece >> 2) & 31, c4 = piece & 3;
+            const int64_t rr = row0 + row < p.M ? row0 + row : p.M - 1;
+            const float* src = (which ? p.sinp : p.cosp) + rr * kD + d0 + 4 * c4;
+            ptx::cp_async16_ca(ptx::smem_u32(tab + which * 32 * 20 + row * 20 + 4 * c4), src);  // the other
+            // warpgroup reads the same rows for its head: through L1
+          }
+          ptx::cp_async_commit();
+        };
+        // two passes: outputs d in [0, 64) (x[d] cos[d] - x[d + 64] sin[d]), then d in [64, 128)
+        // (x[d] cos[d] + x[d - 64] sin[d]); each fills the staging tile and leaves by one TMA store
 #pragma unroll 1
-        for (int c = 0; c < kD / 2; c += 16) {
-          uint32_t alo[16], ahi[16];
-          tmem_ld16(tacc + wg * kD + c, alo);
-          tmem_ld16(tacc + wg * kD + c + kD / 2, ahi);
-          tmem_ld_wait();
-          float olo[16], ohi[16];
-#pragma unroll
-          for (int e4 = 0; e4 < 16; e4 += 4) {
-            float4 cl = make_float4(0.f, 0.f, 0.f, 0.f), ch = cl, sl = cl, sh = cl;
+        for (int pass = 0; pass < 2; ++pass) {
+          if (lane == 0) bulk_wait_read0();  // the previous store has read the staging tile
+          __syncwarp();
+          if (rope) load_tab(pass * kD / 2);
+#pragma unroll 1
+          for (int c = 0; c < kD / 2; c += 16) {
+            float cs[16], sn[16];
             if (rope) {
-              cl = __ldg(reinterpret_cast<const float4*>(cs + c + e4));
-              ch = __ldg(reinterpret_cast<const float4*>(cs + c + e4 + kD / 2));
-              sl = __ldg(reinterpret_cast<const float4*>(sn + c + e4));
-              sh = __ldg(reinterpret_cast<const float4*>(sn + c + e4 + kD / 2));
-            }
-            const float cla[4] = {cl.x, cl.y, cl.z, cl.w}, cha[4] = {ch.x, ch.y, ch.z, ch.w};
-            const float sla[4] = {sl.x, sl.y, sl.z, sl.w}, sha[4] = {sh.x, sh.y, sh.z, sh.w};
+              ptx::cp_async_wait<0>();
+              __syncwarp();
 #pragma unroll
-            for (int e1 = 0; e1 < 4; ++e1) {
-              const int e = e4 + e1, d = c + e;
-              float lo = rnd<T>(__fadd_rn(__uint_as_float(alo[e]), bias_s[d]));
-              float hi = rnd<T>(__fadd_rn(__uint_as_float(ahi[e]), bias_s[d + kD / 2]));
-              if (lora) {
-                lo = __fadd_rn(lo, lora_up<T>(u, b16_s + 2 * d, p.scaling));
-                hi = __fadd_rn(hi, lora_up<T>(u, b16_s + 2 * (d + kD / 2), p.scaling));
+              for (int e4 = 0; e4 < 16; e4 += 4) {
+                const float4 a = *reinterpret_cast<const float4*>(tab + lane * 20 + e4);
+                const float4 b2 = *reinterpret_cast<const float4*>(tab + 32 * 20 + lane * 20 + e4);
+                cs[e4] = a.x; cs[e4 + 1] = a.y; cs[e4 + 2] = a.z; cs[e4 + 3] = a.w;
+                sn[e4] = b2.x; sn[e4 + 1] = b2.y; sn[e4 + 2] = b2.z; sn[e4 + 3] = b2.w;
               }
-              if (rope) {
-                // d < D/2: x[d] cos[d] + (-x[d + D/2]) sin[d];  d + D/2: x[d + D/2] cos + x[d] sin
-                olo[e] = __fadd_rn(__fmul_rn(lo, cla[e1]), __fmul_rn(-hi, sla[e1]));
-                ohi[e] = __fadd_rn(__fmul_rn(hi, cha[e1]), __fmul_rn(lo, sha[e1]));
-              } else {
-                olo[e] = lo;
-                ohi[e] = hi;
-              }
+              __syncwarp();
+              if (c + 16 < kD / 2) load_tab(pass * kD / 2 + c + 16);  // next columns, during the math
             }
-          }
-          // this row's 16 + 16 values into the two [32 rows x 64] halves (128-byte swizzle)
+            uint32_t alo[16], ahi[16];
+            tmem_ld16(tacc + wg * kD + c, alo);
+            tmem_ld16(tacc + wg * kD + c + kD / 2, ahi);
+            tmem_ld_wait();
+            float o[16];
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int chunk = c / 8 + j;
-            const int off = lane * 128 + ((chunk ^ (lane & 7)) << 4);
-            *reinterpret_cast<uint4*>(stg + off) = pack8<T>(*reinterpret_cast<const float(*)[8]>(&olo[8 * j]));
-            *reinterpret_cast<uint4*>(stg + 4096 + off) = pack8<T>(*reinterpret_cast<const float(*)[8]>(&ohi[8 * j]));
+            for (int e = 0; e < 16; ++e) {
+              const int d = c + e;
+              // the accumulator holds x16 W^T + u (scaled lora_B)^T in fp32; the bias joins it here
+              const float lo = __fadd_rn(__uint_as_float(alo[e]), bias_s[d]);
+              const float hi = __fadd_rn(__uint_as_float(ahi[e]), bias_s[d + kD / 2]);
+              if (!rope) o[e] = pass ? hi : lo;
+              else if (pass == 0) o[e] = __fadd_rn(__fmul_rn(lo, cs[e]), __fmul_rn(-hi, sn[e]));
+              else o[e] = __fadd_rn(__fmul_rn(hi, cs[e]), __fmul_rn(lo, sn[e]));
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              *reinterpret_cast<uint4*>(stg + lane * 128 + (((c / 8 + j) ^ (lane & 7)) << 4)) =
+                  pack8<T>(*reinterpret_cast<const float(*)[8]>(&o[8 * j]));
           }
-        }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0 && row0 < p.M) {
-          const int head = kind == 0 ? hh : (kind == 1 ? hh - p.hq : hh - p.hq - p.hk);
-          const CUtensorMap* map = &p.to[kind];
-          const int t = static_cast<int>(row0);
-          if (p.order[kind] == 0) {
-            tma_store_3d(map, stg_s, 0, t, head);
-            tma_store_3d(map, stg_s + 4096, kD / 2, t, head);
-          } else {
-            tma_store_3d(map, stg_s, 0, head, t);
-            tma_store_3d(map, stg_s + 4096, kD / 2, head, t);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < p.M) {
+              const int t = static_cast<int>(row0);
+              if (p.order[kind] == 0) tma_store_3d(&p.to[kind], stg_s, pass * kD / 2, t, head);
+              else tma_store_3d(&p.to[kind], stg_s, pass * kD / 2, head, t);
+            }
+            bulk_commit();
           }
-          bulk_commit();
         }
       }
       tc_fence_before();
@@ -369,25 +352,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
 // ------------------------------------------------------------------------------------------------
 // x fp32 -> x16, u = dt(x16 [A_q; A_v]^T)
 // ------------------------------------------------------------------------------------------------
-constexpr int kCastTok = 64, kCastThreads = 256, kCastLd = 64 + 8;  // padded shared rows (16-bit)
+constexpr int kCastTok = 64, kCastThreads = 256, kCastK = 128, kCastLd = kCastK + 8;  // padded rows (16-bit)
 
+// One CTA = 64 tokens; the K loop walks 128-column chunks of x. Each thread loads 8 float4 of a
+// chunk (warp w: rows w, w + 8, ..., 512 contiguous bytes per row) with the next chunk's loads in
+// flight during the current chunk's work; the 16-bit chunk goes to x16 and to shared memory, where
+// mma.sync multiplies it by the matching 32 x 128 slice of [A_q; A_v].
 template <typename T>
 __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const float* __restrict__ x, int64_t ldx,
                                                                         const T* __restrict__ a16, int64_t lda,
                                                                         T* __restrict__ x16, int64_t ldx16,
                                                                         T* __restrict__ u, int64_t n_tok, int hidden) {
+  // u rows are 64 wide (the GEMM's LoRA K block): columns 32..63 are zero
+  constexpr int kULd = 4 * kR;
   __shared__ __align__(16) T xs[kCastTok * kCastLd];
   __shared__ __align__(16) T as[2 * kR * kCastLd];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kCastTok;
   const bool lora = u != nullptr;
-  // each thread moves 4 float4 per 64-column chunk: rows (tid >> 4) + 16 i, columns 4 (tid & 15)
-  const int cc = 4 * (tid & 15), rr = tid >> 4;
-  float4 cur[4], nxt[4];
-  auto load = [&](int k0, float4 (&dst)[4]) {
+  const int cc = 4 * lane;  // this thread's 4 columns of a chunk; rows warp + 8 i
+  float4 cur[8], nxt[8];
+  auto load = [&](int k0, float4 (&dst)[8]) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t t = t0 + rr + 16 * i;
+    for (int i = 0; i < 8; ++i) {
+      const int64_t t = t0 + warp + 8 * i;
       dst[i] = t < n_tok ? __ldg(reinterpret_cast<const float4*>(x + t * ldx + k0 + cc)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
@@ -397,19 +385,23 @@ __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const fl
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
   load(0, cur);
-  for (int k0 = 0; k0 < hidden; k0 += 64) {
-    if (k0 + 64 < hidden) load(k0 + 64, nxt);
-    if (lora) {  // A rows of this chunk: 32 rows x 64 columns, one 16-byte piece per thread
-      const int ar = tid >> 3, ac = 8 * (tid & 7);
-      ptx::cp_async16(ptx::smem_u32(as + ar * kCastLd + ac), a16 + ar * lda + k0 + ac, true);
+  for (int k0 = 0; k0 < hidden; k0 += kCastK) {
+    if (k0 + kCastK < hidden) load(k0 + kCastK, nxt);
+    if (lora) {  // A rows of this chunk: 32 rows x 128 columns, two 16-byte pieces per thread
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int piece = tid + kCastThreads * i;
+        const int ar = piece >> 4, ac = 8 * (piece & 15);
+        ptx::cp_async16(ptx::smem_u32(as + ar * kCastLd + ac), a16 + ar * lda + k0 + ac, true);
+      }
       ptx::cp_async_commit();
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t t = t0 + rr + 16 * i;
+    for (int i = 0; i < 8; ++i) {
+      const int64_t t = t0 + warp + 8 * i;
       const uint2 v = make_uint2(Dt<T>::pack2(cur[i].x, cur[i].y), Dt<T>::pack2(cur[i].z, cur[i].w));
       if (t < n_tok) *reinterpret_cast<uint2*>(x16 + t * ldx16 + k0 + cc) = v;
-      *reinterpret_cast<uint2*>(xs + (rr + 16 * i) * kCastLd + cc) = v;
+      if (lora) *reinterpret_cast<uint2*>(xs + (warp + 8 * i) * kCastLd + cc) = v;
     }
     if (lora) {
       ptx::cp_async_wait<0>();
@@ -417,7 +409,7 @@ __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const fl
       // warp w: tokens 16 (w & 3) .. + 15, u columns 16 (w >> 2) .. + 15 (two n8 tiles)
       const int mt = warp & 3, nh = warp >> 2;
 #pragma unroll
-      for (int kk = 0; kk < 64; kk += 16) {
+      for (int kk = 0; kk < kCastK; kk += 16) {
         uint32_t a[4], b0, b1, b2, b3;
         const T* ap = xs + (16 * mt + (lane & 15)) * kCastLd + kk + 8 * (lane >> 4);
         ptx::ldsm_x4(ptx::smem_u32(ap), a[0], a[1], a[2], a[3]);
@@ -430,7 +422,7 @@ __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const fl
       __syncthreads();  // xs / as are rewritten by the next chunk
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) cur[i] = nxt[i];
+    for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
   }
   if (lora) {
     const int mt = warp & 3, nh = warp >> 2;
@@ -439,9 +431,11 @@ __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const fl
     for (int n = 0; n < 2; ++n) {
       const int col = 16 * nh + 8 * n + 2 * tq;
       const int64_t ta = t0 + 16 * mt + g, tb = ta + 8;
-      if (ta < n_tok) *reinterpret_cast<uint32_t*>(u + ta * 2 * kR + col) = Dt<T>::pack2(acc[n][0], acc[n][1]);
-      if (tb < n_tok) *reinterpret_cast<uint32_t*>(u + tb * 2 * kR + col) = Dt<T>::pack2(acc[n][2], acc[n][3]);
+      if (ta < n_tok) *reinterpret_cast<uint32_t*>(u + ta * kULd + col) = Dt<T>::pack2(acc[n][0], acc[n][1]);
+      if (tb < n_tok) *reinterpret_cast<uint32_t*>(u + tb * kULd + col) = Dt<T>::pack2(acc[n][2], acc[n][3]);
     }
+    const int64_t tz = t0 + (tid >> 2);  // the zero half: 64 tokens x 4 pieces of 16 bytes
+    if (tz < n_tok) *reinterpret_cast<uint4*>(u + tz * kULd + 2 * kR + 8 * (tid & 3)) = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
@@ -457,7 +451,7 @@ constexpr int kGradTok = 512, kGradStep = 64, kGradThreads = 256, kPLd = 128 + 8
 template <typename T>
 __global__ void __launch_bounds__(kGradThreads) lora_grad_kernel(const T* __restrict__ dy, int64_t ld_dy,
                                                                  const T* __restrict__ x16, int64_t ldx,
-                                                                 const T* __restrict__ u, float* __restrict__ da,
+                                                                 const T* __restrict__ u, int64_t ldu, float* __restrict__ da,
                                                                  float* __restrict__ db, float scaling,
                                                                  int64_t n_tok, int hidden, int hq, int hk) {
   __shared__ __align__(16) T ps[2][kGradStep * kPLd];
@@ -482,7 +476,7 @@ __global__ void __launch_bounds__(kGradThreads) lora_grad_kernel(const T* __rest
     P = dy + col;
     ldp = ld_dy;
     Q = u + (head < hq ? 0 : kR);
-    ldq = 2 * kR;
+    ldq = ldu;
   }
   const int64_t tb0 = static_cast<int64_t>(blockIdx.x) * kGradTok;
   auto stage = [&](int buf, int64_t t0) {
@@ -565,6 +559,27 @@ __global__ void __launch_bounds__(kGradThreads) lora_grad_kernel(const T* __rest
   }
 }
 
+// The LoRA K block's B operand [n_proj, 64]: row c of a q head holds scaling B_q[c] in columns
+// 0..15 (against u_q), row c of a v head scaling B_v[c] in columns 16..31 (against u_v), every
+// other entry 0; rounded to T.
+template <typename T>
+__global__ void lora_b_ext_kernel(const float* __restrict__ bq, const float* __restrict__ bv, float scaling,
+                                  T* __restrict__ out, int hq, int hk) {
+  const int n_proj = (hq + 2 * hk) * kD;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // one 8-element piece of a row
+  if (i >= n_proj * 8) return;
+  const int row = i >> 3, piece = i & 7;
+  float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const float* src = nullptr;
+  if (row < hq * kD && piece < 2) src = bq + row * kR + 8 * piece;
+  else if (row >= (hq + hk) * kD && piece >= 2 && piece < 4) src = bv + (row - (hq + hk) * kD) * kR + 8 * (piece - 2);
+  if (src != nullptr) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = scaling * src[e];
+  }
+  *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * 4 * kR + 8 * piece) = pack8<T>(v);
+}
+
 template <typename T, int EPI>
 int launch_gemm(const Params& p, cudaStream_t s, const char* what) {
   static std::atomic<unsigned long long> set{0};
@@ -580,24 +595,43 @@ int launch_gemm(const Params& p, cudaStream_t s, const char* what) {
 
 using decik::set_error;
 
+extern "C" int decik_lora_b_ext(const float* b_q, const float* b_v, float scaling, void* out, int n_heads, int n_kv,
+                                int dtype, void* stream) {
+  using namespace decik;
+  using namespace decik::proj;
+  if (n_heads <= 0 || n_kv <= 0 || !b_q || !b_v || !out || !aligned16(out))
+    return set_error(DECIK_ERR_INVALID, "lora_b_ext: heads %d/%d or a NULL / unaligned pointer", n_heads, n_kv);
+  const int n = (n_heads + 2 * n_kv) * kD * 8;
+  cudaStream_t s = as_stream(stream);
+  if (dtype == DECIK_BF16)
+    lora_b_ext_kernel<__nv_bfloat16><<<(n + 255) / 256, 256, 0, s>>>(b_q, b_v, scaling,
+                                                                     static_cast<__nv_bfloat16*>(out), n_heads, n_kv);
+  else if (dtype == DECIK_F16)
+    lora_b_ext_kernel<__half><<<(n + 255) / 256, 256, 0, s>>>(b_q, b_v, scaling, static_cast<__half*>(out), n_heads,
+                                                              n_kv);
+  else
+    return set_error(DECIK_ERR_INVALID, "lora_b_ext: dtype %d", dtype);
+  return check_launch("lora_b_ext");
+}
+
 extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* bias,
-                                  const void* lora_b, float scaling, const float* cosp, const float* sinp,
-                                  decik_tensor3_mut q, decik_tensor3_mut k, decik_tensor3_mut v, void* x16,
-                                  int64_t ldx16, void* u, int64_t n_tok, int hidden, int n_heads, int n_kv,
-                                  int head_dim, int dtype, void* stream) {
+                                  const void* lora_b_ext, const float* cosp, const float* sinp, decik_tensor3_mut q,
+                                  decik_tensor3_mut k, decik_tensor3_mut v, void* x16, int64_t ldx16, void* u,
+                                  int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim, int dtype,
+                                  void* stream) {
   using namespace decik;
   using namespace decik::proj;
   if (n_tok == 0) return DECIK_OK;
   if (n_tok < 0 || n_tok > (int64_t(1) << 31) - 1 || head_dim != kD || n_heads <= 0 || n_kv <= 0 ||
-      hidden <= 0 || hidden % 64 != 0 || (n_heads + 2 * n_kv) % 2 != 0)
+      hidden <= 0 || hidden % 128 != 0 || (n_heads + 2 * n_kv) % 2 != 0)
     return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: T=%lld hidden %d heads %d/%d head_dim %d (needs head_dim 128, "
-                     "hidden %% 64 == 0, an even head count)", (long long)n_tok, hidden, n_heads, n_kv, head_dim);
-  if (!x || !w_cat || !bias || !cosp || !sinp || !q.ptr || !k.ptr || !v.ptr || !x16 || ((lora_b == nullptr) != (u == nullptr)))
-    return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: NULL pointer (lora_b and u go together)");
+                     "hidden %% 128 == 0, an even head count)", (long long)n_tok, hidden, n_heads, n_kv, head_dim);
+  if (!x || !w_cat || !bias || !cosp || !sinp || !q.ptr || !k.ptr || !v.ptr || !x16 || ((lora_b_ext == nullptr) != (u == nullptr)))
+    return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: NULL pointer (lora_b_ext and u go together)");
   if (ldx < hidden || ldw < hidden || ldx16 < hidden)
     return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: row strides shorter than hidden");
   if (ldx % 4 || ldw % 8 || ldx16 % 8 || !aligned16(x) || !aligned16(w_cat) || !aligned16(x16) ||
-      (u && !aligned16(u)) || (lora_b && !aligned16(lora_b)) || !aligned16(cosp) || !aligned16(sinp))
+      (u && !aligned16(u)) || (lora_b_ext && !aligned16(lora_b_ext)) || !aligned16(cosp) || !aligned16(sinp))
     return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: rows and pointers need 16-byte alignment");
   if (dtype != DECIK_BF16 && dtype != DECIK_F16) return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: dtype %d", dtype);
   cudaStream_t s = as_stream(stream);
@@ -606,6 +640,12 @@ extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat
   int ord = 0;
   if (int rc = attn::make_map_2d(&p.ta, x16, dtype, hidden, n_tok, ldx16 * 2, 64, BM)) return rc;
   if (int rc = attn::make_map_2d(&p.tb, w_cat, dtype, hidden, n_proj, ldw * 2, 64, Cfg<EPI_QKV>::BN)) return rc;
+  p.lora = lora_b_ext != nullptr;
+  if (p.lora) {
+    if (int rc = attn::make_map_2d(&p.ta2, u, dtype, 4 * kR, n_tok, 4 * kR * 2, 64, BM)) return rc;
+    if (int rc = attn::make_map_2d(&p.tb2, lora_b_ext, dtype, 4 * kR, n_proj, 4 * kR * 2, 64, Cfg<EPI_QKV>::BN))
+      return rc;
+  }
   const decik_tensor3_mut outs[3] = {q, k, v};
   const int heads[3] = {n_heads, n_kv, n_kv};
   for (int j = 0; j < 3; ++j) {
@@ -621,16 +661,12 @@ extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat
   const int64_t m_tiles = (n_tok + BM - 1) / BM;
   p.n_tiles = static_cast<int>(m_tiles * p.n_tiles_n);
   p.bias = bias;
-  p.u = u;
-  p.ldu = 2 * kR;
-  p.b16 = lora_b;
-  p.scaling = scaling;
   p.cosp = cosp;
   p.sinp = sinp;
   p.hq = n_heads;
   p.hk = n_kv;
   p.err = attn::attn_error_word();
-  // x16 and u first (the GEMM's A operand and the LoRA-up input), then the GEMM + epilogue
+  // x16 and u first (the GEMM's A operands), then the GEMM + epilogue
   const int grid_cast = static_cast<int>((n_tok + kCastTok - 1) / kCastTok);
   if (dtype == DECIK_BF16) {
     using T = __nv_bfloat16;
@@ -677,9 +713,9 @@ extern "C" int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const vo
   return launch_gemm<__half, EPI_F32>(p, s, "proj_dx_gemm");
 }
 
-extern "C" int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, int64_t ldx, const void* u, float* da,
-                                float* db, float scaling, int64_t n_tok, int hidden, int n_heads, int n_kv,
-                                int dtype, void* stream) {
+extern "C" int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, int64_t ldx, const void* u,
+                                int64_t ldu, float* da, float* db, float scaling, int64_t n_tok, int hidden,
+                                int n_heads, int n_kv, int dtype, void* stream) {
   using namespace decik;
   using namespace decik::proj;
   if (n_tok < 0 || hidden <= 0 || hidden % kD != 0 || n_heads <= 0 || n_kv <= 0)
@@ -687,8 +723,8 @@ extern "C" int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, 
   if (!dy || !x16 || !u || !da || !db) return set_error(DECIK_ERR_INVALID, "lora_grads: NULL pointer");
   if (ld_dy < static_cast<int64_t>(n_heads + 2 * n_kv) * kD + 2 * kR || ldx < hidden)
     return set_error(DECIK_ERR_INVALID, "lora_grads: dy rows need (heads + 2 kv heads) x 128 + 32 columns, x16 rows hidden");
-  if (ld_dy % 8 || ldx % 8 || !aligned16(dy) || !aligned16(x16) || !aligned16(u))
-    return set_error(DECIK_ERR_INVALID, "lora_grads: rows and pointers need 16-byte alignment");
+  if (ld_dy % 8 || ldx % 8 || ldu % 8 || ldu < 2 * kR || !aligned16(dy) || !aligned16(x16) || !aligned16(u))
+    return set_error(DECIK_ERR_INVALID, "lora_grads: rows and pointers need 16-byte alignment (u rows >= 32)");
   cudaStream_t s = as_stream(stream);
   cudaError_t e = cudaMemsetAsync(da, 0, sizeof(float) * 2 * kR * hidden, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(db, 0, sizeof(float) * (n_heads + n_kv) * kD * kR, s);
@@ -698,12 +734,12 @@ extern "C" int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, 
   if (dtype == DECIK_BF16) {
     using T = __nv_bfloat16;
     lora_grad_kernel<T><<<grid, kGradThreads, 0, s>>>(static_cast<const T*>(dy), ld_dy, static_cast<const T*>(x16),
-                                                      ldx, static_cast<const T*>(u), da, db, scaling, n_tok, hidden,
+                                                      ldx, static_cast<const T*>(u), ldu, da, db, scaling, n_tok, hidden,
                                                       n_heads, n_kv);
   } else if (dtype == DECIK_F16) {
     using T = __half;
     lora_grad_kernel<T><<<grid, kGradThreads, 0, s>>>(static_cast<const T*>(dy), ld_dy, static_cast<const T*>(x16),
-                                                      ldx, static_cast<const T*>(u), da, db, scaling, n_tok, hidden,
+                                                      ldx, static_cast<const T*>(u), ldu, da, db, scaling, n_tok, hidden,
                                                       n_heads, n_kv);
   } else {
     return set_error(DECIK_ERR_INVALID, "lora_grads: dtype %d", dtype);

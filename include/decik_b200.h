@@ -346,26 +346,35 @@ DECIK_API int decik_varlen_attn_bwd_noalloc(decik_tensor3 dout, decik_tensor3 q,
 /* ---------------------------------------------------------------------------------------------
  * The projection GEMMs of the attention block on tcgen05, with their epilogues fused.
  *
- * decik_qkv_proj_fwd replaces, for one layer, the reference's three NF4Linear forwards
+ * decik_lora_b_ext writes the B operand of the LoRA K block, out dt [n_proj, 64]
+ * (n_proj = (n_heads + 2 n_kv) 128): row c of a q head = scaling . B_q[c] in columns 0..15, row c
+ * of a v head = scaling . B_v[c] in columns 16..31, zero elsewhere. b_q fp32 [n_heads 128, 16],
+ * b_v fp32 [n_kv 128, 16] (peft's lora_B weights). */
+DECIK_API int decik_lora_b_ext(const float* b_q, const float* b_v, float scaling, void* out, int n_heads, int n_kv,
+                               int dtype, void* stream);
+
+/* decik_qkv_proj_fwd replaces, for one layer, the reference's three NF4Linear forwards
  * (solution/nf4.py:93-97: F.linear(x16, W, b16)), the LoRA pair's forward (solution/attn.py:217-228)
- * and FusedQKRope.forward (solution/attn.py:97-111, skc_rope_fwd_kernel :28-61):
- *   x16 = dt(x)                                  [T, hidden] (ldx16), dt = dtype
- *   u   = dt(x16 . w_cat[n_proj : n_proj + 32]^T) [T, 32]: u_q | u_v (skipped when lora_b is NULL)
- *   y   = x16 . w_cat[0 : n_proj]^T, per element dt(y + bias) (n_proj = (n_heads + 2 n_kv) 128)
- *   q = rope(dt(y_q + b) + dt(dt(u_q . B_q^T) * scaling)) head-major, k = rope(dt(y_k + b)),
- *   v = dt(dt(y_v + b) + dt(dt(u_v . B_v^T) * scaling)); RoPE with separate fp32 roundings.
+ * and FusedQKRope.forward (solution/attn.py:97-111, skc_rope_fwd_kernel :28-61). Two kernels:
+ *   1. x16 = dt(x) [T, hidden] (ldx16) and u = dt(x16 . w_cat[n_proj : n_proj + 32]^T) into
+ *      u [T, 64] (u_q | u_v | zeros; skipped without LoRA);
+ *   2. one persistent tcgen05 GEMM over K = hidden (+ 64 with LoRA):
+ *      acc = x16 . w_cat[0 : n_proj]^T + u . lora_b_ext^T   (fp32, in TMEM)
+ *      q = rope(acc_q + b) head-major, k = rope(acc_k + b) head-major, v = acc_v + b, each rounded
+ *      once to dt; RoPE in fp32 with separate roundings (no FMA). The projection never leaves the
+ *      chip. The reference rounds the base projection and the LoRA product to dt before adding
+ *      them; here they are added in fp32 (one rounding, at the end).
  *   x       fp32 [T, hidden] (ldx)
  *   w_cat   dt [(n_proj + 32), hidden] (ldw): dequantised W_q, W_k, W_v rows, then A_q, A_v rows
  *           (the last 32 rows are read only with LoRA)
- *   bias    dt [n_proj]; lora_b dt [(n_heads + n_kv) 128, 16]: B_q rows then B_v rows, or NULL
+ *   bias    dt [n_proj]; lora_b_ext: decik_lora_b_ext's output, or NULL for no LoRA (then u NULL)
  *   cos/sin fp32 [T, 128]; q, k, v: [T, H, 128] views (any 16-byte aligned strides)
- * hidden % 64 == 0, head_dim 128, an even n_heads + 2 n_kv. Two kernels: the cast + LoRA-down pass,
- * then the persistent tcgen05 GEMM whose epilogue writes q, k, v (y never leaves the chip). */
+ * hidden % 128 == 0, head_dim 128, an even n_heads + 2 n_kv. */
 DECIK_API int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* bias,
-                                 const void* lora_b, float scaling, const float* cosp, const float* sinp,
-                                 decik_tensor3_mut q, decik_tensor3_mut k, decik_tensor3_mut v, void* x16,
-                                 int64_t ldx16, void* u, int64_t n_tok, int hidden, int n_heads, int n_kv,
-                                 int head_dim, int dtype, void* stream);
+                                 const void* lora_b_ext, const float* cosp, const float* sinp, decik_tensor3_mut q,
+                                 decik_tensor3_mut k, decik_tensor3_mut v, void* x16, int64_t ldx16, void* u,
+                                 int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim, int dtype,
+                                 void* stream);
 
 /* dx = dy[:, 0:k_cols] . w_cat[0:k_cols, :] in fp32 [T, hidden] (ld_dx): the three NF4Linear input
  * gradients (solution/nf4.py:99-104: g16 @ W16) and both LoRA input gradients
@@ -377,11 +386,11 @@ DECIK_API int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const voi
  *   da [32, hidden] fp32 = du^T x16 (du = dy[:, n_proj : n_proj + 32]; rows 0-15 dA_q, 16-31 dA_v)
  *   db [(n_heads + n_kv) 128, 16] fp32 = scaling . g^T u (g = dy's q columns with u_q, then its v
  *      columns with u_v)
- * dy dt [T, >= n_proj + 32] (ld_dy), x16 dt [T, hidden], u dt [T, 32]. Zeroes da and db, then adds
- * token-chunked tensor-core partial products into them. */
+ * dy dt [T, >= n_proj + 32] (ld_dy), x16 dt [T, hidden], u dt [T, >= 32] (ldu). Zeroes da and db,
+ * then adds token-chunked tensor-core partial products into them. */
 DECIK_API int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, int64_t ldx, const void* u,
-                               float* da, float* db, float scaling, int64_t n_tok, int hidden, int n_heads,
-                               int n_kv, int dtype, void* stream);
+                               int64_t ldu, float* da, float* db, float scaling, int64_t n_tok, int hidden,
+                               int n_heads, int n_kv, int dtype, void* stream);
 
 #ifdef __cplusplus
 }
