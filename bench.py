@@ -370,13 +370,25 @@ def measure_block(args, world, rank, local, n_steps, workload=None, e2e=True, cp
             dist.barrier()
         return [a.elapsed_time(b) for a, b in zip(starts, ends)]
 
-    timer = ops.OpTimer()
-    ops.install_timer(timer)
+    # the timed steps carry no instrumentation; this library's launches are counted (no events)
+    counter = ops.OpTimer(names=())
+    ops.install_timer(counter)
     with ClockSampler(local) as clocks:
         step_ms = timed(n_steps, lambda: step(x, dout))
     ops.install_timer(None)
+    launches = counter.launches
+    # the same steps again with CUDA events around the two attention kernels only (the roofline
+    # figure), then a few with events around every op of this library (the kernel table)
+    timer = ops.OpTimer(names=("varlen_attn_fwd", "varlen_attn_bwd"))
+    ops.install_timer(timer)
+    timed(n_steps, lambda: step(x, dout))
+    ops.install_timer(None)
+    attn_ms = timer.elapsed_ms()
+    timer = ops.OpTimer()
+    ops.install_timer(timer)
+    timed(min(n_steps, 5), lambda: step(x, dout))
+    ops.install_timer(None)
     op_ms = timer.elapsed_ms()
-    launches = timer.launches
     total_ms = sum(step_ms)
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
@@ -442,10 +454,10 @@ def measure_block(args, world, rank, local, n_steps, workload=None, e2e=True, cp
         return None
     pk = peaks()
     f_fwd = causal_flops(lengths, n_heads=hq)
-    fwd_ms = statistics.mean(op_ms.get("varlen_attn_fwd", [float("nan")]))
-    bwd_ms = statistics.mean(op_ms.get("varlen_attn_bwd", [float("nan")]))
+    fwd_ms = statistics.mean(attn_ms.get("varlen_attn_fwd", [float("nan")]))
+    bwd_ms = statistics.mean(attn_ms.get("varlen_attn_bwd", [float("nan")]))
     attn_tflops = 3.0 * f_fwd / ((fwd_ms + bwd_ms) / 1e3) / 1e12
-    kernels = {name: {"ms_mean": round(statistics.mean(v), 4), "calls_per_step": len(v) // max(n_steps, 1)}
+    kernels = {name: {"ms_mean": round(statistics.mean(v), 4), "calls_per_step": len(v) // min(n_steps, 5)}
                for name, v in op_ms.items()}
     kernels["varlen_attn_fwd"]["tflops"] = round(f_fwd / (fwd_ms / 1e3) / 1e12, 2)
     kernels["varlen_attn_bwd"]["tflops"] = round(2 * f_fwd / (bwd_ms / 1e3) / 1e12, 2)
@@ -468,6 +480,9 @@ def measure_block(args, world, rank, local, n_steps, workload=None, e2e=True, cp
                      "flops_per_step": 3.0 * f_fwd, "peak_source": pk["source"]},
         "attn_tflops": round(attn_tflops, 2),
         "kernels": kernels,
+        "kernels_note": "CUDA events around every op of this library, 5 extra steps (host-inclusive: an op "
+                        "whose launch the GPU waited for includes the wait); the roofline uses events around "
+                        "the attention kernels only, over a second pass of the timed steps",
         "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
@@ -582,8 +597,8 @@ def run_full_step(args, world, rank, local):
         dist.barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    timer = ops.OpTimer()
-    ops.install_timer(timer)
+    counter = ops.OpTimer(names=())  # counts this library's launches; no events in the timed steps
+    ops.install_timer(counter)
     with ClockSampler(local) as clocks:
         for i in range(args.steps):
             starts[i].record()
@@ -591,8 +606,22 @@ def run_full_step(args, world, rank, local):
             ends[i].record()
         torch.cuda.synchronize()
     ops.install_timer(None)
-    op_ms = timer.elapsed_ms()
     step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    # a second pass of the same steps with events around the attention kernels only (the
+    # roofline), then a few with events around every op of this library (the kernel table)
+    n_inst = min(args.steps, 5)
+    timer = ops.OpTimer(names=("varlen_attn_fwd", "varlen_attn_bwd"))
+    ops.install_timer(timer)
+    for i in range(args.steps):
+        step(ids, mask, labels)
+    ops.install_timer(None)
+    attn_ms = timer.elapsed_ms()
+    timer = ops.OpTimer()
+    ops.install_timer(timer)
+    for i in range(n_inst):
+        step(ids, mask, labels)
+    ops.install_timer(None)
+    op_ms = timer.elapsed_ms()
     ar_ms = statistics.mean(a.elapsed_time(b) for a, b in ar_events) if ar_events else 0.0
     total_ms = sum(step_ms)
     rank_ms = [total_ms / args.steps]
@@ -640,10 +669,10 @@ def run_full_step(args, world, rank, local):
         return
     pk = peaks()
     f_fwd = causal_flops(lengths, n_heads=QWEN25_15B["heads"]) * n_layers
-    fwd_ms = sum(op_ms.get("varlen_attn_fwd", [float("nan")])) / args.steps
-    bwd_ms = sum(op_ms.get("varlen_attn_bwd", [float("nan")])) / args.steps
+    fwd_ms = sum(attn_ms.get("varlen_attn_fwd", [float("nan")])) / args.steps
+    bwd_ms = sum(attn_ms.get("varlen_attn_bwd", [float("nan")])) / args.steps
     attn_tflops = 3.0 * f_fwd / ((fwd_ms + bwd_ms) / 1e3) / 1e12
-    kernels = {name: {"ms_per_step": round(sum(v) / args.steps, 4), "calls_per_step": len(v) // max(args.steps, 1)}
+    kernels = {name: {"ms_per_step": round(sum(v) / n_inst, 4), "calls_per_step": len(v) // n_inst}
                for name, v in op_ms.items()}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -667,7 +696,10 @@ def run_full_step(args, world, rank, local):
         "allreduce_ms_per_step": [round(v, 4) for v in rank_ar],
         "allreduce_bytes": bucket.nbytes,
         "kernels": kernels,
-        "gpu_launches": timer.launches,
+        "kernels_note": "CUDA events around every op of this library over 5 extra steps (host-inclusive: an op "
+                        "whose launch the GPU waited for includes the wait); the roofline uses events around the "
+                        "attention kernels only, over a second pass of the timed steps",
+        "gpu_launches": counter.launches,
         "clocks": clocks.summary(),
         "loss_last": round(float(h_loss[-1]), 5),
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",

@@ -559,8 +559,10 @@ def attn_qkv_bwd(dout, q, k, v, out, lse, cu_seqlens, max_len: int, scale: float
     args = (_t3(dout), _t3(q), _t3(k), _t3(v), _t3(out), _p(lse), _p(cu_seqlens), cu_seqlens.numel() - 1,
             int(max_len), T, Hq, Hk, D, float(scale), _p(cos), _p(sin), _p(frag), float(scaling), _p(dy),
             dy.stride(0), _dt(q), _p(workspace), _stream(q))
-    if _timer is None:
+    if _timer is None or (_timer.names is not None and "varlen_attn_bwd" not in _timer.names):
         rc = lib.decik_attn_qkv_bwd(*args)
+        if _timer is not None:
+            _timer.launches += 3
     else:  # the two stages timed apart: an event recorded between them by the library
         a, mid, b = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         mid.record()  # creates the event; the library records it again between the stages
@@ -582,11 +584,14 @@ def attn_qkv_bwd(dout, q, k, v, out, lse, cu_seqlens, max_len: int, scale: float
 # stream they launch on, and a count of this library's kernel launches.
 # ------------------------------------------------------------------------------------------------
 class OpTimer:
-    """Records (name, start event, end event) around ops while installed with ``install``."""
+    """Records (name, start event, end event) around ops while installed with ``install``, and
+    counts this library's kernel launches. With ``names`` only those ops get events (fewer host-side
+    event records, so the timed GPU work is not starved by the instrumentation)."""
 
-    def __init__(self):
+    def __init__(self, names=None):
         self.events = []
         self.launches = 0
+        self.names = None if names is None else set(names)
 
     def elapsed_ms(self) -> dict:
         torch.cuda.synchronize()
@@ -609,15 +614,17 @@ class _timed:
         self.name, self.launches = name, launches
 
     def __enter__(self):
-        if _timer is not None:
+        self.on = _timer is not None and (_timer.names is None or self.name in _timer.names)
+        if self.on:
             self.a = torch.cuda.Event(enable_timing=True)
             self.a.record()
         return self
 
     def __exit__(self, *exc):
         if _timer is not None:
-            b = torch.cuda.Event(enable_timing=True)
-            b.record()
-            _timer.events.append((self.name, self.a, b))
+            if self.on:
+                b = torch.cuda.Event(enable_timing=True)
+                b.record()
+                _timer.events.append((self.name, self.a, b))
             _timer.launches += self.launches
         return False
