@@ -35,8 +35,8 @@ SIGNATURES = {
     "decik_abi_version": (c_int, []),
     "decik_kernel_error": (c_int, [c_int]),
     "decik_wait_limit_selftest": (c_int, [ctypes.c_longlong, c_void_p, c_void_p]),
-    "decik_lora_b_ext": (c_int, [c_void_p, c_void_p, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
-    "decik_qkv_proj_fwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+    "decik_lora_b_ext": (c_int, [c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "decik_qkv_proj_fwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p,
                                    Tensor3, Tensor3, Tensor3, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int,
                                    c_int, c_int, c_int, c_void_p]),
     "decik_proj_dx": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,

@@ -40,8 +40,8 @@
 namespace decik {
 namespace attn {
 int* attn_error_word();
-int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
-                  int n_heads, int dtype, int* order, int box_rows);
+int make_tile_map_ex(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
+                     int n_heads, int dtype, int* order, int box_rows, int box_inner, int swizzle_bytes);
 int make_map_2d(CUtensorMap* map, const void* ptr, int dtype, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                 uint32_t box_inner, uint32_t box_outer);
 }  // namespace attn
@@ -55,8 +55,8 @@ constexpr int BM = 128, BK = 64, NTHREADS = 384, kEpiWarps = 8, kD = 128, kR = 1
 enum { EPI_QKV = 0, EPI_F32 = 1 };
 
 template <int EPI> struct Cfg;
-template <> struct Cfg<EPI_QKV> {  // two heads per tile
-  static constexpr int BN = 256, STAGES = 3;
+template <> struct Cfg<EPI_QKV> {  // two heads per tile; a CTA pair holds one head each of B
+  static constexpr int BN = 256, STAGES = 4;
   static constexpr bool B_MN = false;
 };
 template <> struct Cfg<EPI_F32> {  // 1536 / 192 = 8 column tiles: 1024 tiles at 16,384 tokens = 6.9 waves
@@ -64,23 +64,25 @@ template <> struct Cfg<EPI_F32> {  // 1536 / 192 = 8 column tiles: 1024 tiles at
   static constexpr bool B_MN = true;
 };
 
-template <int EPI>
+// PAIR: the tile is computed by a cluster of two CTAs with cta_group::2 MMAs (M = 256: each CTA
+// its own 128 rows of A; B split by its N columns, BN / 2 rows in each CTA's shared memory)
+template <int EPI, bool PAIR>
 struct Layout {
-  static constexpr int BN = Cfg<EPI>::BN, S = Cfg<EPI>::STAGES;
+  static constexpr int BN = Cfg<EPI>::BN;
+  static constexpr int S = PAIR ? Cfg<EPI>::STAGES : (EPI == EPI_QKV ? 3 : Cfg<EPI>::STAGES);
   static constexpr int A_BYTES = BM * BK * 2;  // 128 rows x 128 B, 128-byte swizzle
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = S * A_BYTES;
-  // per epilogue warp: EPI_F32 two 4 KB staging tiles (double buffer); EPI_QKV one 4 KB tile (a
-  // [32 rows x 64] half of a head) and its RoPE tables (cos, sin: 32 rows x 16 fp32, rows padded to
-  // 80 bytes so that each thread's row reads are conflict-free)
+  // per epilogue warp: EPI_F32 two 4 KB staging tiles (double buffer); EPI_QKV one 4 KB staging
+  // tile (the tile's two heads x [32 rows x 32 columns], 64-byte swizzle) and its RoPE tables (cos,
+  // sin: 32 rows x 16 fp32, the 16-byte pieces of a row XOR-swizzled by (row / 2) % 4 so that both
+  // the coalesced fills and each thread's row reads are conflict-free)
   static constexpr int OFF_STG = OFF_B + S * B_BYTES;
   static constexpr int STG_WARP = EPI == EPI_QKV ? 4096 : 8192;
   static constexpr int OFF_TAB = OFF_STG + kEpiWarps * STG_WARP;
-  static constexpr int TAB_WARP = EPI == EPI_QKV ? 2 * 32 * 80 : 0;
-  static constexpr int OFF_BIAS = OFF_TAB + kEpiWarps * TAB_WARP;  // QKV: fp32 bias of the tile's 2 heads
-  static constexpr int BIAS_BYTES = EPI == EPI_QKV ? 2 * kD * 4 : 0;
-  static constexpr int OFF_BAR = OFF_BIAS + BIAS_BYTES;
+  static constexpr int TAB_WARP = EPI == EPI_QKV ? 2 * 32 * 64 : 0;
+  static constexpr int OFF_BAR = OFF_TAB + kEpiWarps * TAB_WARP;
   static constexpr int N_BAR = 2 * S + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], done
   static constexpr int OFF_TMEM = OFF_BAR + 8 * N_BAR;
   static constexpr int SMEM = OFF_TMEM + 16 + 1024;  // + slack for the 1024-byte alignment
@@ -95,8 +97,7 @@ struct Params {
   int order[3];           // tile-map coordinate order of q, k, v (0: d, tok, head; 1: d, head, tok)
   int64_t M;
   int N, K, n_tiles_n, n_tiles;
-  const void* bias;       // EPI_QKV: 16-bit [N]
-  int lora;               // EPI_QKV: the extra K block (u x scaled lora_B) is added to the accumulators
+  int lora;               // EPI_QKV: the extra K block (u x [scaled lora_B | bias]) joins the K loop
   float scaling;
   const float* cosp;
   const float* sinp;
@@ -109,11 +110,18 @@ __device__ __forceinline__ float rnd(float x) {
   return Dt<T>::to_f(Dt<T>::from_f(x));
 }
 
-template <typename T, int EPI>
+template <typename T, int EPI, bool PAIR>
 __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_constant__ Params p) {
-  using L = Layout<EPI>;
+  using L = Layout<EPI, PAIR>;
   constexpr int BN = L::BN, S = L::S;
   constexpr bool BMN = Cfg<EPI>::B_MN;
+  static_assert(!(PAIR && BMN), "the pair path loads B K-major");
+  // PAIR: rank 0 is the leader: its mbarriers count both CTAs' loads and epilogues, its thread
+  // issues the MMAs; pairs walk tiles of 256 rows
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int n_units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  constexpr int TM = PAIR ? 2 * BM : BM;  // rows per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = smem_u32(smem);
@@ -131,17 +139,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full(b), 1);
-      mbar_init(acc_empty(b), kEpiWarps);
+      mbar_init(acc_empty(b), PAIR ? 2 * kEpiWarps : kEpiWarps);
     }
     mbar_init(done, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(sb + L::OFF_TMEM, 512);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(sb + L::OFF_TMEM, 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(sb + L::OFF_TMEM, 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the leader's barriers exist before the peer signals them
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + L::OFF_TMEM);
   const int nk = (p.K + BK - 1) / BK;
@@ -154,11 +168,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
       prefetch_tmap(&p.tb);
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / p.n_tiles_n) * BM, n0 = (tile % p.n_tiles_n) * BN;
+      for (int tile = unit; tile < p.n_tiles && ok; tile += n_units) {
+        // this CTA's A rows and B rows of the tile
+        const int m0 = (tile / p.n_tiles_n) * TM + static_cast<int>(rank) * BM;
+        const int n0 = (tile % p.n_tiles_n) * BN + static_cast<int>(rank) * (BN / 2) * (PAIR ? 1 : 0);
         for (int kb = 0; kb < nkt; ++kb, ++it) {
           const int s = static_cast<int>(it % S);
           if (it >= static_cast<uint32_t>(S) && !(ok = mbar_wait(empty(s), ((it / S) - 1) & 1, p.err, 301))) break;
+          if constexpr (PAIR) {
+            // both CTAs' bytes complete on the leader's full barrier
+            const uint32_t fb = map_to_rank(full(s), 0);
+            if (rank == 0) mbar_expect_tx(full(s), 2 * (L::A_BYTES + L::B_BYTES));
+            if (kb == nk) {
+              tma_load_2d_pair(sb + L::OFF_A + s * L::A_BYTES, &p.ta2, fb, 0, m0);
+              tma_load_2d_pair(sb + L::OFF_B + s * L::B_BYTES, &p.tb2, fb, 0, n0);
+            } else {
+              tma_load_2d_pair(sb + L::OFF_A + s * L::A_BYTES, &p.ta, fb, kb * BK, m0);
+              tma_load_2d_pair(sb + L::OFF_B + s * L::B_BYTES, &p.tb, fb, kb * BK, n0);
+            }
+            continue;
+          }
           mbar_expect_tx(full(s), L::A_BYTES + L::B_BYTES);
           if (kb == nk) {  // the LoRA K block: u [tokens, 64] against the scaled lora_B columns
             tma_load_2d(sb + L::OFF_A + s * L::A_BYTES, &p.ta2, full(s), 0, m0);
@@ -175,19 +204,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
           }
         }
       }
-      // wind down: the loads in flight land before the CTA leaves
-      for (uint32_t j = it > static_cast<uint32_t>(S) ? it - S : 0; j < it; ++j)
-        mbar_wait(full(static_cast<int>(j % S)), (j / S) & 1, p.err, 302);
+      // wind down: the loads in flight land before the CTA leaves (a pair's loads all complete on
+      // the leader's barriers; the peer stays until the leader has waited, at the closing cluster sync)
+      if (rank == 0)
+        for (uint32_t j = it > static_cast<uint32_t>(S) ? it - S : 0; j < it; ++j)
+          mbar_wait(full(static_cast<int>(j % S)), (j / S) & 1, p.err, 302);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issue (one thread)
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       constexpr int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-      const uint32_t idesc = idesc_f16(ab, BM, BN, 0, BMN ? 1 : 0);
+      const uint32_t idesc = idesc_f16(ab, TM, BN, 0, BMN ? 1 : 0);
       uint32_t it = 0;
       int i = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x, ++i) {
+      for (int tile = unit; tile < p.n_tiles && ok; tile += n_units, ++i) {
         const int b = i & 1;
         if (i >= 2 && !(ok = mbar_wait(acc_empty(b), ((i >> 1) - 1) & 1, p.err, 311))) break;
         tc_fence_after();
@@ -202,15 +233,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
             const uint64_t ad = smem_desc_sw128(a + kk * 32, 16, 1024);
             const uint64_t bd = BMN ? smem_desc_sw128(bb + kk * 2048, 64 * BK * 2, 1024)
                                     : smem_desc_sw128(bb + kk * 32, 16, 1024);
-            umma_ss(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if constexpr (PAIR) umma_ss_pair(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            else umma_ss(d, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          umma_commit(empty(s));
+          if constexpr (PAIR) umma_commit_pair_mc(empty(s), 0x3);  // both CTAs' stage s is free
+          else umma_commit(empty(s));
         }
         if (!ok) break;
-        umma_commit(acc_full(b));
+        if constexpr (PAIR) umma_commit_pair_mc(acc_full(b), 0x3);
+        else umma_commit(acc_full(b));
       }
       // every MMA this thread issued has completed before TMEM is freed
-      umma_commit(done);
+      if constexpr (PAIR) umma_commit_pair_mc(done, 0x1);
+      else umma_commit(done);
       mbar_wait(done, 0, p.err, 313);
     }
   } else if (warp >= 4) {
@@ -221,13 +256,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
     const uint32_t lane_base = static_cast<uint32_t>(32 * q4) << 16;
     uint32_t n_chunks = 0;  // EPI_F32: staging tiles used so far (double buffer)
     int i = 0;
-    for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x, ++i) {
-      const int m0 = (tile / p.n_tiles_n) * BM, n0 = (tile % p.n_tiles_n) * BN;
+    // PAIR: this CTA's accumulator rows are its own 128 rows of the tile, all BN columns; the
+    // buffer is released on the leader's barrier
+    const uint32_t acc_empty_leader0 = PAIR ? map_to_rank(acc_empty(0), 0) : acc_empty(0);
+    const uint32_t acc_empty_leader1 = PAIR ? map_to_rank(acc_empty(1), 0) : acc_empty(1);
+    for (int tile = unit; tile < p.n_tiles; tile += n_units, ++i) {
+      const int m0 = (tile / p.n_tiles_n) * TM + static_cast<int>(rank) * BM, n0 = (tile % p.n_tiles_n) * BN;
       const int b = i & 1;
       bool ok = mbar_wait(acc_full(b), (i >> 1) & 1, p.err, 321);
-      // EPI_QKV: the warpgroup leaves together (it meets at named barriers below), and this barrier
-      // also orders the previous tile's reads of bias_s / b16_s before they are rewritten
-      if constexpr (EPI == EPI_QKV) ok = named_bar_and(1 + wg, 128, ok);
+      // EPI_QKV: the eight epilogue warps leave together (they meet at named barriers below)
+      if constexpr (EPI == EPI_QKV) ok = named_bar_and(1, 256, ok);
       if (!ok) break;
       tc_fence_after();
       const uint32_t tacc = tmem + lane_base + b * 256;
@@ -256,15 +294,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
           }
         }
       } else {
-        const int hh = n0 / kD + wg;  // head of this warpgroup: q heads, then k, then v
-        const int kind = hh < p.hq ? 0 : (hh < p.hq + p.hk ? 1 : 2);
-        const bool rope = kind != 2;
-        const int tid = threadIdx.x - 128 - 128 * wg;  // 0..127 in the warpgroup
-        float* bias_s = reinterpret_cast<float*>(smem + L::OFF_BIAS) + wg * kD;
-        bias_s[tid] = Dt<T>::to_f(static_cast<const T*>(p.bias)[hh * kD + tid]);
-        named_bar(1 + wg, 128);
-        const int head = kind == 0 ? hh : (kind == 1 ? hh - p.hq : hh - p.hq - p.hk);
-        float* tab = reinterpret_cast<float*>(smem + L::OFF_TAB + ew * L::TAB_WARP);  // [cos | sin][32][20]
+        // Warpgroup wg takes head_dim columns [32 wg, 32 wg + 32) and their RoPE partners + 64 of
+        // both heads of the tile, so each RoPE table piece is loaded once for two heads.
+        const int h0 = n0 / kD;  // the tile's first head: q heads, then k, then v
+        const auto kind_of = [&](int hh) { return hh < p.hq ? 0 : (hh < p.hq + p.hk ? 1 : 2); };
+        const int kind2[2] = {kind_of(h0), kind_of(h0 + 1)};
+        const bool any_rope = kind2[0] != 2 || kind2[1] != 2;
+        uint8_t* tab = smem + L::OFF_TAB + ew * L::TAB_WARP;  // [cos | sin][32 rows][64 B]
         // the warp's 32 table rows of columns [d0, d0 + 16): 2 tables x 32 rows x 4 pieces of 16 B,
         // eight coalesced cp.async per lane (rows past the end read the last row; not stored)
         const auto load_tab = [&](int d0) {
@@ -274,61 +310,76 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
             const int which = piece >> 7, row = (piece >> 2) & 31, c4 = piece & 3;
             const int64_t rr = row0 + row < p.M ? row0 + row : p.M - 1;
             const float* src = (which ? p.sinp : p.cosp) + rr * kD + d0 + 4 * c4;
-            ptx::cp_async16_ca(ptx::smem_u32(tab + which * 32 * 20 + row * 20 + 4 * c4), src);  // the other
-            // warpgroup reads the same rows for its head: through L1
+            ptx::cp_async16_ca(ptx::smem_u32(tab + which * 2048 + row * 64 + ((c4 ^ ((row >> 1) & 3)) << 4)), src);
           }
           ptx::cp_async_commit();
         };
         // two passes: outputs d in [0, 64) (x[d] cos[d] - x[d + 64] sin[d]), then d in [64, 128)
-        // (x[d] cos[d] + x[d - 64] sin[d]); each fills the staging tile and leaves by one TMA store
+        // (x[d] cos[d] + x[d - 64] sin[d]); each fills the staging tile and leaves by two TMA stores
 #pragma unroll 1
         for (int pass = 0; pass < 2; ++pass) {
-          if (lane == 0) bulk_wait_read0();  // the previous store has read the staging tile
+          const int lo0 = 32 * wg;  // this warpgroup's columns in [0, 64)
+          if (lane == 0) bulk_wait_read0();  // the previous stores have read the staging tile
           __syncwarp();
-          if (rope) load_tab(pass * kD / 2);
+          if (any_rope) load_tab(pass * kD / 2 + lo0);
 #pragma unroll 1
-          for (int c = 0; c < kD / 2; c += 16) {
+          for (int c = 0; c < 32; c += 16) {
             float cs[16], sn[16];
-            if (rope) {
+            if (any_rope) {
               ptx::cp_async_wait<0>();
               __syncwarp();
 #pragma unroll
-              for (int e4 = 0; e4 < 16; e4 += 4) {
-                const float4 a = *reinterpret_cast<const float4*>(tab + lane * 20 + e4);
-                const float4 b2 = *reinterpret_cast<const float4*>(tab + 32 * 20 + lane * 20 + e4);
-                cs[e4] = a.x; cs[e4 + 1] = a.y; cs[e4 + 2] = a.z; cs[e4 + 3] = a.w;
-                sn[e4] = b2.x; sn[e4 + 1] = b2.y; sn[e4 + 2] = b2.z; sn[e4 + 3] = b2.w;
+              for (int j4 = 0; j4 < 4; ++j4) {
+                const int off = lane * 64 + ((j4 ^ ((lane >> 1) & 3)) << 4);
+                const float4 a = *reinterpret_cast<const float4*>(tab + off);
+                const float4 b2 = *reinterpret_cast<const float4*>(tab + 2048 + off);
+                cs[4 * j4] = a.x; cs[4 * j4 + 1] = a.y; cs[4 * j4 + 2] = a.z; cs[4 * j4 + 3] = a.w;
+                sn[4 * j4] = b2.x; sn[4 * j4 + 1] = b2.y; sn[4 * j4 + 2] = b2.z; sn[4 * j4 + 3] = b2.w;
               }
               __syncwarp();
-              if (c + 16 < kD / 2) load_tab(pass * kD / 2 + c + 16);  // next columns, during the math
-            }
-            uint32_t alo[16], ahi[16];
-            tmem_ld16(tacc + wg * kD + c, alo);
-            tmem_ld16(tacc + wg * kD + c + kD / 2, ahi);
-            tmem_ld_wait();
-            float o[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int d = c + e;
-              // the accumulator holds x16 W^T + u (scaled lora_B)^T in fp32; the bias joins it here
-              const float lo = __fadd_rn(__uint_as_float(alo[e]), bias_s[d]);
-              const float hi = __fadd_rn(__uint_as_float(ahi[e]), bias_s[d + kD / 2]);
-              if (!rope) o[e] = pass ? hi : lo;
-              else if (pass == 0) o[e] = __fadd_rn(__fmul_rn(lo, cs[e]), __fmul_rn(-hi, sn[e]));
-              else o[e] = __fadd_rn(__fmul_rn(hi, cs[e]), __fmul_rn(lo, sn[e]));
+              if (c == 0) load_tab(pass * kD / 2 + lo0 + 16);  // the next columns, during the math
             }
 #pragma unroll
-            for (int j = 0; j < 2; ++j)
-              *reinterpret_cast<uint4*>(stg + lane * 128 + (((c / 8 + j) ^ (lane & 7)) << 4)) =
-                  pack8<T>(*reinterpret_cast<const float(*)[8]>(&o[8 * j]));
+            for (int hd = 0; hd < 2; ++hd) {
+              const int kind = kind2[hd];
+              const bool rope = kind != 2;
+              uint32_t alo[16], ahi[16];
+              const int lo = lo0 + c;  // x[lo] pairs with x[lo + 64]
+              tmem_ld16(tacc + hd * kD + lo, alo);
+              tmem_ld16(tacc + hd * kD + lo + kD / 2, ahi);
+              tmem_ld_wait();
+              float o[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                // the accumulator holds x16 W^T + u (scaled lora_B)^T + 1 . bias in fp32
+                const float xl = __uint_as_float(alo[e]);
+                const float xh = __uint_as_float(ahi[e]);
+                if (!rope) o[e] = pass ? xh : xl;
+                else if (pass == 0) o[e] = __fadd_rn(__fmul_rn(xl, cs[e]), __fmul_rn(-xh, sn[e]));
+                else o[e] = __fadd_rn(__fmul_rn(xh, cs[e]), __fmul_rn(xl, sn[e]));
+              }
+              // [32 rows x 32 columns] per head, 64-byte rows, 16-byte pieces swizzled by (row / 2) % 4
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const int piece = c / 8 + j;
+                *reinterpret_cast<uint4*>(stg + hd * 2048 + lane * 64 + ((piece ^ ((lane >> 1) & 3)) << 4)) =
+                    pack8<T>(*reinterpret_cast<const float(*)[8]>(&o[8 * j]));
+              }
+            }
           }
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
             if (row0 < p.M) {
               const int t = static_cast<int>(row0);
-              if (p.order[kind] == 0) tma_store_3d(&p.to[kind], stg_s, pass * kD / 2, t, head);
-              else tma_store_3d(&p.to[kind], stg_s, pass * kD / 2, head, t);
+              const int d = pass * kD / 2 + lo0;
+#pragma unroll
+              for (int hd = 0; hd < 2; ++hd) {
+                const int hh = h0 + hd, kind = kind2[hd];
+                const int head = kind == 0 ? hh : (kind == 1 ? hh - p.hq : hh - p.hq - p.hk);
+                if (p.order[kind] == 0) tma_store_3d(&p.to[kind], stg_s + hd * 2048, d, t, head);
+                else tma_store_3d(&p.to[kind], stg_s + hd * 2048, d, head, t);
+              }
             }
             bulk_commit();
           }
@@ -336,16 +387,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty(b));
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_remote(b ? acc_empty_leader1 : acc_empty_leader0);
+        else mbar_arrive(acc_empty(b));
+      }
     }
     if (lane == 0) bulk_wait0();  // the stores have finished before the CTA leaves
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // neither CTA frees TMEM or leaves while its peer still works
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem, 512);
+    else tmem_dealloc(tmem, 512);
   }
 }
 
@@ -369,7 +425,7 @@ __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const fl
   __shared__ __align__(16) T as[2 * kR * kCastLd];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kCastTok;
-  const bool lora = u != nullptr;
+  const bool lora = a16 != nullptr;
   const int cc = 4 * lane;  // this thread's 4 columns of a chunk; rows warp + 8 i
   float4 cur[8], nxt[8];
   auto load = [&](int k0, float4 (&dst)[8]) {
@@ -434,8 +490,18 @@ __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const fl
       if (ta < n_tok) *reinterpret_cast<uint32_t*>(u + ta * kULd + col) = Dt<T>::pack2(acc[n][0], acc[n][1]);
       if (tb < n_tok) *reinterpret_cast<uint32_t*>(u + tb * kULd + col) = Dt<T>::pack2(acc[n][2], acc[n][3]);
     }
-    const int64_t tz = t0 + (tid >> 2);  // the zero half: 64 tokens x 4 pieces of 16 bytes
-    if (tz < n_tok) *reinterpret_cast<uint4*>(u + tz * kULd + 2 * kR + 8 * (tid & 3)) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  // the second half of u's row: a 1 in column 32 (it multiplies the bias row of the extra K block),
+  // zeros after it; without LoRA the first half is zero too. 64 tokens x 8 pieces of 16 bytes
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int piece = tid + kCastThreads * i;
+    const int64_t tz = t0 + (piece >> 3);
+    const int pc = piece & 7;
+    if (tz >= n_tok || (lora && pc < 4)) continue;
+    uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    if (pc == 4) z.x = Dt<T>::pack2(1.f, 0.f);
+    *reinterpret_cast<uint4*>(u + tz * kULd + 8 * pc) = z;
   }
 }
 
@@ -559,34 +625,57 @@ __global__ void __launch_bounds__(kGradThreads) lora_grad_kernel(const T* __rest
   }
 }
 
-// The LoRA K block's B operand [n_proj, 64]: row c of a q head holds scaling B_q[c] in columns
-// 0..15 (against u_q), row c of a v head scaling B_v[c] in columns 16..31 (against u_v), every
-// other entry 0; rounded to T.
+// The extra K block's B operand [n_proj, 64]: row c of a q head holds scaling B_q[c] in columns
+// 0..15 (against u_q), row c of a v head scaling B_v[c] in columns 16..31 (against u_v); every row
+// holds its bias in column 32 (against the 1 in u's column 32); other entries 0; rounded to T (the
+// bias is already T). bq / bv may be NULL (no LoRA).
 template <typename T>
 __global__ void lora_b_ext_kernel(const float* __restrict__ bq, const float* __restrict__ bv, float scaling,
-                                  T* __restrict__ out, int hq, int hk) {
+                                  const T* __restrict__ bias, T* __restrict__ out, int hq, int hk) {
   const int n_proj = (hq + 2 * hk) * kD;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;  // one 8-element piece of a row
   if (i >= n_proj * 8) return;
   const int row = i >> 3, piece = i & 7;
   float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   const float* src = nullptr;
-  if (row < hq * kD && piece < 2) src = bq + row * kR + 8 * piece;
-  else if (row >= (hq + hk) * kD && piece >= 2 && piece < 4) src = bv + (row - (hq + hk) * kD) * kR + 8 * (piece - 2);
+  if (bq != nullptr && row < hq * kD && piece < 2) src = bq + row * kR + 8 * piece;
+  else if (bv != nullptr && row >= (hq + hk) * kD && piece >= 2 && piece < 4)
+    src = bv + (row - (hq + hk) * kD) * kR + 8 * (piece - 2);
   if (src != nullptr) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) v[e] = scaling * src[e];
   }
+  if (piece == 4) v[0] = Dt<T>::to_f(bias[row]);
   *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * 4 * kR + 8 * piece) = pack8<T>(v);
 }
 
-template <typename T, int EPI>
+template <typename T, int EPI, bool PAIR>
 int launch_gemm(const Params& p, cudaStream_t s, const char* what) {
   static std::atomic<unsigned long long> set{0};
-  if (int rc = ensure_dyn_smem(proj_gemm_kernel<T, EPI>, Layout<EPI>::SMEM, set, what)) return rc;
-  const int grid = p.n_tiles < sm_count() ? p.n_tiles : sm_count();
-  proj_gemm_kernel<T, EPI><<<grid, NTHREADS, Layout<EPI>::SMEM, s>>>(p);
-  return check_launch(what);
+  constexpr int smem = Layout<EPI, PAIR>::SMEM;
+  if (int rc = ensure_dyn_smem(proj_gemm_kernel<T, EPI, PAIR>, smem, set, what)) return rc;
+  if constexpr (!PAIR) {
+    const int grid = p.n_tiles < sm_count() ? p.n_tiles : sm_count();
+    proj_gemm_kernel<T, EPI, PAIR><<<grid, NTHREADS, smem, s>>>(p);
+    return check_launch(what);
+  } else {
+    const int pairs = p.n_tiles < sm_count() / 2 ? p.n_tiles : sm_count() / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(NTHREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, proj_gemm_kernel<T, EPI, PAIR>, p);
+    if (e != cudaSuccess) return set_error(DECIK_ERR_CUDA, "%s: cluster launch: %s", what, cudaGetErrorString(e));
+    return check_launch(what);
+  }
 }
 
 }  // namespace
@@ -595,27 +684,31 @@ int launch_gemm(const Params& p, cudaStream_t s, const char* what) {
 
 using decik::set_error;
 
-extern "C" int decik_lora_b_ext(const float* b_q, const float* b_v, float scaling, void* out, int n_heads, int n_kv,
-                                int dtype, void* stream) {
+extern "C" int decik_lora_b_ext(const float* b_q, const float* b_v, float scaling, const void* bias, void* out,
+                                int n_heads, int n_kv, int dtype, void* stream) {
   using namespace decik;
   using namespace decik::proj;
-  if (n_heads <= 0 || n_kv <= 0 || !b_q || !b_v || !out || !aligned16(out))
-    return set_error(DECIK_ERR_INVALID, "lora_b_ext: heads %d/%d or a NULL / unaligned pointer", n_heads, n_kv);
+  if (n_heads <= 0 || n_kv <= 0 || (b_q == nullptr) != (b_v == nullptr) || !bias || !out || !aligned16(out))
+    return set_error(DECIK_ERR_INVALID, "lora_b_ext: heads %d/%d, b_q / b_v (both or neither), bias, or an unaligned out",
+                     n_heads, n_kv);
   const int n = (n_heads + 2 * n_kv) * kD * 8;
   cudaStream_t s = as_stream(stream);
-  if (dtype == DECIK_BF16)
-    lora_b_ext_kernel<__nv_bfloat16><<<(n + 255) / 256, 256, 0, s>>>(b_q, b_v, scaling,
-                                                                     static_cast<__nv_bfloat16*>(out), n_heads, n_kv);
-  else if (dtype == DECIK_F16)
-    lora_b_ext_kernel<__half><<<(n + 255) / 256, 256, 0, s>>>(b_q, b_v, scaling, static_cast<__half*>(out), n_heads,
-                                                              n_kv);
-  else
+  if (dtype == DECIK_BF16) {
+    using T = __nv_bfloat16;
+    lora_b_ext_kernel<T><<<(n + 255) / 256, 256, 0, s>>>(b_q, b_v, scaling, static_cast<const T*>(bias),
+                                                         static_cast<T*>(out), n_heads, n_kv);
+  } else if (dtype == DECIK_F16) {
+    using T = __half;
+    lora_b_ext_kernel<T><<<(n + 255) / 256, 256, 0, s>>>(b_q, b_v, scaling, static_cast<const T*>(bias),
+                                                         static_cast<T*>(out), n_heads, n_kv);
+  } else {
     return set_error(DECIK_ERR_INVALID, "lora_b_ext: dtype %d", dtype);
+  }
   return check_launch("lora_b_ext");
 }
 
-extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* bias,
-                                  const void* lora_b_ext, const float* cosp, const float* sinp, decik_tensor3_mut q,
+extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* ext_b,
+                                  int lora, const float* cosp, const float* sinp, decik_tensor3_mut q,
                                   decik_tensor3_mut k, decik_tensor3_mut v, void* x16, int64_t ldx16, void* u,
                                   int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim, int dtype,
                                   void* stream) {
@@ -626,41 +719,38 @@ extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat
       hidden <= 0 || hidden % 128 != 0 || (n_heads + 2 * n_kv) % 2 != 0)
     return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: T=%lld hidden %d heads %d/%d head_dim %d (needs head_dim 128, "
                      "hidden %% 128 == 0, an even head count)", (long long)n_tok, hidden, n_heads, n_kv, head_dim);
-  if (!x || !w_cat || !bias || !cosp || !sinp || !q.ptr || !k.ptr || !v.ptr || !x16 || ((lora_b_ext == nullptr) != (u == nullptr)))
-    return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: NULL pointer (lora_b_ext and u go together)");
+  if (!x || !w_cat || !ext_b || !cosp || !sinp || !q.ptr || !k.ptr || !v.ptr || !x16 || !u)
+    return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: NULL pointer");
   if (ldx < hidden || ldw < hidden || ldx16 < hidden)
     return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: row strides shorter than hidden");
-  if (ldx % 4 || ldw % 8 || ldx16 % 8 || !aligned16(x) || !aligned16(w_cat) || !aligned16(x16) ||
-      (u && !aligned16(u)) || (lora_b_ext && !aligned16(lora_b_ext)) || !aligned16(cosp) || !aligned16(sinp))
+  if (ldx % 4 || ldw % 8 || ldx16 % 8 || !aligned16(x) || !aligned16(w_cat) || !aligned16(x16) || !aligned16(u) ||
+      !aligned16(ext_b) || !aligned16(cosp) || !aligned16(sinp))
     return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: rows and pointers need 16-byte alignment");
   if (dtype != DECIK_BF16 && dtype != DECIK_F16) return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: dtype %d", dtype);
   cudaStream_t s = as_stream(stream);
   const int n_proj = (n_heads + 2 * n_kv) * kD;
+  constexpr int BN = Cfg<EPI_QKV>::BN;
   Params p{};
   int ord = 0;
   if (int rc = attn::make_map_2d(&p.ta, x16, dtype, hidden, n_tok, ldx16 * 2, 64, BM)) return rc;
-  if (int rc = attn::make_map_2d(&p.tb, w_cat, dtype, hidden, n_proj, ldw * 2, 64, Cfg<EPI_QKV>::BN)) return rc;
-  p.lora = lora_b_ext != nullptr;
-  if (p.lora) {
-    if (int rc = attn::make_map_2d(&p.ta2, u, dtype, 4 * kR, n_tok, 4 * kR * 2, 64, BM)) return rc;
-    if (int rc = attn::make_map_2d(&p.tb2, lora_b_ext, dtype, 4 * kR, n_proj, 4 * kR * 2, 64, Cfg<EPI_QKV>::BN))
-      return rc;
-  }
+  if (int rc = attn::make_map_2d(&p.tb, w_cat, dtype, hidden, n_proj, ldw * 2, 64, BN / 2)) return rc;
+  p.lora = 1;  // the extra K block always runs: it carries the bias
+  if (int rc = attn::make_map_2d(&p.ta2, u, dtype, 4 * kR, n_tok, 4 * kR * 2, 64, BM)) return rc;
+  if (int rc = attn::make_map_2d(&p.tb2, ext_b, dtype, 4 * kR, n_proj, 4 * kR * 2, 64, BN / 2)) return rc;
   const decik_tensor3_mut outs[3] = {q, k, v};
   const int heads[3] = {n_heads, n_kv, n_kv};
   for (int j = 0; j < 3; ++j) {
-    if (int rc = attn::make_tile_map(&p.to[j], outs[j].ptr, outs[j].tok_stride, outs[j].head_stride, n_tok, heads[j],
-                                     dtype, &ord, 32))
+    if (int rc = attn::make_tile_map_ex(&p.to[j], outs[j].ptr, outs[j].tok_stride, outs[j].head_stride, n_tok,
+                                        heads[j], dtype, &ord, 32, 32, 64))
       return rc;
     p.order[j] = ord;
   }
   p.M = n_tok;
   p.N = n_proj;
   p.K = hidden;
-  p.n_tiles_n = n_proj / Cfg<EPI_QKV>::BN + (n_proj % Cfg<EPI_QKV>::BN ? 1 : 0);
-  const int64_t m_tiles = (n_tok + BM - 1) / BM;
+  p.n_tiles_n = n_proj / BN + (n_proj % BN ? 1 : 0);
+  const int64_t m_tiles = (n_tok + 2 * BM - 1) / (2 * BM);  // CTA pairs: 256 rows per tile
   p.n_tiles = static_cast<int>(m_tiles * p.n_tiles_n);
-  p.bias = bias;
   p.cosp = cosp;
   p.sinp = sinp;
   p.hq = n_heads;
@@ -668,20 +758,21 @@ extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat
   p.err = attn::attn_error_word();
   // x16 and u first (the GEMM's A operands), then the GEMM + epilogue
   const int grid_cast = static_cast<int>((n_tok + kCastTok - 1) / kCastTok);
+  const int64_t a_off = static_cast<int64_t>(n_proj) * ldw;
   if (dtype == DECIK_BF16) {
     using T = __nv_bfloat16;
     x_cast_lora_down_kernel<T><<<grid_cast, kCastThreads, 0, s>>>(
-        x, ldx, static_cast<const T*>(w_cat) + static_cast<int64_t>(n_proj) * ldw, ldw, static_cast<T*>(x16), ldx16,
+        x, ldx, lora ? static_cast<const T*>(w_cat) + a_off : nullptr, ldw, static_cast<T*>(x16), ldx16,
         static_cast<T*>(u), n_tok, hidden);
     if (int rc = check_launch("x_cast_lora_down")) return rc;
-    return launch_gemm<T, EPI_QKV>(p, s, "qkv_proj_gemm");
+    return launch_gemm<T, EPI_QKV, true>(p, s, "qkv_proj_gemm");
   }
   using T = __half;
   x_cast_lora_down_kernel<T><<<grid_cast, kCastThreads, 0, s>>>(
-      x, ldx, static_cast<const T*>(w_cat) + static_cast<int64_t>(n_proj) * ldw, ldw, static_cast<T*>(x16), ldx16,
+      x, ldx, lora ? static_cast<const T*>(w_cat) + a_off : nullptr, ldw, static_cast<T*>(x16), ldx16,
       static_cast<T*>(u), n_tok, hidden);
   if (int rc = check_launch("x_cast_lora_down")) return rc;
-  return launch_gemm<T, EPI_QKV>(p, s, "qkv_proj_gemm");
+  return launch_gemm<T, EPI_QKV, true>(p, s, "qkv_proj_gemm");
 }
 
 extern "C" int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const void* w_cat, int64_t ldw, float* dx,
@@ -709,8 +800,8 @@ extern "C" int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const vo
   p.n_tiles = static_cast<int>(((n_tok + BM - 1) / BM) * p.n_tiles_n);
   p.err = attn::attn_error_word();
   cudaStream_t s = as_stream(stream);
-  if (dtype == DECIK_BF16) return launch_gemm<__nv_bfloat16, EPI_F32>(p, s, "proj_dx_gemm");
-  return launch_gemm<__half, EPI_F32>(p, s, "proj_dx_gemm");
+  if (dtype == DECIK_BF16) return launch_gemm<__nv_bfloat16, EPI_F32, false>(p, s, "proj_dx_gemm");
+  return launch_gemm<__half, EPI_F32, false>(p, s, "proj_dx_gemm");
 }
 
 extern "C" int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, int64_t ldx, const void* u,

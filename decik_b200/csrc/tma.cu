@@ -49,8 +49,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // box_rows x 64-element half tile with the 128-byte swizzle (the UMMA K-major / MN-major canonical layout).
 // The two outer dimensions are ordered by increasing stride: order 0 = (d, token, head),
 // order 1 = (d, head, token); the kernel passes its coordinates in that order.
+int make_tile_map_ex(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
+                     int n_heads, int dtype, int* order, int box_rows, int box_inner, int swizzle_bytes);
+
 int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
                   int n_heads, int dtype, int* order, int box_rows) {
+  return make_tile_map_ex(map, ptr, tok_stride, head_stride, n_tok, n_heads, dtype, order, box_rows, 64, 128);
+}
+
+// The same map with a box of box_inner elements of head_dim and the given swizzle (128 or 64 bytes;
+// box_inner x 2 bytes must equal it).
+int make_tile_map_ex(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
+                     int n_heads, int dtype, int* order, int box_rows, int box_inner, int swizzle_bytes) {
+  if (box_inner * 2 != swizzle_bytes || (swizzle_bytes != 128 && swizzle_bytes != 64))
+    return set_error(DECIK_ERR_INVALID, "make_tile_map: box of %d elements with a %d-byte swizzle", box_inner,
+                     swizzle_bytes);
   auto fn = encode_fn();
   if (fn == nullptr) return set_error(DECIK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const bool tok_inner = tok_stride <= head_stride || n_heads == 1;
@@ -63,17 +76,18 @@ int make_tile_map(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t
     dims[2] = static_cast<cuuint64_t>(n_heads);
     strides[0] = static_cast<cuuint64_t>(tok_stride) * 2;
     strides[1] = static_cast<cuuint64_t>(n_heads == 1 ? tok_stride * n_tok : head_stride) * 2;
-    box[0] = 64; box[1] = static_cast<cuuint32_t>(box_rows); box[2] = 1;
+    box[0] = static_cast<cuuint32_t>(box_inner); box[1] = static_cast<cuuint32_t>(box_rows); box[2] = 1;
   } else {
     dims[1] = static_cast<cuuint64_t>(n_heads);
     dims[2] = static_cast<cuuint64_t>(n_tok);
     strides[0] = static_cast<cuuint64_t>(head_stride) * 2;
     strides[1] = static_cast<cuuint64_t>(tok_stride) * 2;
-    box[0] = 64; box[1] = 1; box[2] = static_cast<cuuint32_t>(box_rows);
+    box[0] = static_cast<cuuint32_t>(box_inner); box[1] = 1; box[2] = static_cast<cuuint32_t>(box_rows);
   }
   const CUtensorMapDataType dt = dtype == DECIK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(DECIK_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): tok_stride %lld head_stride %lld",
                      static_cast<int>(r), (long long)tok_stride, (long long)head_stride);

@@ -451,40 +451,45 @@ def qkv_epilogue_fwd(y: torch.Tensor, u: torch.Tensor | None, frag: torch.Tensor
     return q, k, v, u_out
 
 
-def lora_b_ext(b_q: torch.Tensor, b_v: torch.Tensor, scaling: float, dtype: torch.dtype) -> torch.Tensor:
-    """The LoRA K block's B operand [(Hq+2Hk)*D, 64] (decik_lora_b_ext): scaling . B_q rows against
-    u_q (columns 0..15), scaling . B_v rows against u_v (columns 16..31), zero elsewhere."""
-    _cuda(b_q, b_v)
+def lora_b_ext(b_q: torch.Tensor | None, b_v: torch.Tensor | None, scaling: float, bias: torch.Tensor,
+               dtype: torch.dtype, n_heads: int, n_kv: int) -> torch.Tensor:
+    """The B operand of the projection GEMM's extra K block [(Hq+2Hk)*D, 64] (decik_lora_b_ext):
+    scaling . B_q rows against u_q (columns 0..15), scaling . B_v rows against u_v (16..31), the
+    bias in column 32 of every row, zero elsewhere. b_q / b_v None: no LoRA."""
+    _cuda(b_q, b_v, bias)
     D = 128
-    n_heads, n_kv = b_q.shape[0] // D, b_v.shape[0] // D
-    out = torch.empty(((n_heads + 2 * n_kv) * D, 4 * LORA_RANK), dtype=dtype, device=b_q.device)
+    n_proj = (n_heads + 2 * n_kv) * D
+    bias16 = bias[:n_proj].to(dtype).contiguous()
+    out = torch.empty((n_proj, 4 * LORA_RANK), dtype=dtype, device=bias.device)
     with _timed("lora_b_ext", 1):
-        rc = _lib.lib().decik_lora_b_ext(_p(b_q.contiguous()), _p(b_v.contiguous()), float(scaling), _p(out), n_heads,
-                                         n_kv, _DT[dtype], _stream(b_q))
+        rc = _lib.lib().decik_lora_b_ext(_p(b_q.contiguous()) if b_q is not None else None,
+                                         _p(b_v.contiguous()) if b_v is not None else None, float(scaling),
+                                         _p(bias16), _p(out), n_heads, n_kv, _DT[dtype], _stream(bias))
     _lib.check(rc, "lora_b_ext")
     return out
 
 
-def qkv_proj_fwd(x: torch.Tensor, w_cat: torch.Tensor, bias_cat: torch.Tensor, b_ext: torch.Tensor | None,
-                 cos: torch.Tensor, sin: torch.Tensor, n_heads: int, n_kv: int):
+def qkv_proj_fwd(x: torch.Tensor, w_cat: torch.Tensor, ext_b: torch.Tensor, lora: bool, cos: torch.Tensor,
+                 sin: torch.Tensor, n_heads: int, n_kv: int):
     """The block's forward projections on tcgen05 (decik_qkv_proj_fwd): from x fp32 [T, H], w_cat
-    [(Hq+2Hk)*D + 32, H] (W_q, W_k, W_v rows, then A_q, A_v as lora_pack wrote them) and the LoRA
-    K block's B operand (lora_b_ext; None: no LoRA) returns x16 [T, H], u [T, 64] (u_q | u_v |
-    zeros; None without LoRA), q [Hq, T, D] and k [Hk, T, D] head-major with RoPE, v [T, Hk, D]."""
-    _cuda(x, w_cat, bias_cat, b_ext, cos, sin)
+    [(Hq+2Hk)*D (+ 32 with ``lora``), H] (W_q, W_k, W_v rows, then A_q, A_v as lora_pack wrote them)
+    and the extra K block's B operand (lora_b_ext: scaled lora_B and the bias) returns x16 [T, H],
+    u [T, 64] (u_q | u_v | 1 | zeros), q [Hq, T, D] and k [Hk, T, D] head-major with RoPE,
+    v [T, Hk, D]."""
+    _cuda(x, w_cat, ext_b, cos, sin)
     T, H = x.shape
     D = cos.shape[-1]
     dt, dev = w_cat.dtype, x.device
     if x.dtype != torch.float32 or x.stride(1) != 1 or w_cat.stride(1) != 1:
         raise RuntimeError("decik_b200 qkv_proj_fwd: x fp32 and w_cat with contiguous rows")
     x16 = torch.empty((T, H), dtype=dt, device=dev)
-    u = torch.empty((T, 4 * LORA_RANK), dtype=dt, device=dev) if b_ext is not None else None
+    u = torch.empty((T, 4 * LORA_RANK), dtype=dt, device=dev)
     q = torch.empty((n_heads, T, D), dtype=dt, device=dev)
     k = torch.empty((n_kv, T, D), dtype=dt, device=dev)
     v = torch.empty((T, n_kv, D), dtype=dt, device=dev)
     with _timed("qkv_proj_fwd", 2):
         rc = _lib.lib().decik_qkv_proj_fwd(
-            _p(x), x.stride(0), _p(w_cat), w_cat.stride(0), _p(bias_cat.contiguous()), _p(b_ext),
+            _p(x), x.stride(0), _p(w_cat), w_cat.stride(0), _p(ext_b), 1 if lora else 0,
             _p(cos.contiguous()), _p(sin.contiguous()), _t3any(q.transpose(0, 1)), _t3any(k.transpose(0, 1)),
             _t3any(v), _p(x16), x16.stride(0), _p(u), T, H, n_heads, n_kv, D, _dt(w_cat), _stream(x))
     _lib.check(rc, "qkv_proj_fwd")

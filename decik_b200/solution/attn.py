@@ -43,10 +43,10 @@ class FusedAttentionBlock(torch.autograd.Function):
     NF4Linear, LoRAPairFromNorm, FusedQKRope, VarlenSDPA), regrouped so each pass over the tokens
     does as much as it can:
 
-    forward   decik_qkv_proj_fwd: x16 = dt(x) and u = x16 [A_q; A_v]^T in one pass, then one
-              tcgen05 GEMM [x16 | u] [W_q; W_k; W_v | scaling B]^T (the LoRA-up is one more K
-              block) whose epilogue adds the bias and RoPE and writes head-major q / k and v
-              (the projection never reaches HBM); decik_varlen_attn_fwd.
+    forward   decik_qkv_proj_fwd: x16 = dt(x) and u = [x16 [A_q; A_v]^T | 1] in one pass, then one
+              tcgen05 GEMM [x16 | u] [W_q; W_k; W_v | scaling B, bias]^T (the LoRA-up and the bias
+              are one more K block) whose epilogue applies RoPE and writes head-major q / k and
+              v (the projection never reaches HBM); decik_varlen_attn_fwd.
     backward  decik_attn_qkv_bwd (attention backward, RoPE^T, du) into dy; decik_proj_dx:
               dX = dy . W_cat (one tcgen05 GEMM, fp32 out: the three NF4Linear input gradients and
               both LoRA input gradients); decik_lora_grads: dA = du^T x16, dB = scaling . g^T u.
@@ -68,9 +68,9 @@ class FusedAttentionBlock(torch.autograd.Function):
         r = a_q.shape[0]
         n_proj = (n_heads + 2 * n_kv) * D
         frag = ops.lora_pack(a_q, a_v, b_q, b_v, dt, a_out=w_cat[n_proj:])
-        b_ext = ops.lora_b_ext(b_q, b_v, scaling, dt)
+        ext_b = ops.lora_b_ext(b_q, b_v, scaling, bias_cat, dt, n_heads, n_kv)  # scaled lora_B + bias
         x32 = x if (x.dtype == torch.float32 and x.stride(-1) == 1) else x.float().contiguous()
-        x16, u, q, k, v = ops.qkv_proj_fwd(x32, w_cat, bias_cat, b_ext, cos, sin, n_heads, n_kv)
+        x16, u, q, k, v = ops.qkv_proj_fwd(x32, w_cat, ext_b, True, cos, sin, n_heads, n_kv)
         out, lse = ops.varlen_attn_fwd(q.transpose(0, 1), k.transpose(0, 1), v, cu_seqlens, max_len, scale)
         ctx.save_for_backward(x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu_seqlens, w_o)
         ctx.meta = (int(max_len), n_heads, n_kv, float(scaling), float(scale), r)

@@ -346,32 +346,32 @@ DECIK_API int decik_varlen_attn_bwd_noalloc(decik_tensor3 dout, decik_tensor3 q,
 /* ---------------------------------------------------------------------------------------------
  * The projection GEMMs of the attention block on tcgen05, with their epilogues fused.
  *
- * decik_lora_b_ext writes the B operand of the LoRA K block, out dt [n_proj, 64]
+ * decik_lora_b_ext writes the B operand of the GEMM's extra K block, out dt [n_proj, 64]
  * (n_proj = (n_heads + 2 n_kv) 128): row c of a q head = scaling . B_q[c] in columns 0..15, row c
- * of a v head = scaling . B_v[c] in columns 16..31, zero elsewhere. b_q fp32 [n_heads 128, 16],
- * b_v fp32 [n_kv 128, 16] (peft's lora_B weights). */
-DECIK_API int decik_lora_b_ext(const float* b_q, const float* b_v, float scaling, void* out, int n_heads, int n_kv,
-                               int dtype, void* stream);
+ * of a v head = scaling . B_v[c] in columns 16..31, every row its bias (dt [n_proj]) in column 32,
+ * zero elsewhere. b_q fp32 [n_heads 128, 16] and b_v fp32 [n_kv 128, 16] are peft's lora_B weights,
+ * or both NULL (no LoRA). */
+DECIK_API int decik_lora_b_ext(const float* b_q, const float* b_v, float scaling, const void* bias, void* out,
+                               int n_heads, int n_kv, int dtype, void* stream);
 
 /* decik_qkv_proj_fwd replaces, for one layer, the reference's three NF4Linear forwards
  * (solution/nf4.py:93-97: F.linear(x16, W, b16)), the LoRA pair's forward (solution/attn.py:217-228)
  * and FusedQKRope.forward (solution/attn.py:97-111, skc_rope_fwd_kernel :28-61). Two kernels:
- *   1. x16 = dt(x) [T, hidden] (ldx16) and u = dt(x16 . w_cat[n_proj : n_proj + 32]^T) into
- *      u [T, 64] (u_q | u_v | zeros; skipped without LoRA);
- *   2. one persistent tcgen05 GEMM over K = hidden (+ 64 with LoRA):
- *      acc = x16 . w_cat[0 : n_proj]^T + u . lora_b_ext^T   (fp32, in TMEM)
- *      q = rope(acc_q + b) head-major, k = rope(acc_k + b) head-major, v = acc_v + b, each rounded
- *      once to dt; RoPE in fp32 with separate roundings (no FMA). The projection never leaves the
- *      chip. The reference rounds the base projection and the LoRA product to dt before adding
- *      them; here they are added in fp32 (one rounding, at the end).
+ *   1. x16 = dt(x) [T, hidden] (ldx16) and u [T, 64] = [u_q | u_v | 1 | 0 ...] with
+ *      u_q | u_v = dt(x16 . w_cat[n_proj : n_proj + 32]^T) (zero when lora is 0);
+ *   2. one persistent tcgen05 GEMM on CTA pairs over K = hidden + 64:
+ *      acc = x16 . w_cat[0 : n_proj]^T + u . ext_b^T = base + LoRA-up + bias   (fp32, in TMEM)
+ *      q = rope(acc_q) head-major, k = rope(acc_k) head-major, v = acc_v, each rounded once to dt;
+ *      RoPE in fp32 with separate roundings (no FMA). The projection never leaves the chip. The
+ *      reference rounds the biased projection and the LoRA product to dt before adding them; here
+ *      they meet in the fp32 accumulator (one rounding, at the end).
  *   x       fp32 [T, hidden] (ldx)
- *   w_cat   dt [(n_proj + 32), hidden] (ldw): dequantised W_q, W_k, W_v rows, then A_q, A_v rows
- *           (the last 32 rows are read only with LoRA)
- *   bias    dt [n_proj]; lora_b_ext: decik_lora_b_ext's output, or NULL for no LoRA (then u NULL)
+ *   w_cat   dt [n_proj (+ 32 with lora), hidden] (ldw): dequantised W_q, W_k, W_v rows, then A_q, A_v
+ *   ext_b   decik_lora_b_ext's output (required: it carries the bias)
  *   cos/sin fp32 [T, 128]; q, k, v: [T, H, 128] views (any 16-byte aligned strides)
  * hidden % 128 == 0, head_dim 128, an even n_heads + 2 n_kv. */
-DECIK_API int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* bias,
-                                 const void* lora_b_ext, const float* cosp, const float* sinp, decik_tensor3_mut q,
+DECIK_API int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* ext_b,
+                                 int lora, const float* cosp, const float* sinp, decik_tensor3_mut q,
                                  decik_tensor3_mut k, decik_tensor3_mut v, void* x16, int64_t ldx16, void* u,
                                  int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim, int dtype,
                                  void* stream);

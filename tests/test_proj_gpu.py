@@ -61,17 +61,21 @@ def test_qkv_proj_fwd_matches_fp32(cuda_lib, T, hidden, hq, hk, dtype, lora):
     a_q = torch.randn(16, hidden, device=DEV) * hidden ** -0.5
     a_v = torch.randn(16, hidden, device=DEV) * hidden ** -0.5
     ops.lora_pack(a_q, a_v, b_q, b_v, dtype, a_out=w_cat[n_proj:])
-    b_ext = ops.lora_b_ext(b_q, b_v, 2.0, dtype) if lora else None
-    x16, u, q, k, v = ops.qkv_proj_fwd(x, w_cat, bias, b_ext, cos, sin, hq, hk)
+    ext = ops.lora_b_ext(b_q if lora else None, b_v if lora else None, 2.0, bias, dtype, hq, hk)
+    x16, u, q, k, v = ops.qkv_proj_fwd(x, w_cat, ext, lora, cos, sin, hq, hk)
     xr = x.to(dtype)
     assert torch.equal(x16, xr)
-    y = torch.mm(xr.float(), w_cat[:n_proj].float().t())
+    assert torch.equal(u[:, 32].float(), torch.ones_like(u[:, 32].float()))
+    assert torch.equal(u[:, 33:], torch.zeros_like(u[:, 33:]))
+    assert torch.equal(ext[:, 32], bias[:n_proj].to(dtype))
     if lora:
-        assert torch.equal(u[:, 32:], torch.zeros_like(u[:, 32:]))
         _close(u[:, :32], F.linear(xr, w_cat[n_proj:]), "u")
-        assert torch.equal(b_ext[:hq * D, :16], (b_q * 2.0).to(dtype)) and torch.equal(b_ext[hq * D:(hq + hk) * D], torch.zeros_like(b_ext[hq * D:(hq + hk) * D]))
-        y = y + torch.mm(u.float(), b_ext.float().t())
-    y = y + bias[:n_proj].float()
+        assert torch.equal(ext[:hq * D, :16], (b_q * 2.0).to(dtype))
+        assert torch.equal(ext[hq * D:(hq + hk) * D, :32], torch.zeros_like(ext[hq * D:(hq + hk) * D, :32]))
+    else:
+        assert torch.equal(u[:, :32], torch.zeros_like(u[:, :32]))
+    # the same arithmetic in fp32: base + LoRA-up + bias (through the ones column), RoPE
+    y = torch.mm(xr.float(), w_cat[:n_proj].float().t()) + torch.mm(u.float(), ext.float().t())
     rq = _rope32(y[:, :hq * D].view(T, hq, D), cos, sin).transpose(0, 1)
     rk = _rope32(y[:, hq * D:(hq + hk) * D].view(T, hk, D), cos, sin).transpose(0, 1)
     rv = y[:, (hq + hk) * D:].view(T, hk, D)
@@ -113,7 +117,7 @@ def test_proj_entry_points_reject_bad_arguments(cuda_lib):
     lib = _lib.lib()
     z = _lib.Tensor3(None, 0, 0)
     # hidden not a multiple of 64
-    assert lib.decik_qkv_proj_fwd(None, 100, None, 100, None, None, None, None, z, z, z, None, 100, None, 5, 100,
+    assert lib.decik_qkv_proj_fwd(None, 100, None, 100, None, 0, None, None, z, z, z, None, 100, None, 5, 100,
                                   12, 2, 128, _lib.BF16, None) == 1
     assert lib.decik_proj_dx(None, 8, 8, None, 8, None, 8, 5, 100, _lib.BF16, None) == 1
     assert lib.decik_lora_grads(None, 8, None, 8, None, 64, None, None, 1.0, 5, 100, 12, 2, _lib.BF16, None) == 1
