@@ -43,6 +43,13 @@ SIGNATURES = {
                               c_void_p]),
     "decik_lora_grads": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p,
                                  c_float, c_int64, c_int, c_int, c_int, c_int, c_void_p]),
+    "decik_transpose16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "decik_gemm16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_int64, c_int64, c_int, c_int,
+                             c_int, c_void_p]),
+    "decik_mlp_gate_up": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+                                  c_int64, c_int, c_int, c_int, c_void_p]),
+    "decik_mlp_down_grad": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+                                    c_int64, c_int, c_int, c_int, c_void_p]),
     "decik_pack_rows": (c_int, [c_void_p, c_int, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_void_p]),
     "decik_nf4_dequant_batch": (c_int, [c_void_p, c_int, c_int, c_void_p]),

@@ -43,7 +43,7 @@ int* attn_error_word();
 int make_tile_map_ex(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
                      int n_heads, int dtype, int* order, int box_rows, int box_inner, int swizzle_bytes);
 int make_map_2d(CUtensorMap* map, const void* ptr, int dtype, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                uint32_t box_inner, uint32_t box_outer);
+                uint32_t box_inner, uint32_t box_outer, int swizzle_bytes = 128);
 }  // namespace attn
 
 namespace proj {
@@ -52,15 +52,38 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128, BK = 64, NTHREADS = 384, kEpiWarps = 8, kD = 128, kR = 16;
-enum { EPI_QKV = 0, EPI_F32 = 1 };
+// epilogues: EPI_QKV the attention projections (RoPE, head-major q / k, v); EPI_F32 fp32 out;
+// EPI_STORE16 / EPI_STORE16_MN 16-bit out (B K-major / MN-major); EPI_SWIGLU the MLP's gate | up
+// with SwiGLU (writes gu and silu(gate) * up); EPI_DSWIGLU grad_hidden . with the SwiGLU backward
+// (writes [dgate | dup])
+enum { EPI_QKV = 0, EPI_F32 = 1, EPI_STORE16 = 2, EPI_STORE16_MN = 3, EPI_SWIGLU = 4, EPI_DSWIGLU = 5 };
 
 template <int EPI> struct Cfg;
 template <> struct Cfg<EPI_QKV> {  // two heads per tile; a CTA pair holds one head each of B
   static constexpr int BN = 256, STAGES = 4;
   static constexpr bool B_MN = false;
 };
-template <> struct Cfg<EPI_F32> {  // on CTA pairs: 256 x 256 tiles, each CTA two 64-column blocks of B
-  // (256 x 128 tiles with 6 stages measured 126 us against 90 us at T = 16,384, hidden 1536)
+// EPI_F32 / EPI_STORE16 produce outputs of hidden = 1536 columns (dX, the down projection):
+// 256 x 192 pair tiles give 1536 / 192 = 8 column tiles, 512 tiles at 16,384 rows = 6.9 rounds of
+// 74 pairs, where 256 x 256 tiles leave the sixth round 19 % full (dX measured 646 us against
+// cuBLAS's 559 that way). B is K-major (the caller passes the transposed weight for dX).
+template <> struct Cfg<EPI_F32> {
+  static constexpr int BN = 192, STAGES = 5;
+  static constexpr bool B_MN = false;
+};
+template <> struct Cfg<EPI_STORE16> {
+  static constexpr int BN = 192, STAGES = 5;
+  static constexpr bool B_MN = false;
+};
+template <> struct Cfg<EPI_STORE16_MN> {
+  static constexpr int BN = 256, STAGES = 4;
+  static constexpr bool B_MN = true;
+};
+template <> struct Cfg<EPI_SWIGLU> {  // a pair's tile: 128 gate columns (CTA 0's B) | the same 128 up (CTA 1's)
+  static constexpr int BN = 256, STAGES = 4;
+  static constexpr bool B_MN = false;
+};
+template <> struct Cfg<EPI_DSWIGLU> {
   static constexpr int BN = 256, STAGES = 4;
   static constexpr bool B_MN = true;
 };
@@ -80,9 +103,10 @@ struct Layout {
   // sin: 32 rows x 16 fp32, the 16-byte pieces of a row XOR-swizzled by (row / 2) % 4 so that both
   // the coalesced fills and each thread's row reads are conflict-free)
   static constexpr int OFF_STG = OFF_B + S * B_BYTES;
-  static constexpr int STG_WARP = EPI == EPI_QKV ? 4096 : 8192;
+  static constexpr int STG_WARP = EPI == EPI_QKV ? 4096 : (EPI == EPI_SWIGLU ? 12288 : 8192);
   static constexpr int OFF_TAB = OFF_STG + kEpiWarps * STG_WARP;
-  static constexpr int TAB_WARP = EPI == EPI_QKV ? 2 * 32 * 64 : 0;
+  // per warp: EPI_QKV the RoPE tables, EPI_DSWIGLU the gate / up values of 32 rows x 32 columns
+  static constexpr int TAB_WARP = (EPI == EPI_QKV || EPI == EPI_DSWIGLU) ? 2 * 32 * 64 : 0;
   static constexpr int OFF_BAR = OFF_TAB + kEpiWarps * TAB_WARP;
   static constexpr int N_BAR = 2 * S + 5;  // full[S], empty[S], acc_full[2], acc_empty[2], done
   static constexpr int OFF_TMEM = OFF_BAR + 8 * N_BAR;
@@ -99,6 +123,11 @@ struct Params {
   int64_t M;
   int N, K, n_tiles_n, n_tiles;
   int lora;               // EPI_QKV: the extra K block (u x [scaled lora_B | bias]) joins the K loop
+  int b_tile_step;        // PAIR, B K-major: rows of B per column tile; the CTA of rank r loads
+  int b_rank_off;         //   rows tile * b_tile_step + r * b_rank_off (MN-major B: its columns)
+  const void* gu;         // EPI_DSWIGLU: the forward's [gate | up] 16-bit [M, 2 inter]
+  int64_t ld_gu;
+  int inter;              // EPI_SWIGLU / EPI_DSWIGLU
   float scaling;
   const float* cosp;
   const float* sinp;
@@ -109,6 +138,22 @@ struct Params {
 template <typename T>
 __device__ __forceinline__ float rnd(float x) {
   return Dt<T>::to_f(Dt<T>::from_f(x));
+}
+
+// the separate SwiGLU kernels' sigmoid (swiglu.cu): 1 / (1 + exp(-x)), IEEE division
+__device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// one row (this lane's) of 32 fp32 values (bit patterns in v) rounded to T into a [32 rows x 32]
+// 16-bit staging tile with the 64-byte swizzle (16-byte piece p of row r at p ^ ((r / 2) % 4))
+template <typename T>
+__device__ __forceinline__ void store_row32(uint8_t* tile, int lane, const uint32_t (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[8 * j + e]);
+    *reinterpret_cast<uint4*>(tile + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = pack8<T>(f);
+  }
 }
 
 template <typename T, int EPI, bool PAIR>
@@ -169,9 +214,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
       uint32_t it = 0;
       bool ok = true;
       for (int tile = unit; tile < p.n_tiles && ok; tile += n_units) {
-        // this CTA's A rows and B rows of the tile
+        // this CTA's A rows and B rows (columns of an MN-major B) of the tile
         const int m0 = (tile / p.n_tiles_n) * TM + static_cast<int>(rank) * BM;
-        const int n0 = (tile % p.n_tiles_n) * BN + static_cast<int>(rank) * (BN / 2) * (PAIR ? 1 : 0);
+        const int n0 = PAIR ? (tile % p.n_tiles_n) * p.b_tile_step + static_cast<int>(rank) * p.b_rank_off
+                            : (tile % p.n_tiles_n) * BN;
         for (int kb = 0; kb < nkt; ++kb, ++it) {
           const int s = static_cast<int>(it % S);
           if (it >= static_cast<uint32_t>(S) && !(ok = mbar_wait(empty(s), ((it / S) - 1) & 1, p.err, 301))) break;
@@ -297,6 +343,128 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
             if (row0 < p.M && n0 + col < p.N)
               tma_store_2d(&p.to[0], stg_s + (n_chunks & 1) * 4096, n0 + col, static_cast<int>(row0));
             bulk_commit();  // one group per chunk, stored or not: the wait above counts groups
+          }
+        }
+      } else if constexpr (EPI == EPI_STORE16 || EPI == EPI_STORE16_MN) {
+        // warpgroup wg: columns [128 wg, 128 wg + 128) in chunks of 32 through a ring of four 2 KB
+        // staging tiles ([32 rows x 32 columns] 16-bit, 64-byte swizzle)
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32, ++n_chunks) {
+          const int col = wg * (BN / 2) + c;
+          uint32_t v[32];
+          tmem_ld32(tacc + col, v);
+          tmem_ld_wait();
+          if (lane == 0) bulk_wait_read<3>();  // the store that last used this slot has read it
+          __syncwarp();
+          const int slot = static_cast<int>(n_chunks & 3) * 2048;
+          store_row32<T>(stg + slot, lane, v);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < p.M && n0 + col < p.N)
+              tma_store_2d(&p.to[0], stg_s + slot, n0 + col, static_cast<int>(row0));
+            bulk_commit();  // one group per chunk, stored or not: the wait above counts groups
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
+        // accumulator columns [0, 128): gate of j0 .. j0 + 127, [128, 256): up of the same j;
+        // warpgroup wg takes j in [64 wg, 64 wg + 64) in chunks of 32: gate and up rounded to T (the
+        // values the separate SwiGLU kernel reads back), h = silu(gate) * up from them; gate, up
+        // and h leave through three 2 KB staging tiles (double-buffered: 2 x 6 KB per warp)
+        const int j0 = (tile % p.n_tiles_n) * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 4; c += 32, ++n_chunks) {
+          const int jl = wg * (BN / 4) + c;
+          uint32_t g[32], u[32];
+          tmem_ld32(tacc + jl, g);
+          tmem_ld32(tacc + BN / 2 + jl, u);
+          tmem_ld_wait();
+          if (lane == 0) bulk_wait_read1();
+          __syncwarp();
+          const int base = static_cast<int>(n_chunks & 1) * 6144;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float gf = rnd<T>(__uint_as_float(g[e])), uf = rnd<T>(__uint_as_float(u[e]));
+            g[e] = __float_as_uint(gf);
+            u[e] = __float_as_uint(uf);
+          }
+          store_row32<T>(stg + base, lane, g);
+          store_row32<T>(stg + base + 2048, lane, u);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float gf = __uint_as_float(g[e]), uf = __uint_as_float(u[e]);
+            g[e] = __float_as_uint(gf * sigmoid_ref(gf) * uf);
+          }
+          store_row32<T>(stg + base + 4096, lane, g);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < p.M) {
+              const int t = static_cast<int>(row0);
+              tma_store_2d(&p.to[0], stg_s + base, j0 + jl, t);                 // gate
+              tma_store_2d(&p.to[0], stg_s + base + 2048, p.inter + j0 + jl, t);  // up
+              tma_store_2d(&p.to[1], stg_s + base + 4096, j0 + jl, t);          // h
+            }
+            bulk_commit();
+          }
+        }
+      } else if constexpr (EPI == EPI_DSWIGLU) {
+        // accumulator = grad_hidden for j in [n0, n0 + 256); warpgroup wg takes [128 wg, 128 wg + 128)
+        // in chunks of 32; the forward's gate and up for the warp's rows come in by coalesced
+        // cp.async (32 rows x 32 columns each); dgate and dup leave through two 2 KB tiles
+        // (double-buffered)
+        uint8_t* tab = smem + L::OFF_TAB + ew * L::TAB_WARP;  // [gate | up][32 rows][64 B], swizzled
+        const T* gu = static_cast<const T*>(p.gu);
+        const auto load_gu = [&](int j) {
+#pragma unroll
+          for (int i2 = 0; i2 < 8; ++i2) {
+            const int piece = lane + 32 * i2;
+            const int which = piece >> 7, row = (piece >> 2) & 31, c4 = piece & 3;
+            const int64_t rr = row0 + row < p.M ? row0 + row : p.M - 1;
+            const T* src = gu + rr * p.ld_gu + (which ? p.inter : 0) + j + 8 * c4;
+            ptx::cp_async16(ptx::smem_u32(tab + which * 2048 + row * 64 + ((c4 ^ ((row >> 1) & 3)) << 4)), src, true);
+          }
+          ptx::cp_async_commit();
+        };
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32, ++n_chunks) {
+          const int jl = wg * (BN / 2) + c;
+          load_gu(n0 + jl);
+          uint32_t gr[32];
+          tmem_ld32(tacc + jl, gr);
+          tmem_ld_wait();
+          float gv[32], uv[32];
+          ptx::cp_async_wait<0>();
+          __syncwarp();
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4) {
+            const int off = lane * 64 + ((j4 ^ ((lane >> 1) & 3)) << 4);
+            unpack8<T>(*reinterpret_cast<const uint4*>(tab + off), *reinterpret_cast<float(*)[8]>(&gv[8 * j4]));
+            unpack8<T>(*reinterpret_cast<const uint4*>(tab + 2048 + off), *reinterpret_cast<float(*)[8]>(&uv[8 * j4]));
+          }
+          __syncwarp();  // the table is refilled by the next chunk
+          uint32_t dg[32], du[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float grf = rnd<T>(__uint_as_float(gr[e]));  // grad_hidden as the 16-bit GEMM output
+            const float sg = sigmoid_ref(gv[e]);
+            du[e] = __float_as_uint(grf * gv[e] * sg);
+            dg[e] = __float_as_uint(grf * uv[e] * sg * (1.0f + gv[e] * (1.0f - sg)));
+          }
+          if (lane == 0) bulk_wait_read1();
+          __syncwarp();
+          const int base = static_cast<int>(n_chunks & 1) * 4096;
+          store_row32<T>(stg + base, lane, dg);
+          store_row32<T>(stg + base + 2048, lane, du);
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            if (row0 < p.M) {
+              const int t = static_cast<int>(row0);
+              tma_store_2d(&p.to[0], stg_s + base, n0 + jl, t);                 // dgate
+              tma_store_2d(&p.to[0], stg_s + base + 2048, p.inter + n0 + jl, t);  // dup
+            }
+            bulk_commit();
           }
         }
       } else {
@@ -754,6 +922,8 @@ extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat
   p.M = n_tok;
   p.N = n_proj;
   p.K = hidden;
+  p.b_tile_step = BN;
+  p.b_rank_off = BN / 2;
   p.n_tiles_n = n_proj / BN + (n_proj % BN ? 1 : 0);
   const int64_t m_tiles = (n_tok + 2 * BM - 1) / (2 * BM);  // CTA pairs: 256 rows per tile
   p.n_tiles = static_cast<int>(m_tiles * p.n_tiles_n);
@@ -781,27 +951,30 @@ extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat
   return launch_gemm<T, EPI_QKV, true>(p, s, "qkv_proj_gemm");
 }
 
-extern "C" int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const void* w_cat, int64_t ldw, float* dx,
+extern "C" int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const void* w_t, int64_t ldw, float* dx,
                              int64_t ld_dx, int64_t n_tok, int hidden, int dtype, void* stream) {
   using namespace decik;
   using namespace decik::proj;
   if (n_tok == 0) return DECIK_OK;
-  if (n_tok < 0 || n_tok > (int64_t(1) << 31) - 1 || hidden <= 0 || hidden % 64 != 0 || k_cols <= 0)
-    return set_error(DECIK_ERR_INVALID, "proj_dx: T=%lld hidden %d K %d", (long long)n_tok, hidden, k_cols);
-  if (!dy || !w_cat || !dx) return set_error(DECIK_ERR_INVALID, "proj_dx: NULL pointer");
-  if (ld_dy < k_cols || ldw < hidden || ld_dx < hidden)
+  if (n_tok < 0 || n_tok > (int64_t(1) << 31) - 1 || hidden <= 0 || hidden % 8 != 0 || k_cols <= 0 || k_cols % 8 != 0)
+    return set_error(DECIK_ERR_INVALID, "proj_dx: T=%lld hidden %d K %d (multiples of 8)", (long long)n_tok, hidden,
+                     k_cols);
+  if (!dy || !w_t || !dx) return set_error(DECIK_ERR_INVALID, "proj_dx: NULL pointer");
+  if (ld_dy < k_cols || ldw < k_cols || ld_dx < hidden)
     return set_error(DECIK_ERR_INVALID, "proj_dx: row strides shorter than the rows");
-  if (ld_dy % 8 || ldw % 8 || ld_dx % 4 || !aligned16(dy) || !aligned16(w_cat) || !aligned16(dx))
+  if (ld_dy % 8 || ldw % 8 || ld_dx % 4 || !aligned16(dy) || !aligned16(w_t) || !aligned16(dx))
     return set_error(DECIK_ERR_INVALID, "proj_dx: rows and pointers need 16-byte alignment");
   if (dtype != DECIK_BF16 && dtype != DECIK_F16) return set_error(DECIK_ERR_INVALID, "proj_dx: dtype %d", dtype);
+  constexpr int BN = Cfg<EPI_F32>::BN;
   Params p{};
   if (int rc = attn::make_map_2d(&p.ta, dy, dtype, k_cols, n_tok, ld_dy * 2, 64, BM)) return rc;
-  if (int rc = attn::make_map_2d(&p.tb, w_cat, dtype, hidden, k_cols, ldw * 2, 64, 64)) return rc;
+  if (int rc = attn::make_map_2d(&p.tb, w_t, dtype, k_cols, hidden, ldw * 2, 64, BN / 2)) return rc;
   if (int rc = attn::make_map_2d(&p.to[0], dx, DECIK_F32, hidden, n_tok, ld_dx * 4, 32, 32)) return rc;
-  constexpr int BN = Cfg<EPI_F32>::BN;
   p.M = n_tok;
   p.N = hidden;
   p.K = k_cols;
+  p.b_tile_step = BN;
+  p.b_rank_off = BN / 2;
   p.n_tiles_n = (hidden + BN - 1) / BN;
   p.n_tiles = static_cast<int>(((n_tok + 2 * BM - 1) / (2 * BM)) * p.n_tiles_n);  // CTA pairs: 256 rows
   p.err = attn::attn_error_word();
@@ -842,4 +1015,170 @@ extern "C" int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, 
     return set_error(DECIK_ERR_INVALID, "lora_grads: dtype %d", dtype);
   }
   return check_launch("lora_grads");
+}
+
+namespace decik {
+namespace proj {
+namespace {
+
+template <int EPI>
+int launch_typed(const Params& p, int dtype, cudaStream_t s, const char* what) {
+  if (dtype == DECIK_BF16) return launch_gemm<__nv_bfloat16, EPI, true>(p, s, what);
+  if (dtype == DECIK_F16) return launch_gemm<__half, EPI, true>(p, s, what);
+  return set_error(DECIK_ERR_INVALID, "%s: dtype %d", what, dtype);
+}
+
+bool rows16(const void* ptr, int64_t ld) { return aligned16(ptr) && ld % 8 == 0; }
+
+}  // namespace
+}  // namespace proj
+}  // namespace decik
+
+extern "C" int decik_gemm16(const void* a, int64_t lda, const void* b, int64_t ldb, int b_mn, void* out, int64_t ldo,
+                            int64_t m, int n, int k, int dtype, void* stream) {
+  using namespace decik;
+  using namespace decik::proj;
+  if (m == 0 || n == 0) return DECIK_OK;
+  if (m < 0 || m > (int64_t(1) << 31) - 1 || n < 0 || k <= 0 || n % 8 != 0 || k % 8 != 0)
+    return set_error(DECIK_ERR_INVALID, "gemm16: M=%lld N=%d K=%d (N, K multiples of 8)", (long long)m, n, k);
+  if (!a || !b || !out) return set_error(DECIK_ERR_INVALID, "gemm16: NULL pointer");
+  if (!rows16(a, lda) || !rows16(b, ldb) || !rows16(out, ldo) || lda < k || ldb < (b_mn ? n : k) || ldo < n)
+    return set_error(DECIK_ERR_INVALID, "gemm16: rows and pointers need 16-byte alignment and full-width strides");
+  const int BN = b_mn ? Cfg<EPI_STORE16_MN>::BN : Cfg<EPI_STORE16>::BN;
+  Params p{};
+  if (int rc = attn::make_map_2d(&p.ta, a, dtype, k, m, lda * 2, 64, BM)) return rc;
+  if (b_mn) {
+    if (int rc = attn::make_map_2d(&p.tb, b, dtype, n, k, ldb * 2, 64, 64)) return rc;
+  } else {
+    if (int rc = attn::make_map_2d(&p.tb, b, dtype, k, n, ldb * 2, 64, BN / 2)) return rc;
+  }
+  if (int rc = attn::make_map_2d(&p.to[0], out, dtype, n, m, ldo * 2, 32, 32, 64)) return rc;
+  p.M = m;
+  p.N = n;
+  p.K = k;
+  p.b_tile_step = BN;
+  p.b_rank_off = BN / 2;
+  p.n_tiles_n = (n + BN - 1) / BN;
+  p.n_tiles = static_cast<int>(((m + 2 * BM - 1) / (2 * BM)) * p.n_tiles_n);
+  p.err = attn::attn_error_word();
+  cudaStream_t s = as_stream(stream);
+  return b_mn ? launch_typed<EPI_STORE16_MN>(p, dtype, s, "gemm16") : launch_typed<EPI_STORE16>(p, dtype, s, "gemm16");
+}
+
+extern "C" int decik_mlp_gate_up(const void* x16, int64_t ldx, const void* w_gu, int64_t ldw, void* gu, int64_t ldgu,
+                                 void* h, int64_t ldh, int64_t m, int hidden, int inter, int dtype, void* stream) {
+  using namespace decik;
+  using namespace decik::proj;
+  if (m == 0) return DECIK_OK;
+  if (m < 0 || m > (int64_t(1) << 31) - 1 || hidden <= 0 || hidden % 8 != 0 || inter <= 0 || inter % 128 != 0)
+    return set_error(DECIK_ERR_INVALID, "mlp_gate_up: M=%lld hidden %d inter %d (inter %% 128 == 0)", (long long)m,
+                     hidden, inter);
+  if (!x16 || !w_gu || !gu || !h) return set_error(DECIK_ERR_INVALID, "mlp_gate_up: NULL pointer");
+  if (!rows16(x16, ldx) || !rows16(w_gu, ldw) || !rows16(gu, ldgu) || !rows16(h, ldh) || ldx < hidden ||
+      ldw < hidden || ldgu < 2 * static_cast<int64_t>(inter) || ldh < inter)
+    return set_error(DECIK_ERR_INVALID, "mlp_gate_up: rows and pointers need 16-byte alignment and full-width strides");
+  Params p{};
+  if (int rc = attn::make_map_2d(&p.ta, x16, dtype, hidden, m, ldx * 2, 64, BM)) return rc;
+  if (int rc = attn::make_map_2d(&p.tb, w_gu, dtype, hidden, 2 * static_cast<int64_t>(inter), ldw * 2, 64, BM))
+    return rc;
+  if (int rc = attn::make_map_2d(&p.to[0], gu, dtype, 2 * static_cast<int64_t>(inter), m, ldgu * 2, 32, 32, 64))
+    return rc;
+  if (int rc = attn::make_map_2d(&p.to[1], h, dtype, inter, m, ldh * 2, 32, 32, 64)) return rc;
+  p.M = m;
+  p.N = 2 * inter;
+  p.K = hidden;
+  p.inter = inter;
+  p.b_tile_step = BM;    // gate rows j0 .. j0 + 127 in CTA 0, up rows inter + j0 .. in CTA 1
+  p.b_rank_off = inter;
+  p.n_tiles_n = inter / 128;
+  p.n_tiles = static_cast<int>(((m + 2 * BM - 1) / (2 * BM)) * p.n_tiles_n);
+  p.err = attn::attn_error_word();
+  return launch_typed<EPI_SWIGLU>(p, dtype, as_stream(stream), "mlp_gate_up");
+}
+
+extern "C" int decik_mlp_down_grad(const void* grad, int64_t ldg, const void* w_down, int64_t ldw, const void* gu,
+                                   int64_t ldgu, void* dgu, int64_t lddgu, int64_t m, int hidden, int inter, int dtype,
+                                   void* stream) {
+  using namespace decik;
+  using namespace decik::proj;
+  if (m == 0) return DECIK_OK;
+  if (m < 0 || m > (int64_t(1) << 31) - 1 || hidden <= 0 || hidden % 8 != 0 || inter <= 0 || inter % 256 != 0)
+    return set_error(DECIK_ERR_INVALID, "mlp_down_grad: M=%lld hidden %d inter %d (inter %% 256 == 0)", (long long)m,
+                     hidden, inter);
+  if (!grad || !w_down || !gu || !dgu) return set_error(DECIK_ERR_INVALID, "mlp_down_grad: NULL pointer");
+  if (!rows16(grad, ldg) || !rows16(w_down, ldw) || !rows16(gu, ldgu) || !rows16(dgu, lddgu) || ldg < hidden ||
+      ldw < inter || ldgu < 2 * static_cast<int64_t>(inter) || lddgu < 2 * static_cast<int64_t>(inter))
+    return set_error(DECIK_ERR_INVALID, "mlp_down_grad: rows and pointers need 16-byte alignment and full-width strides");
+  constexpr int BN = Cfg<EPI_DSWIGLU>::BN;
+  Params p{};
+  if (int rc = attn::make_map_2d(&p.ta, grad, dtype, hidden, m, ldg * 2, 64, BM)) return rc;
+  if (int rc = attn::make_map_2d(&p.tb, w_down, dtype, inter, hidden, ldw * 2, 64, 64)) return rc;
+  if (int rc = attn::make_map_2d(&p.to[0], dgu, dtype, 2 * static_cast<int64_t>(inter), m, lddgu * 2, 32, 32, 64))
+    return rc;
+  p.M = m;
+  p.N = inter;
+  p.K = hidden;
+  p.inter = inter;
+  p.gu = gu;
+  p.ld_gu = ldgu;
+  p.b_tile_step = BN;
+  p.b_rank_off = BN / 2;
+  p.n_tiles_n = inter / BN;
+  p.n_tiles = static_cast<int>(((m + 2 * BM - 1) / (2 * BM)) * p.n_tiles_n);
+  p.err = attn::attn_error_word();
+  return launch_typed<EPI_DSWIGLU>(p, dtype, as_stream(stream), "mlp_down_grad");
+}
+
+namespace decik {
+namespace proj {
+namespace {
+
+// dst [cols, rows] = src [rows, cols]^T for 16-bit values: 64 x 64 tiles through shared memory
+// (rows padded by one 32-bit word: conflict-free column reads), 16-byte global loads and stores.
+__global__ void __launch_bounds__(256) transpose16_kernel(const uint16_t* __restrict__ src, int64_t lds,
+                                                          uint16_t* __restrict__ dst, int64_t ldd, int64_t rows,
+                                                          int64_t cols) {
+  __shared__ uint16_t tile[64][64 + 2];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 64, c0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {  // 64 rows x 8 pieces of 8 values
+    const int piece = tid + 256 * i;
+    const int r = piece >> 3, c = 8 * (piece & 7);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r0 + r < rows && c0 + c < cols) v = *reinterpret_cast<const uint4*>(src + (r0 + r) * lds + c0 + c);
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tile[r][c + k] = e[k];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {  // output rows = source columns
+    const int piece = tid + 256 * i;
+    const int c = piece >> 3, r = 8 * (piece & 7);
+    if (c0 + c >= cols || r0 + r >= rows) continue;
+    uint4 v;
+    uint16_t* e = reinterpret_cast<uint16_t*>(&v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) e[k] = tile[r + k][c];
+    *reinterpret_cast<uint4*>(dst + (c0 + c) * ldd + r0 + r) = v;
+  }
+}
+
+}  // namespace
+}  // namespace proj
+}  // namespace decik
+
+extern "C" int decik_transpose16(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t rows, int64_t cols,
+                                 void* stream) {
+  using namespace decik;
+  if (rows == 0 || cols == 0) return DECIK_OK;
+  if (rows < 0 || cols < 0 || rows % 8 || cols % 8 || lds < cols || ldd < rows || lds % 8 || ldd % 8 ||
+      !aligned16(src) || !aligned16(dst))
+    return set_error(DECIK_ERR_INVALID, "transpose16: %lld x %lld (multiples of 8), strides, 16-byte alignment",
+                     (long long)rows, (long long)cols);
+  const dim3 grid(static_cast<unsigned>((cols + 63) / 64), static_cast<unsigned>((rows + 63) / 64));
+  proj::transpose16_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const uint16_t*>(src), lds,
+                                                                static_cast<uint16_t*>(dst), ldd, rows, cols);
+  return check_launch("transpose16");
 }

@@ -49,6 +49,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // box_rows x 64-element half tile with the 128-byte swizzle (the UMMA K-major / MN-major canonical layout).
 // The two outer dimensions are ordered by increasing stride: order 0 = (d, token, head),
 // order 1 = (d, head, token); the kernel passes its coordinates in that order.
+// cuTensorMapEncodeTiled on a host thread that has not yet made a CUDA runtime call (an autograd
+// worker, say) has no current context and returns CUDA_ERROR_INVALID_CONTEXT: bind the current
+// device's primary context and encode again.
+template <typename Encode>
+static CUresult encode_with_context(Encode&& encode) {
+  CUresult r = encode();
+  if (r == CUDA_ERROR_INVALID_CONTEXT) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) r = encode();
+  }
+  return r;
+}
+
 int make_tile_map_ex(CUtensorMap* map, const void* ptr, int64_t tok_stride, int64_t head_stride, int64_t n_tok,
                      int n_heads, int dtype, int* order, int box_rows, int box_inner, int swizzle_bytes);
 
@@ -85,33 +98,39 @@ int make_tile_map_ex(CUtensorMap* map, const void* ptr, int64_t tok_stride, int6
     box[0] = static_cast<cuuint32_t>(box_inner); box[1] = 1; box[2] = static_cast<cuuint32_t>(box_rows);
   }
   const CUtensorMapDataType dt = dtype == DECIK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_with_context([&] {
+    return fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  });
   if (r != CUDA_SUCCESS)
     return set_error(DECIK_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d): tok_stride %lld head_stride %lld",
                      static_cast<int>(r), (long long)tok_stride, (long long)head_stride);
   return DECIK_OK;
 }
 
-// A 2-D tiled map with the 128-byte swizzle over a row-major matrix of `outer` rows x `inner`
-// elements (row stride row_bytes), box box_outer rows x box_inner elements (box_inner x the element
-// size must be 128 bytes: one swizzle row). dtype: DECIK_F16 / DECIK_BF16 / DECIK_F32.
+// A 2-D tiled map with the 128- or 64-byte swizzle over a row-major matrix of `outer` rows x
+// `inner` elements (row stride row_bytes), box box_outer rows x box_inner elements (box_inner x the
+// element size must equal the swizzle: one swizzle row). dtype: DECIK_F16 / DECIK_BF16 / DECIK_F32.
 int make_map_2d(CUtensorMap* map, const void* ptr, int dtype, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                uint32_t box_inner, uint32_t box_outer) {
+                uint32_t box_inner, uint32_t box_outer, int swizzle_bytes) {
   auto fn = encode_fn();
   if (fn == nullptr) return set_error(DECIK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const CUtensorMapDataType dt = dtype == DECIK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : dtype == DECIK_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const uint32_t esize = dtype == DECIK_F32 ? 4 : 2;
-  if (box_inner * esize != 128)
-    return set_error(DECIK_ERR_INVALID, "make_map_2d: box inner %u x %u bytes is not one 128-byte row", box_inner, esize);
+  if ((swizzle_bytes != 128 && swizzle_bytes != 64) || box_inner * esize != static_cast<uint32_t>(swizzle_bytes))
+    return set_error(DECIK_ERR_INVALID, "make_map_2d: box inner %u x %u bytes is not one %d-byte swizzle row",
+                     box_inner, esize, swizzle_bytes);
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer}, estr[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_with_context([&] {
+    return fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  });
   if (r != CUDA_SUCCESS)
     return set_error(DECIK_ERR_INVALID, "cuTensorMapEncodeTiled (2-D) failed (%d): %llu x %llu, row %llu bytes",
                      static_cast<int>(r), (unsigned long long)outer, (unsigned long long)inner,
@@ -129,8 +148,10 @@ int make_f32_chunk_map(CUtensorMap* map, float* ptr, int64_t n_tok, int n_heads,
   cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(n_heads), static_cast<cuuint64_t>(n_tok)};
   cuuint64_t strides[2] = {128 * 4, static_cast<cuuint64_t>(n_heads) * 128 * 4};
   cuuint32_t box[3] = {16, 1, static_cast<cuuint32_t>(box_rows)}, estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_with_context([&] {
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  });
   if (r != CUDA_SUCCESS) return set_error(DECIK_ERR_INVALID, "cuTensorMapEncodeTiled (fp32 chunks) failed (%d)", static_cast<int>(r));
   return DECIK_OK;
 }

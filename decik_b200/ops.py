@@ -496,20 +496,81 @@ def qkv_proj_fwd(x: torch.Tensor, w_cat: torch.Tensor, ext_b: torch.Tensor, lora
     return x16, u, q, k, v
 
 
-def proj_dx(dy: torch.Tensor, w_cat: torch.Tensor, k_cols: int | None = None) -> torch.Tensor:
-    """dx = dy[:, :K] . w_cat[:K] in fp32 [T, H] on tcgen05 (decik_proj_dx)."""
-    _cuda(dy, w_cat)
+def transpose16(src: torch.Tensor) -> torch.Tensor:
+    """src [R, C] (16-bit, contiguous rows) -> a new [C, R] tensor (decik_transpose16)."""
+    _cuda(src)
+    R, C = src.shape
+    if src.stride(1) != 1:
+        src = src.contiguous()
+    dst = torch.empty((C, R), dtype=src.dtype, device=src.device)
+    with _timed("transpose16", 1):
+        rc = _lib.lib().decik_transpose16(_p(src), src.stride(0), _p(dst), dst.stride(0), R, C, _stream(src))
+    _lib.check(rc, "transpose16")
+    return dst
+
+
+def proj_dx(dy: torch.Tensor, w_t: torch.Tensor, k_cols: int | None = None) -> torch.Tensor:
+    """dx = dy[:, :K] . w_t[:, :K]^T in fp32 [T, H] on tcgen05 CTA pairs (decik_proj_dx); w_t [H, >= K]
+    is the transposed weight (transpose16 of a [K, H] weight)."""
+    _cuda(dy, w_t)
     T = dy.shape[0]
-    K = int(k_cols if k_cols is not None else w_cat.shape[0])
-    H = w_cat.shape[1]
-    if dy.stride(1) != 1 or w_cat.stride(1) != 1:
-        raise RuntimeError("decik_b200 proj_dx: dy and w_cat need contiguous rows")
+    H = w_t.shape[0]
+    K = int(k_cols if k_cols is not None else w_t.shape[1])
+    if dy.stride(1) != 1 or w_t.stride(1) != 1:
+        raise RuntimeError("decik_b200 proj_dx: dy and w_t need contiguous rows")
     dx = torch.empty((T, H), dtype=torch.float32, device=dy.device)
     with _timed("proj_dx", 1):
-        rc = _lib.lib().decik_proj_dx(_p(dy), dy.stride(0), K, _p(w_cat), w_cat.stride(0), _p(dx), dx.stride(0), T, H,
+        rc = _lib.lib().decik_proj_dx(_p(dy), dy.stride(0), K, _p(w_t), w_t.stride(0), _p(dx), dx.stride(0), T, H,
                                       _dt(dy), _stream(dy))
     _lib.check(rc, "proj_dx")
     return dx
+
+
+def gemm16(a: torch.Tensor, b: torch.Tensor, b_mn: bool, out: torch.Tensor | None = None) -> torch.Tensor:
+    """a [M, K] . b^T (b [N, K], ``b_mn`` False) or a . b (b [K, N], ``b_mn`` True) in a's 16-bit dtype
+    on tcgen05 CTA pairs (decik_gemm16)."""
+    _cuda(a, b, out)
+    M, K = a.shape
+    N = b.shape[1] if b_mn else b.shape[0]
+    if a.stride(1) != 1 or b.stride(1) != 1:
+        raise RuntimeError("decik_b200 gemm16: operands need contiguous rows")
+    if out is None:
+        out = torch.empty((M, N), dtype=a.dtype, device=a.device)
+    with _timed("gemm16", 1):
+        rc = _lib.lib().decik_gemm16(_p(a), a.stride(0), _p(b), b.stride(0), 1 if b_mn else 0, _p(out), out.stride(0),
+                                     M, N, K, _dt(a), _stream(a))
+    _lib.check(rc, "gemm16")
+    return out
+
+
+def mlp_gate_up(x16: torch.Tensor, w_gu: torch.Tensor):
+    """(gu [T, 2 inter], h [T, inter]) = (x16 . w_gu^T, SwiGLU of it) in one tcgen05 GEMM
+    (decik_mlp_gate_up)."""
+    _cuda(x16, w_gu)
+    T, H = x16.shape
+    inter = w_gu.shape[0] // 2
+    gu = torch.empty((T, 2 * inter), dtype=x16.dtype, device=x16.device)
+    h = torch.empty((T, inter), dtype=x16.dtype, device=x16.device)
+    with _timed("mlp_gate_up", 1):
+        rc = _lib.lib().decik_mlp_gate_up(_p(x16), x16.stride(0), _p(w_gu), w_gu.stride(0), _p(gu), gu.stride(0), _p(h),
+                                          h.stride(0), T, H, inter, _dt(x16), _stream(x16))
+    _lib.check(rc, "mlp_gate_up")
+    return gu, h
+
+
+def mlp_down_grad(grad16: torch.Tensor, w_down: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
+    """[dgate | dup] [T, 2 inter] of SwiGLU for grad_hidden = grad16 . w_down, computed in the
+    GEMM's epilogue (decik_mlp_down_grad)."""
+    _cuda(grad16, w_down, gu)
+    T, H = grad16.shape
+    inter = w_down.shape[1]
+    dgu = torch.empty((T, 2 * inter), dtype=grad16.dtype, device=grad16.device)
+    with _timed("mlp_down_grad", 1):
+        rc = _lib.lib().decik_mlp_down_grad(_p(grad16), grad16.stride(0), _p(w_down), w_down.stride(0), _p(gu),
+                                            gu.stride(0), _p(dgu), dgu.stride(0), T, H, inter, _dt(grad16),
+                                            _stream(grad16))
+    _lib.check(rc, "mlp_down_grad")
+    return dgu
 
 
 def lora_grads(dy: torch.Tensor, x16: torch.Tensor, u: torch.Tensor, scaling: float, n_heads: int, n_kv: int):

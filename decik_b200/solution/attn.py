@@ -94,7 +94,7 @@ class FusedAttentionBlock(torch.autograd.Function):
         # from their place in dy
         ops.attn_qkv_bwd(g, q.transpose(0, 1), k.transpose(0, 1), v, out, lse, cu, max_len, scale, cos, sin,
                          frag, scaling, dy)
-        dx = ops.proj_dx(dy, w_cat)
+        dx = ops.proj_dx(dy, ops.transpose16(w_cat))
         da, db = ops.lora_grads(dy, x16, u, scaling, n_heads, n_kv)
         return (dx, da[:r], db[:n_q], da[r:], db[n_q:]) + (None,) * 12
 

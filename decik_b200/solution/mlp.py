@@ -8,12 +8,19 @@ dtype and runs SwiGLU in fp32.
 
 Here, with 180 GB of HBM per GPU, the node:
 - dequantises W_gate, W_up (into one [2 * inter, hidden] matrix) and W_down in one launch;
-- computes gate | up as ONE GEMM;
-- runs SwiGLU on the sm_100a kernel (``decik_swiglu_fwd``), fp32 arithmetic rounded once;
+- computes gate | up as ONE tcgen05 GEMM whose epilogue also applies SwiGLU (decik_mlp_gate_up):
+  gate and up are rounded to the compute dtype and kept, and silu(gate) * up is computed from them
+  with the separate SwiGLU kernel's fp32 arithmetic, rounded once;
 - keeps the dequantised weights and gate | up for the backward: no recompute, no second dequant;
-- computes the input gradient as one GEMM over [dgate | dup] with fp32 output. That sums the two
-  projections' input gradients in fp32 inside the GEMM, where the reference casts each to fp32
-  and adds.
+- computes grad_hidden = grad . W_down with the SwiGLU backward in the GEMM's epilogue
+  (decik_mlp_down_grad: grad_hidden never reaches HBM), then the input gradient as one GEMM over
+  [dgate | dup] with fp32 output. That sums the two projections' input gradients in fp32 inside the
+  GEMM, where the reference casts each to fp32 and adds.
+
+The two plain GEMMs (down projection, input gradient) have nothing to fuse and run on cuBLAS: at
+N = hidden = 1536 cuBLAS's clustered tiles (TMA multicast, which this project's kernels do not use)
+are 10-20% faster than decik_gemm16 / decik_proj_dx on these shapes. The MLP sits outside the
+attention block.
 
 The output is in the projections' compute dtype, as the reference's node returns fp16.
 """
@@ -21,7 +28,6 @@ The output is in the projections' compute dtype, as the reference's node returns
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from .. import ops
 from ._state import on_gpu
@@ -30,17 +36,16 @@ from .nf4 import dequantize_nf4_many, supported
 
 class FusedMLP(torch.autograd.Function):
     """down(silu(gate(x)) * up(x)) with frozen dequantised weights: ``w_gu`` [2 * inter, hidden]
-    (W_gate rows then W_up rows) and ``w_down`` [hidden, inter] in the compute dtype; optional
-    frozen biases ``b_gu`` / ``b_down``. Gradient only for x (returned in x's dtype)."""
+    (W_gate rows then W_up rows) and ``w_down`` [hidden, inter] in the compute dtype (the Qwen2 MLP
+    has no biases). Gradient only for x (returned in x's dtype)."""
 
     @staticmethod
-    def forward(ctx, x, w_gu, w_down, b_gu, b_down):
+    def forward(ctx, x, w_gu, w_down):
         inter = w_down.shape[1]
         shape = x.shape
-        x16 = x.reshape(-1, shape[-1]).to(w_gu.dtype)
-        gu = F.linear(x16, w_gu, b_gu)                     # [T, 2 * inter]
-        hidden = ops.swiglu_fwd(gu, inter)                 # [T, inter]
-        out = F.linear(hidden, w_down, b_down)             # [T, hidden]
+        x16 = x.reshape(-1, shape[-1]).to(w_gu.dtype).contiguous()
+        gu, hidden = ops.mlp_gate_up(x16, w_gu)            # [T, 2 * inter], [T, inter]
+        out = torch.mm(hidden, w_down.t())                 # [T, hidden], plain GEMM
         ctx.save_for_backward(gu, w_gu, w_down)
         ctx.in_dtype, ctx.shape, ctx.inter = x.dtype, shape, inter
         return out.view(*shape[:-1], out.shape[-1])
@@ -48,15 +53,14 @@ class FusedMLP(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         gu, w_gu, w_down = ctx.saved_tensors
-        g16 = grad_out.reshape(-1, grad_out.shape[-1]).to(w_down.dtype)
-        grad_hidden = torch.mm(g16, w_down)                # [T, inter]
-        dgu = ops.swiglu_bwd(grad_hidden, gu, ctx.inter)   # [T, 2 * inter] = [dgate | dup]
+        g16 = grad_out.reshape(-1, grad_out.shape[-1]).to(w_down.dtype).contiguous()
+        dgu = ops.mlp_down_grad(g16, w_down, gu)           # [T, 2 * inter] = [dgate | dup]
         dx = torch.mm(dgu, w_gu, out_dtype=torch.float32)  # both input gradients summed in fp32
-        return dx.to(ctx.in_dtype).view(ctx.shape), None, None, None, None
+        return dx.to(ctx.in_dtype).view(ctx.shape), None, None
 
 
 def mlp_weights(gate_proj, up_proj, down_proj, dtype):
-    """(w_gu, w_down, b_gu, b_down): this step's dequantised weights, one dequant launch."""
+    """(w_gu, w_down): this step's dequantised weights, one dequant launch."""
     gq, uq, dq = (p.weight.quant_state for p in (gate_proj, up_proj, down_proj))
     inter, hidden = gq.shape
     dev = gate_proj.weight.device
@@ -64,18 +68,14 @@ def mlp_weights(gate_proj, up_proj, down_proj, dtype):
     w_down = torch.empty(tuple(dq.shape), dtype=dtype, device=dev)
     dequantize_nf4_many([(gate_proj.weight.data, gq, w_gu[:inter]), (up_proj.weight.data, uq, w_gu[inter:]),
                          (down_proj.weight.data, dq, w_down)], dtype)
-    b_gu = None
-    if gate_proj.bias is not None or up_proj.bias is not None:
-        zeros = torch.zeros(inter, device=dev)
-        b_gu = torch.cat([zeros if p.bias is None else p.bias.float() for p in (gate_proj, up_proj)]).to(dtype)
-    b_down = None if down_proj.bias is None else down_proj.bias.to(dtype)
-    return w_gu, w_down, b_gu, b_down
+    return w_gu, w_down
 
 
 def patch(linear4bit_cls=None):
     """Patch Qwen2MLP.forward (solution/mlp.py:113-163). Eligible: an input on the GPU, the silu
-    activation, and three NF4 Linear4bit projections with one 16-bit compute dtype, frozen
-    weights and biases. Anything else runs the original forward."""
+    activation, and three bias-free NF4 Linear4bit projections with one 16-bit compute dtype and
+    frozen weights, inter a multiple of 256 (the GEMM tiles). Anything else runs the original
+    forward."""
     from transformers.models.qwen2 import modeling_qwen2
 
     if linear4bit_cls is None:
@@ -91,7 +91,7 @@ def patch(linear4bit_cls=None):
         bias = getattr(module, "bias", None)
         return (isinstance(module, linear4bit_cls) and getattr(module, "compute_dtype", None) == dtype
                 and weight is not None and on_gpu(weight) and weight.dtype == torch.uint8
-                and not weight.requires_grad and (bias is None or not bias.requires_grad)
+                and not weight.requires_grad and bias is None
                 and supported(getattr(weight, "quant_state", None), n_in))
 
     def forward(self, x):
@@ -104,10 +104,10 @@ def patch(linear4bit_cls=None):
                 and nf4_projection(gate, x.shape[-1], dtype) and nf4_projection(up, x.shape[-1], dtype)
                 and gate.weight.quant_state.shape == up.weight.quant_state.shape
                 and nf4_projection(down, gate.weight.quant_state.shape[0], dtype)
-                and gate.weight.quant_state.shape[0] % 8 == 0):
+                and gate.weight.quant_state.shape[0] % 256 == 0 and x.shape[-1] % 8 == 0):
             return original(self, x)
-        w_gu, w_down, b_gu, b_down = mlp_weights(gate, up, down, dtype)
-        return FusedMLP.apply(x, w_gu, w_down, b_gu, b_down)
+        w_gu, w_down = mlp_weights(gate, up, down, dtype)
+        return FusedMLP.apply(x, w_gu, w_down)
 
     forward._skc = True
     cls.forward = forward

@@ -376,11 +376,17 @@ DECIK_API int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat,
                                  int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim, int dtype,
                                  void* stream);
 
-/* dx = dy[:, 0:k_cols] . w_cat[0:k_cols, :] in fp32 [T, hidden] (ld_dx): the three NF4Linear input
- * gradients (solution/nf4.py:99-104: g16 @ W16) and both LoRA input gradients
- * (solution/attn.py:264-273), summed in one tcgen05 GEMM (w_cat read MN-major). dy dt [T, >= k_cols]. */
-DECIK_API int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const void* w_cat, int64_t ldw, float* dx,
+/* dx = dy[:, 0:k_cols] . w_t[:, 0:k_cols]^T in fp32 [T, hidden] (ld_dx), w_t dt [hidden, >= k_cols]
+ * (ldw) the TRANSPOSED weight (decik_transpose16 of W_cat [k_cols, hidden]): the three NF4Linear
+ * input gradients (solution/nf4.py:99-104: g16 @ W16) and both LoRA input gradients
+ * (solution/attn.py:264-273) summed in one tcgen05 GEMM on CTA pairs; also the MLP's input gradient
+ * ([dgate | dup] . [W_gate; W_up]). dy dt [T, >= k_cols]. hidden, k_cols multiples of 8. */
+DECIK_API int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const void* w_t, int64_t ldw, float* dx,
                             int64_t ld_dx, int64_t n_tok, int hidden, int dtype, void* stream);
+
+/* dst [cols, rows] = src [rows, cols]^T for 16-bit values (rows, cols multiples of 8). */
+DECIK_API int decik_transpose16(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t rows, int64_t cols,
+                                void* stream);
 
 /* The LoRA parameter gradients of the fused block (solution/attn.py:255-262):
  *   da [32, hidden] fp32 = du^T x16 (du = dy[:, n_proj : n_proj + 32]; rows 0-15 dA_q, 16-31 dA_v)
@@ -391,6 +397,30 @@ DECIK_API int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const voi
 DECIK_API int decik_lora_grads(const void* dy, int64_t ld_dy, const void* x16, int64_t ldx, const void* u,
                                int64_t ldu, float* da, float* db, float scaling, int64_t n_tok, int hidden,
                                int n_heads, int n_kv, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * The MLP's GEMMs on tcgen05 CTA pairs (the same kernel as the projections), with SwiGLU fused.
+ * They replace the four F.linear / torch.mm calls of the MLP node and its separate SwiGLU kernels:
+ * the reference's RecomputedMLP (solution/mlp.py:62-110: gate and up projections, SwiGLU, down
+ * projection, and their input gradients) and skc_swiglu (solution/swiglu.py:15-37).
+ *
+ * decik_gemm16: out[M, N] (dt, ldo) = a[M, K] . b^T with b dt [N, K] (b_mn = 0), or a . b with
+ * b [K, N] (b_mn = 1); fp32 accumulation, one rounding. N, K multiples of 8. */
+DECIK_API int decik_gemm16(const void* a, int64_t lda, const void* b, int64_t ldb, int b_mn, void* out, int64_t ldo,
+                           int64_t m, int n, int k, int dtype, void* stream);
+
+/* gu [M, 2 inter] = x16 . w_gu^T (w_gu dt [2 inter, hidden]: W_gate rows then W_up rows), each
+ * value rounded to dt, and h [M, inter] = dt(gate * sigmoid(gate) * up) from those rounded values
+ * (the separate SwiGLU kernel's arithmetic, decik_swiglu_fwd). inter % 128 == 0. */
+DECIK_API int decik_mlp_gate_up(const void* x16, int64_t ldx, const void* w_gu, int64_t ldw, void* gu, int64_t ldgu,
+                                void* h, int64_t ldh, int64_t m, int hidden, int inter, int dtype, void* stream);
+
+/* dgu [M, 2 inter] = [dgate | dup] of SwiGLU for grad_hidden = dt(grad . w_down) (grad dt [M, hidden],
+ * w_down dt [hidden, inter]) and the forward's gu: dup = g' g s, dgate = g' u s (1 + g (1 - s)),
+ * s = sigmoid(g) (decik_swiglu_bwd's arithmetic); grad_hidden never reaches HBM. inter % 256 == 0. */
+DECIK_API int decik_mlp_down_grad(const void* grad, int64_t ldg, const void* w_down, int64_t ldw, const void* gu,
+                                  int64_t ldgu, void* dgu, int64_t lddgu, int64_t m, int hidden, int inter, int dtype,
+                                  void* stream);
 
 #ifdef __cplusplus
 }

@@ -89,7 +89,7 @@ def test_fused_mlp_matches_reference_fixture(cuda_lib):
     T, H, I = (int(v) for v in g["dims"])
     w_gu, w_down = _nf4_weights(g, torch.float16)
     x = torch.from_numpy(g["x"].reshape(T, H)).to(DEV).requires_grad_(True)
-    out = FusedMLP.apply(x, w_gu, w_down, None, None)
+    out = FusedMLP.apply(x, w_gu, w_down)
     assert out.dtype == torch.float16
     out.backward(torch.from_numpy(g["gout"].reshape(T, H)).to(DEV))
     for got, ref in ((out.detach().float().cpu().numpy(), g["out"].reshape(T, H).astype(np.float32)),
@@ -116,7 +116,7 @@ def test_fused_mlp_bf16_vs_unfused_chain(cuda_lib):
     x = torch.randn(T, H, device=DEV).requires_grad_(True)
     x2 = x.detach().clone().requires_grad_(True)
     gout = torch.randn(T, H, device=DEV).to(torch.bfloat16)
-    out = FusedMLP.apply(x, torch.cat([w["gate"], w["up"]]), w["down"], None, None)
+    out = FusedMLP.apply(x, torch.cat([w["gate"], w["up"]]), w["down"])
     out.backward(gout)
     x16 = x2.to(torch.bfloat16)
     gate = F.linear(x16, w["gate"]).float()

@@ -98,7 +98,9 @@ def test_proj_dx_and_lora_grads_match_torch(cuda_lib, T, hidden, hq, hk, dtype):
     w_cat = (torch.randn(n_proj + 2 * r, hidden, device=DEV, generator=g) * 0.02).to(dtype)
     x16 = torch.randn(T, hidden, device=DEV, generator=g).to(dtype)
     u = torch.randn(T, 2 * r, device=DEV, generator=g).to(dtype)
-    dx = ops.proj_dx(dy, w_cat)
+    w_t = ops.transpose16(w_cat)
+    assert torch.equal(w_t, w_cat.t())
+    dx = ops.proj_dx(dy, w_t)
     ref = torch.mm(dy.float(), w_cat.float())
     _close(dx, ref, "dx", rel=1e-5, mx=1e-4)
     u64 = torch.cat((u, torch.zeros_like(u)), 1)  # the forward's u rows are 64 wide
