@@ -268,8 +268,9 @@ REF_BUDGET_S = 90.0  # the reference arm's timed steps, seconds
 # DRAM bytes (read + write) of the two attention kernels in one config-3 step (N = 1 packing), from
 # one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum; forward 68.1 + 15.6 MB, backward
 # 412.0 + 186.0 MB). Not measured by this run: the second field says which kernel build it describes.
-ATTN_DRAM_BYTES = {"config3": (681.6e6, "ncu capture of both attention kernels, one step, kernels as of "
-                                        "commit a73d9e0 (the forward has changed since); not this run's")}
+ATTN_DRAM_BYTES = {"config3": (699.2e6, "ncu capture (dram__bytes_read + write) of attn_fwd_sm100_kernel "
+                                        "(83.4 MB) and attn_bwd_sm100_kernel (615.8 MB), one launch each, "
+                                        "kernels as of commit 4716b58; not this run's")}
 
 
 def run_reference(args, world, rank):

@@ -5,28 +5,32 @@
 // matmuls, solution/attn.py:217-273).
 //
 // Forward, two kernels:
-// 1. x_cast_lora_down_kernel: x fp32 [T, H] -> x16 = dt(x) [T, H] and u = dt(x16 [A_q; A_v]^T)
-//    [T, 32] (the reference's lora_A products, solution/attn.py:225-227) in one pass over x: the
-//    cast has to read x anyway, and the rank-32 product rides along on mma.sync.
-// 2. proj_gemm_kernel<EPI_QKV>: y = x16 [W_q; W_k; W_v]^T on tcgen05, tile 128 tokens x 256
-//    outputs (two heads), K-major A and B from TMA, fp32 accumulators in TMEM (two buffers, so a
-//    tile's epilogue overlaps the next tile's MMAs). The epilogue is the projection epilogue
-//    of qkv.cu applied straight to the accumulators: + bias rounded to dt (F.linear with bias),
-//    LoRA-up dt(dt(u B16^T) * scaling) on q and v, v = dt(base + lora), RoPE with separate
-//    roundings and no FMA (solution/attn.py:39-60) on q and k, and the head-major q / k and
-//    token-major v tiles leave through shared memory by TMA stores. y never reaches HBM.
+// 1. x_cast_lora_down_kernel: x fp32 [T, H] -> x16 = dt(x) [T, H] and u = [dt(x16 [A_q; A_v]^T) | 1 | 0]
+//    [T, 64] (the reference's lora_A products, solution/attn.py:225-227, and a column of ones) in
+//    one pass over x: the cast has to read x anyway, and the rank-32 product rides along on mma.sync.
+// 2. proj_gemm_kernel<EPI_QKV>: y = x16 [W_q; W_k; W_v]^T + u b_ext^T on tcgen05 CTA pairs, tile
+//    256 tokens x 256 outputs (two heads), K-major A and B from TMA, fp32 accumulators in TMEM (two
+//    buffers, so a tile's epilogue overlaps the next tile's MMAs). The last K block multiplies u by
+//    b_ext = [scaling B_q | scaling B_v | bias | 0]: the LoRA-up of q and v and the bias land in the
+//    accumulator. The epilogue is RoPE with separate roundings and no FMA (solution/attn.py:39-60)
+//    on q and k, and the head-major q / k and token-major v tiles leave through shared memory by
+//    TMA stores. y never reaches HBM.
 // Backward:
-// 3. proj_gemm_kernel<EPI_F32>: dx = dy W_cat (dy [T, 2080] K-major, W_cat [2080, H] read
-//    MN-major), fp32 out by TMA stores: the three NF4Linear input gradients and both LoRA input
-//    gradients summed in one product (K = 2080, the tail zero-filled by TMA).
+// 3. proj_gemm_kernel<EPI_F32>: dx = dy W_cat on CTA pairs, tile 256 x 192 (dy [T, 2080] and the
+//    transposed weight W_cat^T [H, 2080], both K-major), fp32 out by TMA stores: the three
+//    NF4Linear input gradients and both LoRA input gradients summed in one product (K = 2080, the
+//    tail zero-filled by TMA).
 // 4. lora_grad_kernel: dA = du^T x16 [32, H] and dB = scaling g^T u [(Hq + Hk) 128, 16] as
 //    token-chunked mma.sync products reduced into fp32 outputs (red.global.add).
+// The MLP node uses the same kernel for gate | up with SwiGLU in the epilogue (EPI_SWIGLU) and for
+// grad_hidden = grad W_down with the SwiGLU backward in the epilogue (EPI_DSWIGLU).
 //
 // GEMM kernel roles (12 warps, one CTA per SM, persistent over tiles in n-fastest order so the
 // CTAs running together share their A row tiles in L2): warp 0 TMA producer (one thread), warp 1
-// TMEM allocation and the single-thread tcgen05.mma issue, warps 2-3 idle, warps 4-11 the
-// epilogue (warp w reads TMEM lanes 32 (w % 4) .. + 31; warps 4-7 take the first half of the
-// tile's columns, 8-11 the second). Every mbarrier wait is bounded (sm100::mbar_wait): one that
+// TMEM allocation and the single-thread tcgen05.mma issue (the pair's leader CTA issues for both),
+// warps 2-3 idle, warps 4-11 the epilogue (warp w reads TMEM lanes 32 (w % 4) .. + 31; warps 4-7
+// and 8-11 split the tile's columns). No TMA load uses cluster multicast: each CTA of a pair loads
+// its own A rows and its own half of B. Every mbarrier wait is bounded (sm100::mbar_wait): one that
 // gives up records a code in the error word and the CTA winds down.
 #include <cudaTypedefs.h>
 
