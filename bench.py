@@ -42,9 +42,9 @@ sys.path.insert(0, ROOT)
 METRIC = "QLoRA step tokens/s at 1/2/4/8 B200; varlen attn fwd+bwd TFLOP/s vs BF16 peak"
 HIDDEN, HQ, HK, D = 1536, 12, 2, 128
 TOKENS = 16384
-WORKLOAD = ("attention block fwd+bwd of one Qwen2.5-1.5B QLoRA layer (NF4 dq q/k/v + bias, "
+WORKLOAD = ("attention block fwd+bwd of one Qwen2.5-1.5B QLoRA layer (input RMSNorm, NF4 dq q/k/v + bias, "
             "LoRA r16 q,v, RoPE, varlen causal GQA attention) over config-3 packing")
-WORKLOAD7B = ("attention block fwd+bwd of one Qwen2.5-7B QLoRA layer (NF4 dq q/k/v + bias, "
+WORKLOAD7B = ("attention block fwd+bwd of one Qwen2.5-7B QLoRA layer (input RMSNorm, NF4 dq q/k/v + bias, "
               "LoRA r16 q,v, RoPE, varlen causal GQA attention) over config-4 packing")
 
 
@@ -237,7 +237,8 @@ def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0
     T = s
     rng = np.random.default_rng(seed)
     g = torch.Generator().manual_seed(seed)
-    inputs = dict(x=torch.randn(T, hidden, generator=g), spans=spans, n_heads=n_heads, n_kv=n_kv, scaling=2.0)
+    inputs = dict(x=torch.randn(T, hidden, generator=g), spans=spans, n_heads=n_heads, n_kv=n_kv, scaling=2.0,
+                  norm_w=1.0 + 0.1 * torch.randn(hidden, generator=g), eps=1e-6)
     for name, n_out in (("q", n_heads * D), ("k", n_kv * D), ("v", n_kv * D)):
         inputs[f"nf4_{name}"] = quantize_nf4((rng.standard_normal((n_out, hidden)) * 0.02).astype(np.float32))
         inputs[f"b_{name}"] = torch.randn(n_out, generator=g) * 0.02
@@ -336,7 +337,10 @@ def measure_block(args, world, rank, local, n_steps, workload=None, e2e=True, cp
     packing = packing_from_lengths(lengths, dev)
     cos, sin = rope_cos_sin(packing.positions, D)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
+    # x is the decoder layer's input h: the block starts with the layer's input RMSNorm (weight
+    # ~ 1 + 0.1 N(0, 1), frozen), which the fused node runs inside its first kernel
     x = torch.randn(T, hidden, device=dev, generator=g).requires_grad_(True)
+    norm_w = 1.0 + 0.1 * torch.randn(hidden, device=dev, generator=g)
     dout = torch.randn(T, hq * D, device=dev, generator=g).to(torch.bfloat16)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
     bucket = GradBucket(block.lora_params())                         # LoRA grads: views of one fp32 buffer
@@ -346,7 +350,7 @@ def measure_block(args, world, rank, local, n_steps, workload=None, e2e=True, cp
     def step(xin, din):
         bucket.zero_()
         xin.grad = None
-        out = block.forward(xin, packing, cos, sin)
+        out = block.forward(xin, packing, cos, sin, norm=(norm_w, 1e-6))
         out.backward(din)
         bucket.all_reduce()   # data-parallel exchange: one flat NCCL all-reduce (no-op at N=1)
         return out

@@ -39,6 +39,9 @@ SIGNATURES = {
     "decik_qkv_proj_fwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p,
                                    Tensor3, Tensor3, Tensor3, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int,
                                    c_int, c_int, c_int, c_void_p]),
+    "decik_qkv_proj_norm_fwd": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_float, c_void_p, c_void_p, c_int64,
+                                        c_void_p, c_int, c_void_p, c_void_p, Tensor3, Tensor3, Tensor3, c_void_p,
+                                        c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "decik_proj_dx": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
                               c_void_p]),
     "decik_lora_grads": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p,

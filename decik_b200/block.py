@@ -123,18 +123,25 @@ class QLoRAAttentionBlock:
         return w
 
     def forward(self, x: torch.Tensor, packing: Packing, cos: torch.Tensor, sin: torch.Tensor,
-                fused: bool = True):
+                fused: bool = True, norm: tuple | None = None):
         """x fp32 [T, hidden] (the normed hidden states) -> attention output [T, n_heads*D] (dtype).
         ``fused``: one projection GEMM + the sm_100a epilogues (FusedAttentionBlock); otherwise the
-        reference's chain of autograd Functions (NF4Linear x3, LoRA, FusedQKRope, VarlenSDPA)."""
+        reference's chain of autograd Functions (NF4Linear x3, LoRA, FusedQKRope, VarlenSDPA).
+        With ``norm`` = (weight, eps) x is the decoder layer's input and the block starts with its
+        input RMSNorm: inside the fused node's first kernel, or as RMSNormFn before the chain."""
         dt = self.dtype
         T = x.shape[0]
         if fused:
             a_q, b_q, a_v, b_v = self.lora_params()
+            norm_w, eps = norm if norm is not None else (None, 0.0)
             out = FusedAttentionBlock.apply(x, a_q, b_q, a_v, b_v, self.dequant_cat(), self.bias_cat, cos, sin,
                                             packing.cu_seqlens(x.device), packing.max_len, self.n_heads,
-                                            self.n_kv, self.scaling, self.head_dim ** -0.5)
+                                            self.n_kv, self.scaling, self.head_dim ** -0.5, None, None, norm_w,
+                                            eps)
             return out.view(T, self.n_heads * self.head_dim)
+        if norm is not None:
+            from .solution.rmsnorm import RMSNormFn
+            x = RMSNormFn.apply(x, norm[0], norm[1])
         x16 = x.to(dt)
         (pq, sq), (pk, sk), (pv, sv) = self.weights["q"], self.weights["k"], self.weights["v"]
         q_base = NF4Linear.apply(x16, pq, self.bias["q"].to(dt), sq)

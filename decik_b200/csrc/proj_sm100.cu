@@ -38,6 +38,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "norm_math.cuh"
 #include "ptx.cuh"
 #include "sm100.cuh"
 
@@ -584,7 +585,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
 }
 
 // ------------------------------------------------------------------------------------------------
-// x fp32 -> x16, u = dt(x16 [A_q; A_v]^T)
+// x fp32 -> x16, u = dt(x16 [A_q; A_v]^T); with NORM, x = RMSNorm(h) first
 // ------------------------------------------------------------------------------------------------
 constexpr int kCastTok = 64, kCastThreads = 256, kCastK = 128, kCastLd = kCastK + 8;  // padded rows (16-bit)
 
@@ -592,11 +593,18 @@ constexpr int kCastTok = 64, kCastThreads = 256, kCastK = 128, kCastLd = kCastK 
 // chunk (warp w: rows w, w + 8, ..., 512 contiguous bytes per row) with the next chunk's loads in
 // flight during the current chunk's work; the 16-bit chunk goes to x16 and to shared memory, where
 // mma.sync multiplies it by the matching 32 x 128 slice of [A_q; A_v].
-template <typename T>
+// NORM: x holds the decoder layer's input h, and the pass first computes each row's rstd (a warp
+// owns 8 whole rows; each lane sums its 16-byte pieces in column order, then the warp_sum tree:
+// the plain norm kernel's reduction) and writes it to rstd_out; the chunk loop then casts
+// x = w * (h * rstd) (the norm kernel's output, bit for bit) instead of h. The second read of the
+// CTA's rows (393 KB) comes from L2.
+template <typename T, typename W, bool NORM>
 __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const float* __restrict__ x, int64_t ldx,
                                                                         const T* __restrict__ a16, int64_t lda,
                                                                         T* __restrict__ x16, int64_t ldx16,
-                                                                        T* __restrict__ u, int64_t n_tok, int hidden) {
+                                                                        T* __restrict__ u, int64_t n_tok, int hidden,
+                                                                        const W* __restrict__ norm_w, float eps,
+                                                                        float* __restrict__ rstd_out) {
   // u rows are 64 wide (the GEMM's LoRA K block): columns 32..63 are zero
   constexpr int kULd = 4 * kR;
   __shared__ __align__(16) T xs[kCastTok * kCastLd];
@@ -613,6 +621,24 @@ __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const fl
       dst[i] = t < n_tok ? __ldg(reinterpret_cast<const float4*>(x + t * ldx + k0 + cc)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   };
+  float rs[8];
+  if constexpr (NORM) {
+    float ss[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss[i] = 0.f;
+#pragma unroll 2
+    for (int k0 = 0; k0 < hidden; k0 += kCastK) {
+      load(k0, cur);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss[i] += norm::sumsq4(cur[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      rs[i] = norm::row_rstd(ss[i], hidden, eps);
+      const int64_t t = t0 + warp + 8 * i;
+      if (rstd_out != nullptr && lane == 0 && t < n_tok) rstd_out[t] = rs[i];
+    }
+  }
   float acc[2][4];
 #pragma unroll
   for (int n = 0; n < 2; ++n)
@@ -629,6 +655,11 @@ __global__ void __launch_bounds__(kCastThreads) x_cast_lora_down_kernel(const fl
         ptx::cp_async16(ptx::smem_u32(as + ar * kCastLd + ac), a16 + ar * lda + k0 + ac, true);
       }
       ptx::cp_async_commit();
+    }
+    if constexpr (NORM) {
+      const float4 wv = norm::wload4<W>(norm_w, k0 + cc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cur[i] = norm::norm_out4w(cur[i], wv, rs[i]);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -885,13 +916,33 @@ extern "C" int decik_lora_b_ext(const float* b_q, const float* b_v, float scalin
   return check_launch("lora_b_ext");
 }
 
-extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* ext_b,
-                                  int lora, const float* cosp, const float* sinp, decik_tensor3_mut q,
-                                  decik_tensor3_mut k, decik_tensor3_mut v, void* x16, int64_t ldx16, void* u,
-                                  int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim, int dtype,
-                                  void* stream) {
-  using namespace decik;
-  using namespace decik::proj;
+namespace decik {
+namespace proj {
+namespace {
+
+// the first kernel of the forward projection: the cast + LoRA-down pass, with the input norm when
+// norm_w is given
+template <typename T>
+int launch_cast(const float* x, int64_t ldx, const T* a16, int64_t lda, T* x16, int64_t ldx16, T* u, int64_t n_tok,
+                int hidden, const void* norm_w, int norm_dtype, float eps, float* rstd, cudaStream_t s) {
+  const int grid = static_cast<int>((n_tok + kCastTok - 1) / kCastTok);
+  if (norm_w == nullptr)
+    x_cast_lora_down_kernel<T, float, false><<<grid, kCastThreads, 0, s>>>(x, ldx, a16, lda, x16, ldx16, u, n_tok,
+                                                                           hidden, nullptr, 0.f, nullptr);
+  else if (norm_dtype == DECIK_F32)
+    x_cast_lora_down_kernel<T, float, true><<<grid, kCastThreads, 0, s>>>(
+        x, ldx, a16, lda, x16, ldx16, u, n_tok, hidden, static_cast<const float*>(norm_w), eps, rstd);
+  else
+    x_cast_lora_down_kernel<T, __half, true><<<grid, kCastThreads, 0, s>>>(
+        x, ldx, a16, lda, x16, ldx16, u, n_tok, hidden, static_cast<const __half*>(norm_w), eps, rstd);
+  return check_launch(norm_w == nullptr ? "x_cast_lora_down" : "rmsnorm_cast_lora_down");
+}
+
+int qkv_proj_fwd_impl(const float* x, int64_t ldx, const void* norm_w, int norm_dtype, float eps, float* rstd,
+                      const void* w_cat, int64_t ldw, const void* ext_b, int lora, const float* cosp,
+                      const float* sinp, decik_tensor3_mut q, decik_tensor3_mut k, decik_tensor3_mut v, void* x16,
+                      int64_t ldx16, void* u, int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim,
+                      int dtype, void* stream) {
   if (n_tok == 0) return DECIK_OK;
   if (n_tok < 0 || n_tok > (int64_t(1) << 31) - 1 || head_dim != kD || n_heads <= 0 || n_kv <= 0 ||
       hidden <= 0 || hidden % 128 != 0 || (n_heads + 2 * n_kv) % 2 != 0)
@@ -905,6 +956,10 @@ extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat
       !aligned16(ext_b) || !aligned16(cosp) || !aligned16(sinp))
     return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: rows and pointers need 16-byte alignment");
   if (dtype != DECIK_BF16 && dtype != DECIK_F16) return set_error(DECIK_ERR_INVALID, "qkv_proj_fwd: dtype %d", dtype);
+  if (norm_w != nullptr && ((norm_dtype != DECIK_F32 && norm_dtype != DECIK_F16) || !(eps >= 0.f) ||
+                            (norm_dtype == DECIK_F32 && !aligned16(norm_w))))
+    return set_error(DECIK_ERR_INVALID, "qkv_proj_norm_fwd: norm weight dtype %d (F32 16-byte aligned, or F16), eps %g",
+                     norm_dtype, static_cast<double>(eps));
   cudaStream_t s = as_stream(stream);
   const int n_proj = (n_heads + 2 * n_kv) * kD;
   constexpr int BN = Cfg<EPI_QKV>::BN;
@@ -937,22 +992,45 @@ extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat
   p.hk = n_kv;
   p.err = attn::attn_error_word();
   // x16 and u first (the GEMM's A operands), then the GEMM + epilogue
-  const int grid_cast = static_cast<int>((n_tok + kCastTok - 1) / kCastTok);
   const int64_t a_off = static_cast<int64_t>(n_proj) * ldw;
   if (dtype == DECIK_BF16) {
     using T = __nv_bfloat16;
-    x_cast_lora_down_kernel<T><<<grid_cast, kCastThreads, 0, s>>>(
-        x, ldx, lora ? static_cast<const T*>(w_cat) + a_off : nullptr, ldw, static_cast<T*>(x16), ldx16,
-        static_cast<T*>(u), n_tok, hidden);
-    if (int rc = check_launch("x_cast_lora_down")) return rc;
+    if (int rc = launch_cast<T>(x, ldx, lora ? static_cast<const T*>(w_cat) + a_off : nullptr, ldw,
+                                static_cast<T*>(x16), ldx16, static_cast<T*>(u), n_tok, hidden, norm_w, norm_dtype,
+                                eps, rstd, s))
+      return rc;
     return launch_gemm<T, EPI_QKV, true>(p, s, "qkv_proj_gemm");
   }
   using T = __half;
-  x_cast_lora_down_kernel<T><<<grid_cast, kCastThreads, 0, s>>>(
-      x, ldx, lora ? static_cast<const T*>(w_cat) + a_off : nullptr, ldw, static_cast<T*>(x16), ldx16,
-      static_cast<T*>(u), n_tok, hidden);
-  if (int rc = check_launch("x_cast_lora_down")) return rc;
+  if (int rc = launch_cast<T>(x, ldx, lora ? static_cast<const T*>(w_cat) + a_off : nullptr, ldw,
+                              static_cast<T*>(x16), ldx16, static_cast<T*>(u), n_tok, hidden, norm_w, norm_dtype, eps,
+                              rstd, s))
+    return rc;
   return launch_gemm<T, EPI_QKV, true>(p, s, "qkv_proj_gemm");
+}
+
+}  // namespace
+}  // namespace proj
+}  // namespace decik
+
+extern "C" int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat, int64_t ldw, const void* ext_b,
+                                  int lora, const float* cosp, const float* sinp, decik_tensor3_mut q,
+                                  decik_tensor3_mut k, decik_tensor3_mut v, void* x16, int64_t ldx16, void* u,
+                                  int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim, int dtype,
+                                  void* stream) {
+  return decik::proj::qkv_proj_fwd_impl(x, ldx, nullptr, 0, 0.f, nullptr, w_cat, ldw, ext_b, lora, cosp, sinp, q, k,
+                                        v, x16, ldx16, u, n_tok, hidden, n_heads, n_kv, head_dim, dtype, stream);
+}
+
+extern "C" int decik_qkv_proj_norm_fwd(const float* h, int64_t ldh, const void* norm_w, int norm_dtype, float eps,
+                                       float* rstd, const void* w_cat, int64_t ldw, const void* ext_b, int lora,
+                                       const float* cosp, const float* sinp, decik_tensor3_mut q, decik_tensor3_mut k,
+                                       decik_tensor3_mut v, void* x16, int64_t ldx16, void* u, int64_t n_tok,
+                                       int hidden, int n_heads, int n_kv, int head_dim, int dtype, void* stream) {
+  if (n_tok != 0 && (norm_w == nullptr || rstd == nullptr))
+    return decik::set_error(DECIK_ERR_INVALID, "qkv_proj_norm_fwd: NULL norm weight or rstd");
+  return decik::proj::qkv_proj_fwd_impl(h, ldh, norm_w, norm_dtype, eps, rstd, w_cat, ldw, ext_b, lora, cosp, sinp, q,
+                                        k, v, x16, ldx16, u, n_tok, hidden, n_heads, n_kv, head_dim, dtype, stream);
 }
 
 extern "C" int decik_proj_dx(const void* dy, int64_t ld_dy, int k_cols, const void* w_t, int64_t ldw, float* dx,

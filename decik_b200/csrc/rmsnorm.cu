@@ -13,49 +13,19 @@
 // as the plain kernels (sumsq4 / wdot4 / the output lines), so y and the norm gradient equal
 // rmsnorm_fwd / rmsnorm_bwd applied to the same h bit for bit.
 #include "common.cuh"
+#include "norm_math.cuh"
 
 namespace decik {
 namespace {
 
-template <typename W>
-__device__ __forceinline__ float wload(const W* w, int i);
-template <> __device__ __forceinline__ float wload<float>(const float* w, int i) { return __ldg(w + i); }
-template <> __device__ __forceinline__ float wload<__half>(const __half* w, int i) { return __half2float(w[i]); }
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
+using norm::norm_grad4;
+using norm::norm_out4;
+using norm::sumsq4;
+using norm::warp_sum;
+using norm::wdot4;
+using norm::wload;
 
 constexpr int kMaxCols = 8192;
-
-// x . x of four values and the weighted dot g . (w x) of four, the per-step row terms of the
-// forward and backward reductions (shared by the plain and the fused kernels)
-__device__ __forceinline__ float sumsq4(float4 v) { return v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w; }
-template <typename W>
-__device__ __forceinline__ float wdot4(float4 g, float4 v, const W* w, int c) {
-  return g.x * wload<W>(w, c) * v.x + g.y * wload<W>(w, c + 1) * v.y + g.z * wload<W>(w, c + 2) * v.z +
-         g.w * wload<W>(w, c + 3) * v.w;
-}
-template <typename W>
-__device__ __forceinline__ float4 norm_out4(float4 v, const W* w, int c, float rstd) {
-  float4 o;
-  o.x = wload<W>(w, c) * (v.x * rstd);
-  o.y = wload<W>(w, c + 1) * (v.y * rstd);
-  o.z = wload<W>(w, c + 2) * (v.z * rstd);
-  o.w = wload<W>(w, c + 3) * (v.w * rstd);
-  return o;
-}
-template <typename W>
-__device__ __forceinline__ float4 norm_grad4(float4 g, float4 v, const W* w, int c, float rstd, float k) {
-  float4 o;
-  o.x = rstd * (g.x * wload<W>(w, c) - v.x * k);
-  o.y = rstd * (g.y * wload<W>(w, c + 1) - v.y * k);
-  o.z = rstd * (g.z * wload<W>(w, c + 2) - v.z * k);
-  o.w = rstd * (g.w * wload<W>(w, c + 3) - v.w * k);
-  return o;
-}
 
 // four consecutive values of the delta operand as fp32, and four fp32 values stored in its type
 template <typename D>
@@ -93,8 +63,7 @@ rmsnorm_fwd_kernel(const float* __restrict__ x, const W* __restrict__ w, float* 
   const float* xr = x + row * sx;
   float acc = 0.f;
   for (int c = lane * 4; c < n_cols; c += 128) acc += sumsq4(__ldg(reinterpret_cast<const float4*>(xr + c)));
-  const float mean_sq = warp_sum(acc) / static_cast<float>(n_cols);
-  const float rstd = rsqrtf(mean_sq + eps);
+  const float rstd = norm::row_rstd(acc, n_cols, eps);
   float* yr = y + row * sy;
   for (int c = lane * 4; c < n_cols; c += 128)
     *reinterpret_cast<float4*>(yr + c) = norm_out4<W>(__ldg(reinterpret_cast<const float4*>(xr + c)), w, c, rstd);
@@ -139,8 +108,7 @@ add_rmsnorm_fwd_kernel(const float* __restrict__ residual, const D* __restrict__
     *reinterpret_cast<float4*>(h + off + c) = v;
     acc += sumsq4(v);
   }
-  const float mean_sq = warp_sum(acc) / static_cast<float>(n_cols);
-  const float rstd = rsqrtf(mean_sq + eps);
+  const float rstd = norm::row_rstd(acc, n_cols, eps);
   for (int c = lane * 4; c < n_cols; c += 128) {
     const float4 v = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
     *reinterpret_cast<float4*>(y + off + c) = norm_out4<W>(v, w, c, rstd);

@@ -470,12 +470,14 @@ def lora_b_ext(b_q: torch.Tensor | None, b_v: torch.Tensor | None, scaling: floa
 
 
 def qkv_proj_fwd(x: torch.Tensor, w_cat: torch.Tensor, ext_b: torch.Tensor, lora: bool, cos: torch.Tensor,
-                 sin: torch.Tensor, n_heads: int, n_kv: int):
+                 sin: torch.Tensor, n_heads: int, n_kv: int, norm: tuple | None = None):
     """The block's forward projections on tcgen05 (decik_qkv_proj_fwd): from x fp32 [T, H], w_cat
     [(Hq+2Hk)*D (+ 32 with ``lora``), H] (W_q, W_k, W_v rows, then A_q, A_v as lora_pack wrote them)
     and the extra K block's B operand (lora_b_ext: scaled lora_B and the bias) returns x16 [T, H],
     u [T, 64] (u_q | u_v | 1 | zeros), q [Hq, T, D] and k [Hk, T, D] head-major with RoPE,
-    v [T, Hk, D]."""
+    v [T, Hk, D]. With ``norm`` = (weight, eps) x is the decoder layer's input h and the input
+    RMSNorm runs inside the first kernel (decik_qkv_proj_norm_fwd); then rstd [T] comes back as a
+    sixth value."""
     _cuda(x, w_cat, ext_b, cos, sin)
     T, H = x.shape
     D = cos.shape[-1]
@@ -487,13 +489,23 @@ def qkv_proj_fwd(x: torch.Tensor, w_cat: torch.Tensor, ext_b: torch.Tensor, lora
     q = torch.empty((n_heads, T, D), dtype=dt, device=dev)
     k = torch.empty((n_kv, T, D), dtype=dt, device=dev)
     v = torch.empty((T, n_kv, D), dtype=dt, device=dev)
+    outs = (_t3any(q.transpose(0, 1)), _t3any(k.transpose(0, 1)), _t3any(v), _p(x16), x16.stride(0), _p(u), T, H,
+            n_heads, n_kv, D, _dt(w_cat), _stream(x))
+    tail = (_p(w_cat), w_cat.stride(0), _p(ext_b), 1 if lora else 0, _p(cos.contiguous()), _p(sin.contiguous()))
+    if norm is None:
+        with _timed("qkv_proj_fwd", 2):
+            rc = _lib.lib().decik_qkv_proj_fwd(_p(x), x.stride(0), *tail, *outs)
+        _lib.check(rc, "qkv_proj_fwd")
+        return x16, u, q, k, v
+    w, eps = norm
+    _cuda(w)
+    w = w.contiguous()
+    rstd = torch.empty(T, dtype=torch.float32, device=dev)
     with _timed("qkv_proj_fwd", 2):
-        rc = _lib.lib().decik_qkv_proj_fwd(
-            _p(x), x.stride(0), _p(w_cat), w_cat.stride(0), _p(ext_b), 1 if lora else 0,
-            _p(cos.contiguous()), _p(sin.contiguous()), _t3any(q.transpose(0, 1)), _t3any(k.transpose(0, 1)),
-            _t3any(v), _p(x16), x16.stride(0), _p(u), T, H, n_heads, n_kv, D, _dt(w_cat), _stream(x))
-    _lib.check(rc, "qkv_proj_fwd")
-    return x16, u, q, k, v
+        rc = _lib.lib().decik_qkv_proj_norm_fwd(_p(x), x.stride(0), _p(w), _dt(w), float(eps), _p(rstd), *tail,
+                                                *outs)
+    _lib.check(rc, "qkv_proj_norm_fwd")
+    return x16, u, q, k, v, rstd
 
 
 def transpose16(src: torch.Tensor) -> torch.Tensor:

@@ -6,7 +6,9 @@
 - ``SKC_RMSNORM``     Qwen2RMSNorm -> sm_100a RMSNorm, recorded as the LoRA input link (rmsnorm.py)
 - ``SKC_MLP``         Qwen2MLP with NF4 gate/up/down -> one node: one gate|up GEMM, sm_100a SwiGLU (mlp.py)
 - ``SKC_VARLEN``      padding-free decoder + varlen attention (varlen.py); ``SKC_VARLEN_ATTN``;
-                      ``SKC_ADDNORM`` (residual add + post-attention norm as one node)
+                      ``SKC_ADDNORM`` (residual add + post-attention norm as one node);
+                      ``SKC_FUSED_NORM`` (this build's addition: the input RMSNorm runs inside the
+                      fused block's first kernel)
 - ``SKC_ATTN``        Qwen2Attention forward: LoRA + RoPE + varlen attention (attn.py);
                       ``SKC_LORA_RECOMPUTE``; ``SKC_FUSED_BLOCK`` (this build's addition: LoRA
                       without dropout runs as one fused projection + attention node)
@@ -40,7 +42,7 @@ def apply(linear4bit_cls=None, lora_classes=None):
         _try(mlp.patch, "Qwen2MLP", linear4bit_cls)
     if _enabled("VARLEN"):
         _try(varlen.patch, "Qwen2Model", varlen_attention=_enabled("VARLEN_ATTN"),
-             fuse_residual=_enabled("ADDNORM"))
+             fuse_residual=_enabled("ADDNORM"), fuse_input_norm=_enabled("FUSED_NORM"))
         if _enabled("ATTN"):
             _try(attn.patch, "Qwen2Attention", recompute_lora=_enabled("LORA_RECOMPUTE"),
                  linear4bit_cls=linear4bit_cls, lora_classes=lora_classes,

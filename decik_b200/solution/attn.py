@@ -19,6 +19,9 @@ from .. import ops
 from . import rmsnorm
 from ._state import STATE, on_gpu
 
+# keyword under which the patched decoder layer hands its input RMSNorm to the patched attention
+INPUT_NORM_KW = "decik_input_norm"
+
 
 class FusedQKRope(torch.autograd.Function):
     """(q_base + q_lora, k) -> RoPE'd q [1, HQ, T, D] and k [1, HK, T, D] (solution/attn.py:93-126)."""
@@ -58,11 +61,17 @@ class FusedAttentionBlock(torch.autograd.Function):
 
     With ``w_o`` (the dequantised NF4 o_proj weight [H, Hq*D], optional bias ``b_o``) the node
     also applies o_proj (solution/attn.py:418) and returns [T, H]: the same F.linear the
-    reference's NF4Linear runs, with the weight kept for backward instead of dequantised again."""
+    reference's NF4Linear runs, with the weight kept for backward instead of dequantised again.
+
+    With ``norm_w`` (the decoder layer's input RMSNorm weight, ``norm_eps`` its epsilon) ``x`` is
+    the layer input h and the norm runs inside the forward's first kernel
+    (decik_qkv_proj_norm_fwd: the norm's fp32 output is never written); the backward applies the
+    norm's backward (decik_rmsnorm_bwd, from the kept rstd) to dX and returns the gradient for h.
+    The LoRA gradients use the kept x16, so there is no norm recompute (solution/attn.py:238)."""
 
     @staticmethod
     def forward(ctx, x, a_q, b_q, a_v, b_v, w_cat, bias_cat, cos, sin, cu_seqlens, max_len, n_heads,
-                n_kv, scaling, scale, w_o=None, b_o=None):
+                n_kv, scaling, scale, w_o=None, b_o=None, norm_w=None, norm_eps=0.0):
         dt = w_cat.dtype
         D = cos.shape[-1]
         r = a_q.shape[0]
@@ -70,9 +79,15 @@ class FusedAttentionBlock(torch.autograd.Function):
         frag = ops.lora_pack(a_q, a_v, b_q, b_v, dt, a_out=w_cat[n_proj:])
         ext_b = ops.lora_b_ext(b_q, b_v, scaling, bias_cat, dt, n_heads, n_kv)  # scaled lora_B + bias
         x32 = x if (x.dtype == torch.float32 and x.stride(-1) == 1) else x.float().contiguous()
-        x16, u, q, k, v = ops.qkv_proj_fwd(x32, w_cat, ext_b, True, cos, sin, n_heads, n_kv)
+        if norm_w is None:
+            x16, u, q, k, v = ops.qkv_proj_fwd(x32, w_cat, ext_b, True, cos, sin, n_heads, n_kv)
+            h = rstd = None
+        else:
+            x16, u, q, k, v, rstd = ops.qkv_proj_fwd(x32, w_cat, ext_b, True, cos, sin, n_heads, n_kv,
+                                                     norm=(norm_w, norm_eps))
+            h = x32
         out, lse = ops.varlen_attn_fwd(q.transpose(0, 1), k.transpose(0, 1), v, cu_seqlens, max_len, scale)
-        ctx.save_for_backward(x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu_seqlens, w_o)
+        ctx.save_for_backward(x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu_seqlens, w_o, h, norm_w, rstd)
         ctx.meta = (int(max_len), n_heads, n_kv, float(scaling), float(scale), r)
         if w_o is not None:
             return F.linear(out.view(out.shape[0], -1), w_o, b_o)
@@ -80,7 +95,7 @@ class FusedAttentionBlock(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu, w_o = ctx.saved_tensors
+        x16, w_cat, u, frag, cos, sin, q, k, v, out, lse, cu, w_o, h, norm_w, rstd = ctx.saved_tensors
         max_len, n_heads, n_kv, scaling, scale, r = ctx.meta
         if w_o is not None:  # through o_proj first: the attention output's gradient
             grad_out = torch.mm(grad_out.reshape(-1, grad_out.shape[-1]).to(w_o.dtype), w_o).view(out.shape)
@@ -96,7 +111,9 @@ class FusedAttentionBlock(torch.autograd.Function):
                          frag, scaling, dy)
         dx = ops.proj_dx(dy, ops.transpose16(w_cat))
         da, db = ops.lora_grads(dy, x16, u, scaling, n_heads, n_kv)
-        return (dx, da[:r], db[:n_q], da[r:], db[n_q:]) + (None,) * 12
+        if norm_w is not None:  # through the input norm: the gradient for the layer input h
+            dx = ops.rmsnorm_bwd(dx, h, norm_w, rstd)
+        return (dx, da[:r], db[:n_q], da[r:], db[n_q:]) + (None,) * 14
 
 
 def pack_keep(keep_q, keep_v):
@@ -259,11 +276,14 @@ def _nf4_parts(module, n_in, dtype):
     return weight.data, qs, bias
 
 
-def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim, o_nf4=False):
+def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim, o_nf4=False,
+                 input_norm=None):
     """(output, o_proj applied) through FusedAttentionBlock, or None when this layer does not
     qualify: both LoRA branches without dropout, rank 16 and one scaling; q, k, v NF4 linears of the
     compute dtype; the varlen attention switched on; head_dim 128. With ``o_nf4`` (o_proj is a plain
-    NF4 Linear4bit of the compute dtype) o_proj joins the node: the output is then [1, T, H]."""
+    NF4 Linear4bit of the compute dtype) o_proj joins the node: the output is then [1, T, H].
+    With ``input_norm`` (the decoder layer's input RMSNorm module, eligible for the fused kernel)
+    ``x`` is the layer input and the norm runs inside the node."""
     from .nf4 import dequantize_nf4_many
 
     pq, pv = _lora_parts(self.q_proj, q_name), _lora_parts(self.v_proj, v_name)
@@ -297,7 +317,9 @@ def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_k
     out = FusedAttentionBlock.apply(x.reshape(n_tok, hidden), pq[0], pq[1], pv[0], pv[1], w_cat, bias_cat,
                                     cos.reshape(n_tok, -1), sin.reshape(n_tok, -1),
                                     packing.cu_seqlens(x.device), packing.max_len, n_heads, n_kv, pq[2],
-                                    self.scaling, w_o, b_o)
+                                    self.scaling, w_o, b_o,
+                                    None if input_norm is None else input_norm.weight,
+                                    0.0 if input_norm is None else float(input_norm.variance_epsilon))
     return out.reshape(1, n_tok, -1), w_o is not None
 
 
@@ -326,6 +348,10 @@ def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None, fused_blo
                 and getattr(module, "compute_dtype", None) in (torch.float16, torch.bfloat16))
 
     def forward(self, hidden_states, position_embeddings, attention_mask, past_key_values=None, **kwargs):
+        # the patched decoder layer may hand over its input RMSNorm with the layer input (instead of
+        # the norm's output) so that the fused block runs the norm in its first kernel; any other
+        # path applies the norm here first
+        input_norm = kwargs.pop(INPUT_NORM_KW, None)
         packing = STATE.packing
         q_name = _single_lora(getattr(self, "q_proj", None), lora_classes)
         v_name = _single_lora(getattr(self, "v_proj", None), lora_classes)
@@ -343,6 +369,8 @@ def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None, fused_blo
                 and cos.shape == (1, packing.n_tokens, head_dim) and sin.shape == cos.shape
                 and head_dim == 128 and cos.is_contiguous() and sin.is_contiguous()
                 and getattr(self, "sliding_window", None) is None):
+            if input_norm is not None:
+                hidden_states = input_norm(hidden_states)
             return original(self, hidden_states, position_embeddings, attention_mask,
                             past_key_values=past_key_values, **kwargs)
         dtype = self.q_proj.base_layer.compute_dtype
@@ -352,10 +380,12 @@ def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None, fused_blo
         x = hidden_states
         if fused_block:
             res = _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim,
-                               o_nf4=nf4_linear(getattr(self, "o_proj", None)))
+                               o_nf4=nf4_linear(getattr(self, "o_proj", None)), input_norm=input_norm)
             if res is not None:
                 out, o_done = res
                 return (out if o_done else self.o_proj(out)), None
+        if input_norm is not None:
+            x = input_norm(x)
         link = STATE.norm_link
         parts_q = parts_v = None
         if (recompute_lora and link is not None and link[0] is x

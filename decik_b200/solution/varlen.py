@@ -279,8 +279,9 @@ def _packed_sdpa(original, varlen_attention):
     return sdpa
 
 
-def _decoder_layer(original, fuse_residual):
+def _decoder_layer(original, fuse_residual, fuse_input_norm=True):
     from . import rmsnorm
+    from .attn import INPUT_NORM_KW
 
     def forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
                 use_cache=False, position_embeddings=None, **kwargs):
@@ -294,9 +295,18 @@ def _decoder_layer(original, fuse_residual):
         # (solution/varlen.py:323-343): the norm input is rebuilt in backward from the layer input
         # and the 16-bit attention output, not kept
         layer_in = hidden_states
-        attn, _ = self.self_attn(hidden_states=self.input_layernorm(layer_in), attention_mask=None,
-                                 position_ids=position_ids, past_key_values=None, use_cache=False,
-                                 position_embeddings=position_embeddings, **kwargs)
+        norm_in = getattr(self, "input_layernorm", None)
+        if (fuse_input_norm and getattr(type(self.self_attn).forward, "_skc", False)
+                and rmsnorm.fusable(norm_in, layer_in)):
+            # the patched attention takes the layer input and its norm: the fused block then runs
+            # the norm inside its first kernel (any other path applies it first)
+            attn, _ = self.self_attn(hidden_states=layer_in, attention_mask=None, position_ids=position_ids,
+                                     past_key_values=None, use_cache=False,
+                                     position_embeddings=position_embeddings, **{INPUT_NORM_KW: norm_in}, **kwargs)
+        else:
+            attn, _ = self.self_attn(hidden_states=norm_in(layer_in), attention_mask=None,
+                                     position_ids=position_ids, past_key_values=None, use_cache=False,
+                                     position_embeddings=position_embeddings, **kwargs)
         if (isinstance(attn, torch.Tensor) and attn.is_cuda and attn.shape == layer_in.shape
                 and attn.dtype in (torch.float16, torch.bfloat16)):
             eps = float(post_norm.variance_epsilon)
@@ -320,10 +330,12 @@ def _dropout(original):
     return forward
 
 
-def patch(varlen_attention=True, fuse_residual=True):
+def patch(varlen_attention=True, fuse_residual=True, fuse_input_norm=True):
     """Install the packed decoder (solution/varlen.py:229-359): Qwen2Model.forward (packing),
     ALL_ATTENTION_FUNCTIONS["sdpa"], Qwen2DecoderLayer.forward (with ``fuse_residual``: the
-    residual add + post-attention norm as one AddRMSNormFn) and nn.Dropout. Inputs the packed path
+    residual add + post-attention norm as one AddRMSNormFn; with ``fuse_input_norm`` the input
+    RMSNorm is handed to the patched attention, whose fused block runs it in its first kernel) and
+    nn.Dropout. Inputs the packed path
     is not for go to the original code; eligible packed attention always runs the sm_100a kernel
     (no per-row fallback). Idempotent."""
     from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
@@ -335,7 +347,7 @@ def patch(varlen_attention=True, fuse_residual=True):
     STATE.varlen_attention = bool(varlen_attention)
     installs = ((model_cls, "forward", _model_forward(model_cls.forward)),
                 (modeling_qwen2.Qwen2DecoderLayer, "forward",
-                 _decoder_layer(modeling_qwen2.Qwen2DecoderLayer.forward, fuse_residual)),
+                 _decoder_layer(modeling_qwen2.Qwen2DecoderLayer.forward, fuse_residual, fuse_input_norm)),
                 (torch.nn.Dropout, "forward", _dropout(torch.nn.Dropout.forward)))
     ALL_ATTENTION_FUNCTIONS["sdpa"] = _packed_sdpa(ALL_ATTENTION_FUNCTIONS["sdpa"], varlen_attention)
     for cls, name, fn in installs:

@@ -376,6 +376,19 @@ DECIK_API int decik_qkv_proj_fwd(const float* x, int64_t ldx, const void* w_cat,
                                  int64_t n_tok, int hidden, int n_heads, int n_kv, int head_dim, int dtype,
                                  void* stream);
 
+/* decik_qkv_proj_norm_fwd: decik_qkv_proj_fwd with the decoder layer's input RMSNorm fused into its
+ * first kernel (the reference's Qwen2RMSNorm, solution/rmsnorm.py:17-28, whose fp32 output the
+ * attention casts to 16 bits). h fp32 [T, hidden] (ldh) is the layer input; the pass computes
+ * x = norm_w * (h * rstd), rstd = rsqrt(mean(h^2) + eps), exactly as decik_rmsnorm_fwd does (the
+ * same reduction order: x16 equals decik_rmsnorm_fwd's output cast to dt), and writes rstd fp32
+ * [T] for the norm's backward (decik_rmsnorm_bwd). x never exists in fp32. norm_w of norm_dtype
+ * (F32, 16-byte aligned, or F16) [hidden]. The other arguments are decik_qkv_proj_fwd's. */
+DECIK_API int decik_qkv_proj_norm_fwd(const float* h, int64_t ldh, const void* norm_w, int norm_dtype, float eps,
+                                      float* rstd, const void* w_cat, int64_t ldw, const void* ext_b, int lora,
+                                      const float* cosp, const float* sinp, decik_tensor3_mut q, decik_tensor3_mut k,
+                                      decik_tensor3_mut v, void* x16, int64_t ldx16, void* u, int64_t n_tok,
+                                      int hidden, int n_heads, int n_kv, int head_dim, int dtype, void* stream);
+
 /* dx = dy[:, 0:k_cols] . w_t[:, 0:k_cols]^T in fp32 [T, hidden] (ld_dx), w_t dt [hidden, >= k_cols]
  * (ldw) the TRANSPOSED weight (decik_transpose16 of W_cat [k_cols, hidden]): the three NF4Linear
  * input gradients (solution/nf4.py:99-104: g16 @ W16) and both LoRA input gradients

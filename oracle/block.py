@@ -93,18 +93,26 @@ def block_forward(x, w_q, w_k, w_v, b_q, b_k, b_v, a_q, bb_q, a_v, bb_v, scaling
     return out[0].reshape(T, n_heads * D)
 
 
+def rmsnorm_torch(h: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """Qwen2RMSNorm in fp32 (solution/rmsnorm.py:17-28): w * (h * rsqrt(mean(h^2) + eps))."""
+    return w * (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps))
+
+
 def block_step(inputs: dict, grad_out: torch.Tensor, weights: dict | None = None):
     """One forward + backward of the block. ``inputs`` holds torch fp32 CPU tensors: x, b_q, b_k,
     b_v, a_q, bb_q, a_v, bb_v, cos, sin and the NF4 states nf4_q/k/v, spans, n_heads, n_kv,
     scaling. Returns (out, dx, dA_q, dB_q, dA_v, dB_v). ``weights`` may carry pre-dequantised
-    (w_q, w_k, w_v); otherwise the dequant runs here, as in every reference step."""
+    (w_q, w_k, w_v); otherwise the dequant runs here, as in every reference step. With
+    ``inputs["norm_w"]`` (and ``"eps"``) x is the decoder layer's input and the block starts with
+    its input RMSNorm; dx is then the gradient for that input."""
     if weights is None:
         w_q, w_k, w_v = (dequant_torch(inputs[n]) for n in ("nf4_q", "nf4_k", "nf4_v"))
     else:
         w_q, w_k, w_v = weights["w_q"], weights["w_k"], weights["w_v"]
     x = inputs["x"].detach().clone().requires_grad_(True)
     params = [inputs[n].detach().clone().requires_grad_(True) for n in ("a_q", "bb_q", "a_v", "bb_v")]
-    out = block_forward(x, w_q, w_k, w_v, inputs["b_q"], inputs["b_k"], inputs["b_v"],
+    xn = x if inputs.get("norm_w") is None else rmsnorm_torch(x, inputs["norm_w"], inputs["eps"])
+    out = block_forward(xn, w_q, w_k, w_v, inputs["b_q"], inputs["b_k"], inputs["b_v"],
                         params[0], params[1], params[2], params[3], inputs["scaling"],
                         inputs["cos"], inputs["sin"], inputs["spans"], inputs["n_heads"],
                         inputs["n_kv"])

@@ -116,3 +116,34 @@ def test_block_7b_shape(cuda_lib, dtype):
         bar = _bar("7b", dtype, name)
         assert_close16(a.numpy(), e.numpy(), f"{name} (7B shape, {dtype})", rel_l2=bar)
     assert cuda_lib.decik_kernel_error(1) == 0
+
+
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "chain"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+def test_block_with_input_norm_matches_oracle(cuda_lib, fused, dtype):
+    """The block fed the decoder layer's input h and its input RMSNorm (weight ~ 1 + 0.1 N(0, 1),
+    eps 1e-6): in the fused node the norm runs inside the first kernel and its backward after the dX
+    GEMM; the chain runs RMSNormFn first. Against the oracle: RMSNorm in fp64 (oracle/rmsnorm.py),
+    the norm output rounded to the 16-bit dtype as the kernels' x16, the block in fp32, then the
+    norm's backward of dx. The gradient checked is the one for h."""
+    from oracle import rmsnorm as o_norm
+
+    block, packing, cos, sin, h, dout = _case(dtype, seed=7)
+    g = torch.Generator().manual_seed(11)
+    w = 1.0 + 0.1 * torch.randn(h.shape[1], generator=g)
+    eps = 1e-6
+    hg = h.cuda().requires_grad_(True)
+    for p in block.lora_params():
+        p.grad = None
+    out = block.forward(hg, packing, cos, sin, fused=fused, norm=(w.cuda(), eps))
+    out.backward(dout.cuda())
+    torch.cuda.synchronize()
+    got = (out.detach().float().cpu(), hg.grad.cpu()) + tuple(p.grad.cpu() for p in block.lora_params())
+    x_ref, _ = o_norm.forward(h.numpy(), w.numpy(), eps)
+    ref = list(_oracle(block, packing, cos, sin, torch.from_numpy(x_ref).float(), dout))
+    ref[1] = torch.from_numpy(o_norm.backward(ref[1].numpy(), h.numpy(), w.numpy(), eps)).float()
+    for name, a, e in zip(("out", "dh", "dA_q", "dB_q", "dA_v", "dB_v"), got, ref):
+        bar = _bar("fused" if fused else "chain", dtype, name)
+        assert_close16(a.numpy(), e.numpy(), f"{name} (input norm, {'fused' if fused else 'chain'}, {dtype})",
+                       rel_l2=bar)
+    assert cuda_lib.decik_kernel_error(1) == 0

@@ -120,7 +120,7 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     solution.apply(linear4bit_cls=Linear4bit, lora_classes=(LoraLayer,))
     fns = (("rope", attn.FusedQKRope), ("varlen", varlen.VarlenSDPA), ("pair", attn.LoRAPairFromNorm),
            ("fused", attn.FusedAttentionBlock), ("addnorm", rmsnorm.AddRMSNormFn), ("mlp", mlp.FusedMLP),
-           ("nf4linear", nf4.NF4Linear))
+           ("nf4linear", nf4.NF4Linear), ("rmsnorm", rmsnorm.RMSNormFn))
     calls = {n: 0 for n, _ in fns}
     orig = {n: getattr(c, "forward") for n, c in fns}
 
@@ -139,11 +139,13 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
             c.forward = orig[n]
     assert packed1
     n_layers = len(model.model.layers)
-    # without LoRA dropout every layer runs as one fused node (o_proj included); with it, the
-    # reference's chain, whose q, k, v and o projections are NF4Linear calls
+    # without LoRA dropout every layer runs as one fused node (o_proj and the input norm included);
+    # with it, the reference's chain, whose q, k, v and o projections are NF4Linear calls and whose
+    # input norm is an RMSNormFn. The model's final norm is one more RMSNormFn.
     chain = n_layers if lora_dropout > 0 else 0
     assert calls == {"rope": chain, "varlen": chain, "pair": chain, "fused": n_layers - chain,
-                     "addnorm": n_layers, "mlp": n_layers, "nf4linear": 4 * chain}, calls
+                     "addnorm": n_layers, "mlp": n_layers, "nf4linear": 4 * chain,
+                     "rmsnorm": chain + 1}, calls
     print(f"loss {l0.item():.6f} -> {l1.item():.6f}")
     assert abs(l1.item() - l0.item()) / abs(l0.item()) < 2e-3, (l1.item(), l0.item())
     assert set(g1) == set(g0)

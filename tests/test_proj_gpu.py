@@ -113,6 +113,34 @@ def test_proj_dx_and_lora_grads_match_torch(cuda_lib, T, hidden, hq, hk, dtype):
     assert cuda_lib.decik_kernel_error(1) == 0
 
 
+@pytest.mark.parametrize("T,hidden,hq,hk", [(830, 1536, 12, 2), (1, 1536, 12, 2), (16384, 1536, 12, 2),
+                                          (1000, 3584, 28, 4), (257, 1536, 12, 2)],
+                         ids=["config1", "one-token", "bench", "7b", "ragged"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("w_dtype", [torch.float32, torch.float16], ids=["w32", "w16"])
+def test_qkv_proj_norm_fwd_equals_norm_then_proj(cuda_lib, T, hidden, hq, hk, dtype, w_dtype):
+    """The input RMSNorm inside the first kernel (decik_qkv_proj_norm_fwd) against the norm kernel
+    followed by decik_qkv_proj_fwd: rstd, x16, u, q, k and v equal bit for bit."""
+    from decik_b200 import ops
+
+    h, w_cat, bias, b_q, b_v, cos, sin = _inputs(T, hidden, hq, hk, dtype, seed=3 * T + hq)
+    h = h * 3.0 + 0.5
+    n_proj = (hq + 2 * hk) * 128
+    g = torch.Generator(device=DEV).manual_seed(T)
+    w = (1.0 + 0.1 * torch.randn(hidden, device=DEV, generator=g)).to(w_dtype)
+    a_q = torch.randn(16, hidden, device=DEV) * hidden ** -0.5
+    a_v = torch.randn(16, hidden, device=DEV) * hidden ** -0.5
+    ops.lora_pack(a_q, a_v, b_q, b_v, dtype, a_out=w_cat[n_proj:])
+    ext = ops.lora_b_ext(b_q, b_v, 2.0, bias, dtype, hq, hk)
+    x, rstd_ref = ops.rmsnorm_fwd(h, w, 1e-6)
+    ref = ops.qkv_proj_fwd(x, w_cat, ext, True, cos, sin, hq, hk)
+    got = ops.qkv_proj_fwd(h, w_cat, ext, True, cos, sin, hq, hk, norm=(w, 1e-6))
+    assert torch.equal(got[5], rstd_ref)
+    for name, a, e in zip(("x16", "u", "q", "k", "v"), got[:5], ref):
+        assert torch.equal(a, e), name
+    assert cuda_lib.decik_kernel_error(1) == 0
+
+
 def test_proj_entry_points_reject_bad_arguments(cuda_lib):
     from decik_b200 import _lib
 
@@ -123,3 +151,6 @@ def test_proj_entry_points_reject_bad_arguments(cuda_lib):
                                   12, 2, 128, _lib.BF16, None) == 1
     assert lib.decik_proj_dx(None, 8, 8, None, 8, None, 8, 5, 100, _lib.BF16, None) == 1
     assert lib.decik_lora_grads(None, 8, None, 8, None, 64, None, None, 1.0, 5, 100, 12, 2, _lib.BF16, None) == 1
+    # the norm variant: no norm weight, and a norm weight of an unsupported dtype
+    assert lib.decik_qkv_proj_norm_fwd(None, 1536, None, _lib.F32, 1e-6, None, None, 1536, None, 1, None, None,
+                                       z, z, z, None, 1536, None, 5, 1536, 12, 2, 128, _lib.BF16, None) == 1
