@@ -102,6 +102,14 @@ __device__ __forceinline__ void load_tile(uint32_t dst, const CUtensorMap* map, 
   load_half(dst, map, bar, order, 0, tok, head);
   load_half(dst + HALF, map, bar, order, 64, tok, head);
 }
+// a [128 x 128] tile into L2 ahead of its load
+__device__ __forceinline__ void prefetch_tile(const CUtensorMap* map, int order, int tok, int head) {
+#pragma unroll
+  for (int c = 0; c < 128; c += 64) {
+    if (order == 0) tma_prefetch_3d(map, c, tok, head);
+    else tma_prefetch_3d(map, c, head, tok);
+  }
+}
 
 // Descriptors are built once; a k-step advances the 14-bit start-address field (bytes >> 4), which
 // never carries out of the field for shared-memory addresses.
@@ -263,6 +271,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       if (lane == 0) {
         mbar_expect_tx(bar(B_DOF), TILE);
         load_tile(sb + OFF_DO, &p.tdo, bar(B_DOF), p.order_do, start + m0, h);
+        // dO(it + 1) is loaded only once dV(it) has read this stage, right before dP(it + 1) needs
+        // it: bring it (and Q two iterations ahead) into L2 now, an iteration early
+        if (it + 1 < n_iter) prefetch_tile(&p.tdo, p.order_do, start + it_m0(it + 1), it_head(it + 1));
+        if (it + 2 < n_iter) prefetch_tile(&p.tq, p.order_q, start + it_m0(it + 2), it_head(it + 2));
       }
       issued_do = it + 1;
     }

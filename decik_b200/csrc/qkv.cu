@@ -35,7 +35,10 @@ namespace {
 
 constexpr int kD = 128;     // head_dim
 constexpr int kR = 16;      // LoRA rank
-constexpr int kWarps = 8;   // backward: warps per CTA; warp w takes heads w, w + 8, ...
+// backward: warps per CTA; warp w takes heads w, w + 16, ...: at the 1.5B shape (16 heads of q,
+// k, v) every head's tile load is in flight at once (8 warps, two heads each in turn: 52 us at
+// 16,384 tokens)
+constexpr int kWarps = 16;
 constexpr int kFwdWarps = 4;  // forward: warps per CTA = heads per CTA (grid.y covers the heads)
 constexpr int kLd = kD + 8; // shared tile row, elements (272 bytes: conflict-free for both maps)
 constexpr int kTile = 16 * kLd;               // one warp's 16 x 128 tile, elements
@@ -336,7 +339,7 @@ qkv_fwd_kernel(const QkvFwdParams p) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kWarps * 32, 4)
+__global__ void __launch_bounds__(kWarps * 32, 2)
 qkv_bwd_kernel(const QkvBwdParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* cs = reinterpret_cast<float*>(smem);
