@@ -385,11 +385,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
               if (64 + c > lim) s1v[c] = __float_as_uint(-INFINITY);
             }
           }
+          // four independent max chains (16 steps each instead of one of 64); max is exact, so the
+          // result equals the single chain's
+          float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
           for (int c = 0; c < 64; c += 2) {
-            mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
-            mx = fmax3(mx, __uint_as_float(s1v[c]), __uint_as_float(s1v[c + 1]));
+            const int a2 = (c >> 1) & 1;
+            mq[a2] = fmax3(mq[a2], __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+            mq[2 + a2] = fmax3(mq[2 + a2], __uint_as_float(s1v[c]), __uint_as_float(s1v[c + 1]));
           }
+          mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
         }
         const float m_new = fmaxf(m_run, mx * p.scale_log2);
         const bool resc = m_new > m_run + 8.f;
