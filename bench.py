@@ -269,6 +269,13 @@ REF_BUDGET_S = 90.0  # the reference arm's timed steps, seconds
 # DRAM bytes (read + write) of the two attention kernels in one config-3 step (N = 1 packing), from
 # one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum; forward 68.1 + 15.6 MB, backward
 # 412.0 + 186.0 MB). Not measured by this run: the second field says which kernel build it describes.
+# the full step's attention pair, per step: 28 layers x (forward 81.2 + backward 370.4 MB), the
+# means of two layers each from one-pass ncu captures of a timed step at N = 1
+FULL_STEP_ATTN_DRAM_BYTES = {
+    "config5": (28 * (81.2e6 + 370.4e6),
+                "ncu captures (dram__bytes_read + write, one pass) of attn_fwd_sm100_kernel (83.3, 79.0 MB) and "
+                "attn_bwd_sm100_kernel (375.0, 365.9 MB) of two layers of a timed config-5 step at N=1, x 28 "
+                "layers; kernels as of commit c39bb33; not this run's")}
 ATTN_DRAM_BYTES = {"config3": (699.2e6, "ncu capture (dram__bytes_read + write) of attn_fwd_sm100_kernel "
                                         "(83.4 MB) and attn_bwd_sm100_kernel (615.8 MB), one launch each, "
                                         "kernels as of commit 4716b58; not this run's")}
@@ -693,7 +700,9 @@ def run_full_step(args, world, rank, local):
                    "parallelism": f"dp{world}"},
         "roofline": {"bound": "tensor", "kernel": "varlen attention fwd+bwd of the 28 layers (decik_varlen_attn_fwd/bwd)",
                      "achieved": round(attn_tflops, 2), "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
-                     "frac": round(attn_tflops / pk["bf16_tflops_sustained"], 4), "traffic": None,
+                     "frac": round(attn_tflops / pk["bf16_tflops_sustained"], 4),
+                     "traffic": FULL_STEP_ATTN_DRAM_BYTES.get(args.workload, (None, None))[0],
+                     "traffic_source": FULL_STEP_ATTN_DRAM_BYTES.get(args.workload, (None, None))[1],
                      "flops_per_step": 3.0 * f_fwd,
                      "peak_source": pk["source_sustained"]},
         "attn_tflops": round(attn_tflops, 2),
