@@ -70,8 +70,9 @@ template <> struct Cfg<EPI_QKV> {  // two heads per tile; a CTA pair holds one h
 };
 // EPI_F32 / EPI_STORE16 produce outputs of hidden = 1536 columns (dX, the down projection):
 // 256 x 192 pair tiles give 1536 / 192 = 8 column tiles, 512 tiles at 16,384 rows = 6.9 rounds of
-// 74 pairs, where 256 x 256 tiles leave the sixth round 19 % full (dX measured 646 us against
-// cuBLAS's 559 that way). B is K-major (the caller passes the transposed weight for dX).
+// 74 pairs, where 256 x 256 tiles leave the sixth round 19 % full (the block's dX: 126 us with
+// 256 x 256 tiles, 92-96 us with 256 x 192). B is K-major (the caller passes the transposed weight
+// for dX).
 template <> struct Cfg<EPI_F32> {
   static constexpr int BN = 192, STAGES = 5;
   static constexpr bool B_MN = false;
