@@ -37,17 +37,26 @@ from .nf4 import dequantize_nf4_many, supported
 class FusedMLP(torch.autograd.Function):
     """down(silu(gate(x)) * up(x)) with frozen dequantised weights: ``w_gu`` [2 * inter, hidden]
     (W_gate rows then W_up rows) and ``w_down`` [hidden, inter] in the compute dtype (the Qwen2 MLP
-    has no biases). Gradient only for x (returned in x's dtype)."""
+    has no biases). Gradient for x (returned in x's dtype).
+
+    With ``residual`` (the decoder layer's fp32 stream, x's shape) the node returns
+    residual + mlp(x) in fp32 from the down projection's GEMM (beta = 1, fp32 output): the layer's
+    residual add (solution/varlen.py:343) needs no pass of its own, and the MLP output is added
+    before any 16-bit rounding. The residual's gradient is the output's."""
 
     @staticmethod
-    def forward(ctx, x, w_gu, w_down):
+    def forward(ctx, x, w_gu, w_down, residual=None):
         inter = w_down.shape[1]
         shape = x.shape
         x16 = x.reshape(-1, shape[-1]).to(w_gu.dtype).contiguous()
         gu, hidden = ops.mlp_gate_up(x16, w_gu)            # [T, 2 * inter], [T, inter]
-        out = torch.mm(hidden, w_down.t())                 # [T, hidden], plain GEMM
+        if residual is None:
+            out = torch.mm(hidden, w_down.t())             # [T, hidden], plain GEMM
+        else:
+            out = torch.addmm(residual.reshape(-1, residual.shape[-1]), hidden, w_down.t(), out_dtype=torch.float32)
         ctx.save_for_backward(gu, w_gu, w_down)
         ctx.in_dtype, ctx.shape, ctx.inter = x.dtype, shape, inter
+        ctx.residual = residual is not None
         return out.view(*shape[:-1], out.shape[-1])
 
     @staticmethod
@@ -56,7 +65,7 @@ class FusedMLP(torch.autograd.Function):
         g16 = grad_out.reshape(-1, grad_out.shape[-1]).to(w_down.dtype).contiguous()
         dgu = ops.mlp_down_grad(g16, w_down, gu)           # [T, 2 * inter] = [dgate | dup]
         dx = torch.mm(dgu, w_gu, out_dtype=torch.float32)  # both input gradients summed in fp32
-        return dx.to(ctx.in_dtype).view(ctx.shape), None, None
+        return dx.to(ctx.in_dtype).view(ctx.shape), None, None, (grad_out if ctx.residual else None)
 
 
 def mlp_weights(gate_proj, up_proj, down_proj, dtype):
@@ -94,7 +103,8 @@ def patch(linear4bit_cls=None):
                 and not weight.requires_grad and bias is None
                 and supported(getattr(weight, "quant_state", None), n_in))
 
-    def forward(self, x):
+    def forward(self, x, residual=None):
+        # ``residual``: the patched decoder layer's fp32 stream; the result is then residual + mlp(x)
         config = getattr(self, "config", None)
         gate, up, down = (getattr(self, n, None) for n in ("gate_proj", "up_proj", "down_proj"))
         dtype = getattr(gate, "compute_dtype", None)
@@ -105,9 +115,13 @@ def patch(linear4bit_cls=None):
                 and gate.weight.quant_state.shape == up.weight.quant_state.shape
                 and nf4_projection(down, gate.weight.quant_state.shape[0], dtype)
                 and gate.weight.quant_state.shape[0] % 256 == 0 and x.shape[-1] % 8 == 0):
-            return original(self, x)
+            out = original(self, x)
+            return out if residual is None else residual + out
         w_gu, w_down = mlp_weights(gate, up, down, dtype)
-        return FusedMLP.apply(x, w_gu, w_down)
+        if residual is not None and not (residual.dtype == torch.float32 and residual.shape == x.shape
+                                         and residual.is_contiguous()):
+            return residual + FusedMLP.apply(x, w_gu, w_down)
+        return FusedMLP.apply(x, w_gu, w_down, residual)
 
     forward._skc = True
     cls.forward = forward

@@ -315,6 +315,8 @@ def _decoder_layer(original, fuse_residual, fuse_input_norm=True):
         else:
             mid = layer_in + attn
             normed = post_norm(mid)
+        if getattr(type(self.mlp).forward, "_skc", False):
+            return self.mlp(normed, residual=mid)  # the residual add inside the MLP's down projection
         return mid + self.mlp(normed)
 
     return forward

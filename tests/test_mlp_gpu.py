@@ -126,3 +126,32 @@ def test_fused_mlp_bf16_vs_unfused_chain(cuda_lib):
     for got, exp in ((out.float(), ref.float()), (x.grad, x2.grad)):
         rel = ((got - exp).norm() / exp.norm()).item()
         assert rel < 1e-2, rel
+
+
+def test_fused_mlp_with_residual(cuda_lib):
+    """The node with the decoder layer's residual (fp32): residual + mlp(x) from the down projection's
+    GEMM, against residual + the node's own 16-bit output (which rounds the MLP output first: within
+    that rounding), and the residual's gradient is the output's gradient, exactly."""
+    from decik_b200.solution.mlp import FusedMLP
+
+    g = torch.Generator(device=DEV).manual_seed(5)
+    T, H, inter = 700, 1536, 8960
+    dt = torch.bfloat16
+    x = torch.randn(T, H, device=DEV, generator=g)
+    res = torch.randn(T, H, device=DEV, generator=g) * 4.0
+    w_gu = (torch.randn(2 * inter, H, device=DEV, generator=g) * 0.02).to(dt)
+    w_down = (torch.randn(H, inter, device=DEV, generator=g) * 0.02).to(dt)
+    grad = torch.randn(T, H, device=DEV, generator=g)
+    xa, ra = x.clone().requires_grad_(True), res.clone().requires_grad_(True)
+    out = FusedMLP.apply(xa, w_gu, w_down, ra)
+    out.backward(grad)
+    xb = x.clone().requires_grad_(True)
+    out_b = res + FusedMLP.apply(xb, w_gu, w_down).float()
+    out_b.backward(grad)
+    assert out.dtype == torch.float32
+    d = (out - out_b).abs().max().item()
+    assert d <= 2.0 ** -8 * (out_b - res).abs().max().item() + 1e-6, d
+    assert torch.equal(ra.grad, grad)
+    rel = ((xa.grad - xb.grad).norm() / xb.grad.norm()).item()
+    assert rel < 1e-5, rel  # the same kernels on the same 16-bit gradient
+    assert cuda_lib.decik_kernel_error(1) == 0
