@@ -318,16 +318,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
     // buffer is released on the leader's barrier
     const uint32_t acc_empty_leader0 = PAIR ? map_to_rank(acc_empty(0), 0) : acc_empty(0);
     const uint32_t acc_empty_leader1 = PAIR ? map_to_rank(acc_empty(1), 0) : acc_empty(1);
+    // EPI_DSWIGLU: the forward's gate and up of the warp's 32 rows x 32 columns j.. come in by
+    // coalesced cp.async into a swizzled table ([gate | up][32 rows][64 B]); a chunk's table is
+    // issued one step ahead (the first chunk of a tile before its accumulator is ready) so the HBM
+    // latency overlaps the previous chunk's work
+    uint8_t* gu_tab = smem + L::OFF_TAB + ew * L::TAB_WARP;
+    const auto load_gu = [&](int64_t row_base, int j) {
+      const T* gu = static_cast<const T*>(p.gu);
+#pragma unroll
+      for (int i2 = 0; i2 < 8; ++i2) {
+        const int piece = lane + 32 * i2;
+        const int which = piece >> 7, row = (piece >> 2) & 31, c4 = piece & 3;
+        const int64_t rr = row_base + row < p.M ? row_base + row : p.M - 1;
+        const T* src = gu + rr * p.ld_gu + (which ? p.inter : 0) + j + 8 * c4;
+        ptx::cp_async16(ptx::smem_u32(gu_tab + which * 2048 + row * 64 + ((c4 ^ ((row >> 1) & 3)) << 4)), src, true);
+      }
+      ptx::cp_async_commit();
+    };
     for (int tile = unit; tile < p.n_tiles; tile += n_units, ++i) {
       const int m0 = (tile / p.n_tiles_n) * TM + static_cast<int>(rank) * BM, n0 = (tile % p.n_tiles_n) * BN;
       const int b = i & 1;
+      const int64_t row0 = m0 + 32 * q4;
+      if constexpr (EPI == EPI_DSWIGLU) load_gu(row0, n0 + wg * (BN / 2));
       bool ok = mbar_wait(acc_full(b), (i >> 1) & 1, p.err, 321);
       // EPI_QKV: the eight epilogue warps leave together (they meet at named barriers below)
       if constexpr (EPI == EPI_QKV) ok = named_bar_and(1, 256, ok);
-      if (!ok) break;
+      if (!ok) {
+        if constexpr (EPI == EPI_DSWIGLU) ptx::cp_async_wait<0>();  // no copy may land after the CTA leaves
+        break;
+      }
       tc_fence_after();
       const uint32_t tacc = tmem + lane_base + b * 256;
-      const int64_t row0 = m0 + 32 * q4;
       const int64_t r = row0 + lane;
       if constexpr (EPI == EPI_F32) {
 #pragma unroll 1
@@ -416,26 +437,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
         }
       } else if constexpr (EPI == EPI_DSWIGLU) {
         // accumulator = grad_hidden for j in [n0, n0 + 256); warpgroup wg takes [128 wg, 128 wg + 128)
-        // in chunks of 32; the forward's gate and up for the warp's rows come in by coalesced
-        // cp.async (32 rows x 32 columns each); dgate and dup leave through two 2 KB tiles
-        // (double-buffered)
-        uint8_t* tab = smem + L::OFF_TAB + ew * L::TAB_WARP;  // [gate | up][32 rows][64 B], swizzled
-        const T* gu = static_cast<const T*>(p.gu);
-        const auto load_gu = [&](int j) {
-#pragma unroll
-          for (int i2 = 0; i2 < 8; ++i2) {
-            const int piece = lane + 32 * i2;
-            const int which = piece >> 7, row = (piece >> 2) & 31, c4 = piece & 3;
-            const int64_t rr = row0 + row < p.M ? row0 + row : p.M - 1;
-            const T* src = gu + rr * p.ld_gu + (which ? p.inter : 0) + j + 8 * c4;
-            ptx::cp_async16(ptx::smem_u32(tab + which * 2048 + row * 64 + ((c4 ^ ((row >> 1) & 3)) << 4)), src, true);
-          }
-          ptx::cp_async_commit();
-        };
+        // in chunks of 32 (the gate / up table of the first one was issued before the accumulator
+        // was ready); dgate and dup leave through two 2 KB tiles (double-buffered)
+        uint8_t* tab = gu_tab;
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32, ++n_chunks) {
           const int jl = wg * (BN / 2) + c;
-          load_gu(n0 + jl);
           uint32_t gr[32];
           tmem_ld32(tacc + jl, gr);
           tmem_ld_wait();
@@ -448,7 +455,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
             unpack8<T>(*reinterpret_cast<const uint4*>(tab + off), *reinterpret_cast<float(*)[8]>(&gv[8 * j4]));
             unpack8<T>(*reinterpret_cast<const uint4*>(tab + 2048 + off), *reinterpret_cast<float(*)[8]>(&uv[8 * j4]));
           }
-          __syncwarp();  // the table is refilled by the next chunk
+          __syncwarp();  // the table is in registers: the next chunk's may come in
+          if (c + 32 < BN / 2) load_gu(row0, n0 + jl + 32);
           uint32_t dg[32], du[32];
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
