@@ -146,6 +146,118 @@ add_rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ g
 }
 
 }  // namespace
+// The same four kernels for rows of NC * 128 columns (NC a compile-time count): the lane keeps its
+// NC 16-byte pieces of each row in registers between the reduction and the output pass instead
+// of reading them again. Same per-element and per-row arithmetic in the same order as the loops
+// above, so the outputs are equal bit for bit.
+template <typename W, int NC>
+__global__ void __launch_bounds__(256)
+rmsnorm_fwd_reg_kernel(const float* __restrict__ x, const W* __restrict__ w, float* __restrict__ y,
+                       float* __restrict__ rstd_out, int64_t n_rows, int64_t sx, int64_t sy, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
+  const float* xr = x + row * sx;
+  float4 v[NC];
+#pragma unroll
+  for (int j = 0; j < NC; ++j) v[j] = __ldg(reinterpret_cast<const float4*>(xr + lane * 4 + 128 * j));
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < NC; ++j) acc += sumsq4(v[j]);
+  const float rstd = norm::row_rstd(acc, NC * 128, eps);
+  float* yr = y + row * sy;
+#pragma unroll
+  for (int j = 0; j < NC; ++j)
+    *reinterpret_cast<float4*>(yr + lane * 4 + 128 * j) = norm_out4<W>(v[j], w, lane * 4 + 128 * j, rstd);
+  if (rstd_out != nullptr && lane == 0) rstd_out[row] = rstd;
+}
+
+template <typename W, int NC>
+__global__ void __launch_bounds__(256)
+rmsnorm_bwd_reg_kernel(const float* __restrict__ dy, const float* __restrict__ x, const W* __restrict__ w,
+                       const float* __restrict__ rstd_in, float* __restrict__ dx, int64_t n_rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
+  const int64_t off = row * (NC * 128);
+  const float rstd = rstd_in[row];
+  float4 g[NC], v[NC];
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    g[j] = __ldg(reinterpret_cast<const float4*>(dy + off + lane * 4 + 128 * j));
+    v[j] = __ldg(reinterpret_cast<const float4*>(x + off + lane * 4 + 128 * j));
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < NC; ++j) acc += wdot4<W>(g[j], v[j], w, lane * 4 + 128 * j);
+  const float dot = warp_sum(acc) / static_cast<float>(NC * 128);
+  const float k = rstd * rstd * dot;
+#pragma unroll
+  for (int j = 0; j < NC; ++j)
+    *reinterpret_cast<float4*>(dx + off + lane * 4 + 128 * j) = norm_grad4<W>(g[j], v[j], w, lane * 4 + 128 * j, rstd, k);
+}
+
+template <typename W, typename D, int NC>
+__global__ void __launch_bounds__(256)
+add_rmsnorm_fwd_reg_kernel(const float* __restrict__ residual, const D* __restrict__ delta, const W* __restrict__ w,
+                           float* __restrict__ h, float* __restrict__ y, float* __restrict__ rstd_out, int64_t n_rows,
+                           float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
+  const int64_t off = row * (NC * 128);
+  float4 v[NC];
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    const int c = lane * 4 + 128 * j;
+    v[j] = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    *reinterpret_cast<float4*>(h + off + lane * 4 + 128 * j) = v[j];
+    acc += sumsq4(v[j]);
+  }
+  const float rstd = norm::row_rstd(acc, NC * 128, eps);
+#pragma unroll
+  for (int j = 0; j < NC; ++j)
+    *reinterpret_cast<float4*>(y + off + lane * 4 + 128 * j) = norm_out4<W>(v[j], w, lane * 4 + 128 * j, rstd);
+  if (rstd_out != nullptr && lane == 0) rstd_out[row] = rstd;
+}
+
+template <typename W, typename D, int NC>
+__global__ void __launch_bounds__(256)
+add_rmsnorm_bwd_reg_kernel(const float* __restrict__ dy, const float* __restrict__ grad_h,
+                           const float* __restrict__ residual, const D* __restrict__ delta, const W* __restrict__ w,
+                           const float* __restrict__ rstd_in, float* __restrict__ dx, D* __restrict__ dx16,
+                           int64_t n_rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n_rows) return;
+  const int64_t off = row * (NC * 128);
+  const float rstd = rstd_in[row];
+  float4 g[NC], v[NC];
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    const int c = lane * 4 + 128 * j;
+    v[j] = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
+    g[j] = __ldg(reinterpret_cast<const float4*>(dy + off + c));
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < NC; ++j) acc += wdot4<W>(g[j], v[j], w, lane * 4 + 128 * j);
+  const float dot = warp_sum(acc) / static_cast<float>(NC * 128);
+  const float k = rstd * rstd * dot;
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    const int c = lane * 4 + 128 * j;
+    float4 o = norm_grad4<W>(g[j], v[j], w, c, rstd, k);
+    if (grad_h != nullptr) o = add4(__ldg(reinterpret_cast<const float4*>(grad_h + off + c)), o);
+    *reinterpret_cast<float4*>(dx + off + c) = o;
+    if (dx16 != nullptr) dstore4<D>(dx16 + off + c, o);
+  }
+}
+
 }  // namespace decik
 
 extern "C" int decik_rmsnorm_fwd(const float* x, const void* w, int w_dtype, float* y, float* rstd,
@@ -158,12 +270,18 @@ extern "C" int decik_rmsnorm_fwd(const float* x, const void* w, int w_dtype, flo
   if (!x || !w || !y) return set_error(DECIK_ERR_INVALID, "rmsnorm_fwd: null pointer");
   if (!aligned16(x) || !aligned16(y)) return set_error(DECIK_ERR_INVALID, "rmsnorm_fwd: x, y must be 16-byte aligned");
   const int grid = static_cast<int>((n_rows + 7) / 8);
-  if (w_dtype == DECIK_F32)
-    rmsnorm_fwd_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(x, static_cast<const float*>(w), y, rstd, n_rows, n_cols, stride_x, stride_y, eps);
-  else if (w_dtype == DECIK_F16)
-    rmsnorm_fwd_kernel<__half><<<grid, 256, 0, as_stream(stream)>>>(x, static_cast<const __half*>(w), y, rstd, n_rows, n_cols, stride_x, stride_y, eps);
-  else
+  const cudaStream_t st = as_stream(stream);
+  if (w_dtype != DECIK_F32 && w_dtype != DECIK_F16)
     return set_error(DECIK_ERR_INVALID, "rmsnorm_fwd: w_dtype must be F32 or F16");
+  const bool wf = w_dtype == DECIK_F32;
+  if (n_cols == 12 * 128) {  // the 1.5B hidden size: the row stays in registers
+    if (wf) rmsnorm_fwd_reg_kernel<float, 12><<<grid, 256, 0, st>>>(x, static_cast<const float*>(w), y, rstd, n_rows, stride_x, stride_y, eps);
+    else rmsnorm_fwd_reg_kernel<__half, 12><<<grid, 256, 0, st>>>(x, static_cast<const __half*>(w), y, rstd, n_rows, stride_x, stride_y, eps);
+  } else if (wf) {
+    rmsnorm_fwd_kernel<float><<<grid, 256, 0, st>>>(x, static_cast<const float*>(w), y, rstd, n_rows, n_cols, stride_x, stride_y, eps);
+  } else {
+    rmsnorm_fwd_kernel<__half><<<grid, 256, 0, st>>>(x, static_cast<const __half*>(w), y, rstd, n_rows, n_cols, stride_x, stride_y, eps);
+  }
   return check_launch("rmsnorm_fwd");
 }
 
@@ -178,12 +296,18 @@ extern "C" int decik_rmsnorm_bwd(const float* dy, const float* x, const void* w,
   if (!aligned16(dy) || !aligned16(x) || !aligned16(dx))
     return set_error(DECIK_ERR_INVALID, "rmsnorm_bwd: dy, x, dx must be 16-byte aligned");
   const int grid = static_cast<int>((n_rows + 7) / 8);
-  if (w_dtype == DECIK_F32)
-    rmsnorm_bwd_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(dy, x, static_cast<const float*>(w), rstd, dx, n_rows, n_cols);
-  else if (w_dtype == DECIK_F16)
-    rmsnorm_bwd_kernel<__half><<<grid, 256, 0, as_stream(stream)>>>(dy, x, static_cast<const __half*>(w), rstd, dx, n_rows, n_cols);
-  else
+  const cudaStream_t st = as_stream(stream);
+  if (w_dtype != DECIK_F32 && w_dtype != DECIK_F16)
     return set_error(DECIK_ERR_INVALID, "rmsnorm_bwd: w_dtype must be F32 or F16");
+  const bool wf = w_dtype == DECIK_F32;
+  if (n_cols == 12 * 128) {
+    if (wf) rmsnorm_bwd_reg_kernel<float, 12><<<grid, 256, 0, st>>>(dy, x, static_cast<const float*>(w), rstd, dx, n_rows);
+    else rmsnorm_bwd_reg_kernel<__half, 12><<<grid, 256, 0, st>>>(dy, x, static_cast<const __half*>(w), rstd, dx, n_rows);
+  } else if (wf) {
+    rmsnorm_bwd_kernel<float><<<grid, 256, 0, st>>>(dy, x, static_cast<const float*>(w), rstd, dx, n_rows, n_cols);
+  } else {
+    rmsnorm_bwd_kernel<__half><<<grid, 256, 0, st>>>(dy, x, static_cast<const __half*>(w), rstd, dx, n_rows, n_cols);
+  }
   return check_launch("rmsnorm_bwd");
 }
 
@@ -207,15 +331,24 @@ int add_rmsnorm_check(int64_t n_rows, int n_cols, const void* delta, int d_dtype
 template <typename W, typename D>
 void launch_add_fwd(const float* residual, const void* delta, const void* w, float* h, float* y, float* rstd,
                     int64_t n_rows, int n_cols, float eps, cudaStream_t st) {
-  add_rmsnorm_fwd_kernel<W, D><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
-      residual, static_cast<const D*>(delta), static_cast<const W*>(w), h, y, rstd, n_rows, n_cols, eps);
+  if (n_cols == 12 * 128)
+    add_rmsnorm_fwd_reg_kernel<W, D, 12><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+        residual, static_cast<const D*>(delta), static_cast<const W*>(w), h, y, rstd, n_rows, eps);
+  else
+    add_rmsnorm_fwd_kernel<W, D><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+        residual, static_cast<const D*>(delta), static_cast<const W*>(w), h, y, rstd, n_rows, n_cols, eps);
 }
 template <typename W, typename D>
 void launch_add_bwd(const float* dy, const float* grad_h, const float* residual, const void* delta, const void* w,
                     const float* rstd, float* dx, void* dx16, int64_t n_rows, int n_cols, cudaStream_t st) {
-  add_rmsnorm_bwd_kernel<W, D><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
-      dy, grad_h, residual, static_cast<const D*>(delta), static_cast<const W*>(w), rstd, dx, static_cast<D*>(dx16),
-      n_rows, n_cols);
+  if (n_cols == 12 * 128)
+    add_rmsnorm_bwd_reg_kernel<W, D, 12><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+        dy, grad_h, residual, static_cast<const D*>(delta), static_cast<const W*>(w), rstd, dx, static_cast<D*>(dx16),
+        n_rows);
+  else
+    add_rmsnorm_bwd_kernel<W, D><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+        dy, grad_h, residual, static_cast<const D*>(delta), static_cast<const W*>(w), rstd, dx, static_cast<D*>(dx16),
+        n_rows, n_cols);
 }
 
 }  // namespace
