@@ -349,7 +349,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
       }
       tc_fence_after();
       const uint32_t tacc = tmem + lane_base + b * 256;
-      const int64_t r = row0 + lane;
       if constexpr (EPI == EPI_F32) {
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32, ++n_chunks) {
