@@ -141,6 +141,19 @@ struct Params {
   int* err;
 };
 
+// Tile t -> (row block, column block). Tiles go in groups of kGroupRows row blocks, row block
+// fastest within a group: the tiles resident at a time share a few row blocks of A and a few column
+// blocks of B, so both stay in L2 while the output streams through it (column block fastest over
+// all rows re-read B from HBM once the output had pushed it out of L2).
+constexpr int kGroupRows = 16;
+__device__ __forceinline__ void tile_coords(int tile, int n_tiles_n, int m_tiles, int& mt, int& nt) {
+  const int per_group = kGroupRows * n_tiles_n;
+  const int g = tile / per_group, r = tile % per_group;
+  const int rows = min(kGroupRows, m_tiles - g * kGroupRows);
+  mt = g * kGroupRows + r % rows;
+  nt = r / rows;
+}
+
 template <typename T>
 __device__ __forceinline__ float rnd(float x) {
   return Dt<T>::to_f(Dt<T>::from_f(x));
@@ -221,9 +234,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
       bool ok = true;
       for (int tile = unit; tile < p.n_tiles && ok; tile += n_units) {
         // this CTA's A rows and B rows (columns of an MN-major B) of the tile
-        const int m0 = (tile / p.n_tiles_n) * TM + static_cast<int>(rank) * BM;
-        const int n0 = PAIR ? (tile % p.n_tiles_n) * p.b_tile_step + static_cast<int>(rank) * p.b_rank_off
-                            : (tile % p.n_tiles_n) * BN;
+        int mt, nt;
+        tile_coords(tile, p.n_tiles_n, p.n_tiles / p.n_tiles_n, mt, nt);
+        const int m0 = mt * TM + static_cast<int>(rank) * BM;
+        const int n0 = PAIR ? nt * p.b_tile_step + static_cast<int>(rank) * p.b_rank_off : nt * BN;
         for (int kb = 0; kb < nkt; ++kb, ++it) {
           const int s = static_cast<int>(it % S);
           if (it >= static_cast<uint32_t>(S) && !(ok = mbar_wait(empty(s), ((it / S) - 1) & 1, p.err, 301))) break;
@@ -336,7 +350,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
       ptx::cp_async_commit();
     };
     for (int tile = unit; tile < p.n_tiles; tile += n_units, ++i) {
-      const int m0 = (tile / p.n_tiles_n) * TM + static_cast<int>(rank) * BM, n0 = (tile % p.n_tiles_n) * BN;
+      int mt, nt;
+      tile_coords(tile, p.n_tiles_n, p.n_tiles / p.n_tiles_n, mt, nt);
+      const int m0 = mt * TM + static_cast<int>(rank) * BM, n0 = nt * BN;
       const int b = i & 1;
       const int64_t row0 = m0 + 32 * q4;
       if constexpr (EPI == EPI_DSWIGLU) load_gu(row0, n0 + wg * (BN / 2));
@@ -397,7 +413,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
         // warpgroup wg takes j in [64 wg, 64 wg + 64) in chunks of 32: gate and up rounded to T (the
         // values the separate SwiGLU kernel reads back), h = silu(gate) * up from them; gate, up
         // and h leave through three 2 KB staging tiles (double-buffered: 2 x 6 KB per warp)
-        const int j0 = (tile % p.n_tiles_n) * (BN / 2);
+        const int j0 = nt * (BN / 2);
 #pragma unroll 1
         for (int c = 0; c < BN / 4; c += 32, ++n_chunks) {
           const int jl = wg * (BN / 4) + c;
