@@ -6,22 +6,26 @@
 // CTA = one 128-key block of one row x one kv head x one subset of the group's query heads. It
 // loops over its query heads and the 128-query blocks at or below the diagonal. Per iteration
 // (S^T etc. are key-major; every MMA is M=128 N=128, kind::f16):
-//   S^T  = K Q^T      SS              -> TMEM S
-//   dP^T = V dO^T     SS              -> TMEM dP/P/dQ
-//   softmax warps: P^T = exp2(S^T*scale*log2e - lse*log2e) -> TMEM (16-bit, over dP^T columns the
-//                  same warpgroup has read), dS^T = P^T (dP^T - delta) -> shared memory
+//   S^T  = K Q^T      SS              -> TMEM S/P
+//   dP^T = V dO^T     SS              -> TMEM dP/dQ
+//   softmax warps, in two phases:
+//     P phase:  P^T = exp2(S^T*scale*log2e - lse*log2e) -> TMEM (operand type, over S^T columns the
+//               same warpgroup has read; an f16 copy stays in registers)
+//     dS phase: dS^T = P^T (dP^T - delta) -> shared memory
 //   dV  += P^T dO     TS (A = P^T in TMEM)
 //   dK  += dS^T Q     SS (A = dS^T, K-major)
-//   dQ   = dS K       SS (A = the same dS^T tile read MN-major)  -> TMEM dP/P/dQ after dV
+//   dQ   = dS K       SS (A = the same dS^T tile read MN-major)  -> TMEM dP/dQ
 //   dQ warps: read dQ out of TMEM at once (freeing the columns for the next dP^T), then stream it as
 //   16-column fp32 chunks through two staging buffers (64-byte swizzle) into the fp32 dq
 //   accumulator by TMA bulk reduce-add, concurrently with the next softmax.
-// TMEM (512 columns): dK [0,128) dV [128,256) dP^T/P^T/dQ [256,384) S^T [384,512). The softmax
-// warpgroups take interleaved 32-query blocks (w and w + 2), so each writes P^T only over dP^T
-// columns it has itself read. Issue order per iteration i: S(i+1) as soon as both warpgroups have
-// loaded S^T(i) (it runs under their softmax), dV(i), dQ(i), dP(i+1), dK(i). dQ(i) overwrites P^T(i)
-// after dV(i) in issue order (tcgen05 MMAs of one thread execute in order); dP(i+1) waits until
-// the dQ warps read dQ(i) out; dK(i) runs under the next softmax.
+// TMEM (512 columns): dK [0,128) dV [128,256) dP^T/dQ [256,384) S^T/P^T [384,512). The softmax
+// warpgroups take interleaved 32-query blocks (w and w + 2), so each writes P^T only over S^T
+// columns it has itself read. Issue order per iteration i: dV(i) and S(i+1) once P^T(i) is written
+// (S(i+1) overwrites P^T(i) after dV(i) in issue order: tcgen05 MMAs of one thread execute in
+// order; both run under the dS phase of i), dQ(i) and dK(i) once dS^T(i) is written, dP(i+1) once
+// the dQ warps read dQ(i) out. The P phase of i+1 needs only S(i+1), so it runs while dQ(i) is
+// computed and read out and dP(i+1) is computed. What then sets the period is the dQ warps'
+// stream of fp32 reduce-adds (64 KB per iteration), not the softmax.
 // With more than one head subset per key block, dK / dV go to fp32 accumulators by TMA reduce-add
 // (the caller casts them); with one, they are written directly. Launch order: key block 0 of every
 // row first (the longest CTAs), or, when the dq accumulator is far larger than L2, the key blocks
@@ -58,7 +62,7 @@ constexpr int OFF_DO = 4 * TILE, OFF_DS = 5 * TILE;       // dO (one stage), dS^
 constexpr int OFF_STG = 6 * TILE;                          // dQ staging: two chunk buffers
 constexpr int OFF_STAT = OFF_STG + 2 * CHUNK;              // [2][-lse*log2e 128 | -delta 128] fp32
 constexpr int OFF_BAR = OFF_STAT + 2 * 2 * BM * 4;
-enum { B_KV = 0, B_QF, B_QF1, B_QE, B_QE1, B_DOF, B_DOE, B_SF, B_SREAD, B_DPF, B_PF, B_DSF, B_DSFREE, B_DQF,
+enum { B_KV = 0, B_QF, B_QF1, B_QE, B_QE1, B_DOF, B_DOE, B_SF, B_DPF, B_PF, B_DSF, B_DSFREE, B_DQF,
        B_DQFREE, B_DONE, N_BAR };
 constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
 constexpr int kSmem = OFF_TMEM + 16 + 1024;
@@ -146,6 +150,12 @@ template <typename T>
 __device__ __forceinline__ uint32_t pk2(float lo, float hi);
 template <> __device__ __forceinline__ uint32_t pk2<__nv_bfloat16>(float lo, float hi) { return pack_bf16x2(lo, hi); }
 template <> __device__ __forceinline__ uint32_t pk2<__half>(float lo, float hi) { return pack_f16x2(lo, hi); }
+// the two values of an f16 pair as fp32 (exact)
+__device__ __forceinline__ void unpk2(uint32_t v, float& lo, float& hi) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v));
+  lo = f.x;
+  hi = f.y;
+}
 
 // Row `r` (64 bytes: 16 fp32) of a [128 x 16] staging chunk laid out with the TMA 64-byte swizzle:
 // 16-byte unit j of row r sits at unit j ^ ((r >> 1) & 3).
@@ -192,7 +202,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
     mbar_init(bar(B_DOF), 1);
     mbar_init(bar(B_DOE), 1);
     mbar_init(bar(B_SF), 1);
-    mbar_init(bar(B_SREAD), 256);
     mbar_init(bar(B_DPF), 1);
     mbar_init(bar(B_PF), 256);
     mbar_init(bar(B_DSF), 256);
@@ -286,7 +295,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
     }
   } else if (warp == 13) {
     // ---------------------------------------------------------------- MMA issue (one thread)
-    // Per iteration: S(it+1) (under the softmax of it), dV(it), dQ(it), dP(it+1), dK(it).
+    // Per iteration: dV(it) and S(it+1) once P^T(it) is in TMEM (they run under the dS phase of
+    // it), then dQ(it) and dK(it) once dS^T(it) is in shared memory, then dP(it+1) once the dQ warps
+    // read dQ(it) out (it runs under the P phase of it+1).
     if (lane == 0) {
       constexpr int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t id_kk = idesc_f16(ab, 128, 128, 0, 0);  // S^T, dP^T
@@ -312,28 +323,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       }
       for (int it = 0; it < n_iter && ok; ++it) {
         const int s = it & 1;
+        // dV += P^T dO once the softmax wrote P^T(it) (over the S^T columns); frees dO
+        ok = mbar_wait(bar(B_PF), it & 1, p.err, 504);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(tmem + T_DV, tmem + T_SP, dOm, id_km, it > 0);
+        umma_commit(bar(B_DOE));
         if (it + 1 < n_iter) {
-          // S^T(it+1) once the softmax loaded S^T(it): runs under the softmax of it
-          ok = mbar_wait(bar(B_SREAD), it & 1, p.err, 510) &&
-               mbar_wait(bar(B_QF + (s ^ 1)), ((it + 1) >> 1) & 1, p.err, 506);
+          // S^T(it+1) over P^T(it): after dV(it) in issue order (tcgen05 MMAs of one thread execute
+          // in order)
+          ok = mbar_wait(bar(B_QF + (s ^ 1)), ((it + 1) >> 1) & 1, p.err, 506);
           if (!ok) break;
           tc_fence_after();
           issue_ss_kk(tmem + T_SP, dKk, dQk0 + (s ^ 1) * kStage, id_kk, false);
           umma_commit(bar(B_SF));
         }
-        // dV += P^T dO once the softmax wrote P^T(it) (over the dP^T columns); frees dO
-        ok = mbar_wait(bar(B_PF), it & 1, p.err, 504);
-        if (!ok) break;
-        tc_fence_after();
-        issue_pv(tmem + T_DV, tmem + T_DPQ, dOm, id_km, it > 0);
-        umma_commit(bar(B_DOE));
-        // dQ(it) = dS K over the dP^T / P^T columns: after dV(it) in issue order, and the softmax read
-        // dP^T(it) before it wrote dS
+        // dQ(it) = dS K over the dP^T columns, which the softmax read before it wrote dS
         ok = mbar_wait(bar(B_DSF), it & 1, p.err, 505);
         if (!ok) break;
         tc_fence_after();
         issue_ss_mm(tmem + T_DPQ, dSm, dKm, id_mm, false);
         umma_commit(bar(B_DQF));
+        // dK += dS^T Q(it), while the dQ warps read dQ(it) out; frees dS^T and the Q stage
+        issue_ss_km(tmem + T_DK, dSk, dQm0 + s * kStage, id_km, it > 0);
+        umma_commit(bar(B_DSFREE));
+        umma_commit(bar(B_QE + s));
         if (it + 1 < n_iter) {
           // dP^T(it+1) once dO(it+1) landed and the dQ warps read dQ(it) out
           ok = mbar_wait(bar(B_DOF), (it + 1) & 1, p.err, 507) && mbar_wait(bar(B_DQFREE), it & 1, p.err, 508);
@@ -342,10 +356,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
           issue_ss_kk(tmem + T_DPQ, dVk, dOk, id_kk, false);
           umma_commit(bar(B_DPF));
         }
-        // dK += dS^T Q(it) (runs under the next softmax); frees dS^T and the Q stage
-        issue_ss_km(tmem + T_DK, dSk, dQm0 + s * kStage, id_km, it > 0);
-        umma_commit(bar(B_DSFREE));
-        umma_commit(bar(B_QE + s));
       }
       umma_commit(bar(B_DONE));
       mbar_wait(bar(B_DONE), 0, p.err, 509);
@@ -404,39 +414,38 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
       return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, p.err, code));
     };
 
+    const float sc = p.scale_log2;
     for (int it = 0; it < n_iter; ++it) {
       const int s = it & 1;
       const int m0 = it_m0(it);
       if (!ok) continue;
-      ok = wait_w(B_SF, it & 1, 602) && wait_w(B_DPF, it & 1, 603) && wait_w(B_QF + s, (it >> 1) & 1, 604);
+      const float* st = stat + s * 2 * BM;
+      // P phase: P^T = exp2(S^T * scale * log2e - lse * log2e), written in the operand type over
+      // S^T columns this warpgroup has read (dV(it) reads it from there, then S^T(it+1) overwrites
+      // it). P stays in registers for the dS phase as f16 pairs: P <= 1, and f16's 11-bit
+      // significand keeps dS as accurate as with fp32 P (bf16 pairs raised dQ's error by a fifth)
+      ok = wait_w(B_SF, it & 1, 602) && wait_w(B_QF + s, (it >> 1) & 1, 604);
       if (!ok) continue;
       tc_fence_after();
-      const float* st = stat + s * 2 * BM;
-#pragma unroll 1
-      for (int h2 = 0; h2 < 2 && ok; ++h2) {
+      uint32_t pp[2][16];
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
         const int blk = 2 * h2 + wg;       // 32-query block of this pass: warpgroup w takes w, w + 2
         const int c0 = 32 * blk;           // its first query column
-        uint32_t sv[32], dp[32];
+        uint32_t sv[32];
         tmem_ld32(tmem + lane_off + T_SP + c0, sv);
-        tmem_ld32(tmem + lane_off + T_DPQ + c0, dp);
         tmem_ld_wait();
-        if (h2 == 1) {  // both blocks of S^T(it) are in registers: S^T(it+1) may overwrite them
-          tc_fence_before();
-          mbar_arrive(bar(B_SREAD));
-        }
-        const float4* nl4 = reinterpret_cast<const float4*>(st + c0);       // -lse * log2e
-        const float4* nd4 = reinterpret_cast<const float4*>(st + BM + c0);  // -delta
+        const float4* nl4 = reinterpret_cast<const float4*>(st + c0);  // -lse * log2e
         // visible query columns of this key: q >= key (causal) and q < L (row end)
         const int qlo = key - m0 - c0;
         const int qhi = (key < L ? min(BM, L - m0) : 0) - c0;
         const bool masked = qlo > 0 || qhi < 32;
-        uint32_t pp[16], dd[16];
-        const float sc = p.scale_log2;
+        const uint32_t p_tm = tmem + lane_off + T_SP + p_col(blk);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {  // 4 query columns per step
-          const float4 nl = nl4[c], nd = nd4[c];
-          const float nls[4] = {nl.x, nl.y, nl.z, nl.w}, nds[4] = {nd.x, nd.y, nd.z, nd.w};
-          float e[4], g[4];
+          const float4 nl = nl4[c];
+          const float nls[4] = {nl.x, nl.y, nl.z, nl.w};
+          float e[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) e[i] = ptx::ex2(fmaf(__uint_as_float(sv[4 * c + i]), sc, nls[i]));
           if (masked) {
@@ -444,18 +453,44 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
             for (int i = 0; i < 4; ++i)
               if (4 * c + i < qlo || 4 * c + i >= qhi) e[i] = 0.f;
           }
+          pp[h2][2 * c] = pack_f16x2(e[0], e[1]);
+          pp[h2][2 * c + 1] = pack_f16x2(e[2], e[3]);
+          // the operand copy two columns at a time (a 16-column store would need 16 more live
+          // registers and spills at this warpgroup's register budget)
+          if constexpr (!std::is_same<T, __half>::value)
+            tmem_st2(p_tm + 2 * c, pk2<T>(e[0], e[1]), pk2<T>(e[2], e[3]));
+        }
+        if constexpr (std::is_same<T, __half>::value) tmem_st16(p_tm, pp[h2]);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar(B_PF));
+      // dS phase: dS^T = P^T (dP^T - delta) into shared memory, once dQ(it - 1) / dK(it - 1) have
+      // read the previous dS^T
+      ok = wait_w(B_DPF, it & 1, 603) && (it == 0 || wait_w(B_DSFREE, (it - 1) & 1, 605));
+      if (!ok) continue;
+      tc_fence_after();
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int blk = 2 * h2 + wg;
+        const int c0 = 32 * blk;
+        uint32_t dp[32];
+        tmem_ld32(tmem + lane_off + T_DPQ + c0, dp);
+        tmem_ld_wait();
+        const float4* nd4 = reinterpret_cast<const float4*>(st + BM + c0);  // -delta
+        uint32_t dd[16];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 nd = nd4[c];
+          const float nds[4] = {nd.x, nd.y, nd.z, nd.w};
+          float e[4], g[4];
+          unpk2(pp[h2][2 * c], e[0], e[1]);
+          unpk2(pp[h2][2 * c + 1], e[2], e[3]);
 #pragma unroll
           for (int i = 0; i < 4; ++i) g[i] = e[i] * (__uint_as_float(dp[4 * c + i]) + nds[i]);
-          pp[2 * c] = pk2<T>(e[0], e[1]);
-          pp[2 * c + 1] = pk2<T>(e[2], e[3]);
           dd[2 * c] = pk2<T>(g[0], g[1]);
           dd[2 * c + 1] = pk2<T>(g[2], g[3]);
         }
-        // P^T over dP^T columns this warpgroup has already read
-        tmem_st16(tmem + lane_off + T_DPQ + p_col(blk), pp);
-        // dS^T into shared memory once dQ(it - 1) / dK(it - 1) have read the previous one
-        if (h2 == 0 && it > 0) ok = wait_w(B_DSFREE, (it - 1) & 1, 605);
-        if (!ok) break;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {  // 16-byte unit of this key's row in its 64-query half, 128B-swizzled
           const int unit = 4 * (blk & 1) + c;
@@ -463,11 +498,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_sm100_kernel(const __gri
               make_uint4(dd[4 * c], dd[4 * c + 1], dd[4 * c + 2], dd[4 * c + 3]);
         }
       }
-      if (!ok) continue;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(bar(B_PF));
       mbar_arrive(bar(B_DSF));
     }
     // epilogue: warpgroup 0 takes the dV rows, warpgroup 1 the dK rows (x scale); every thread of
