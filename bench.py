@@ -266,19 +266,18 @@ def cpu_reference_steps(lengths, n_steps: int, sample_tokens: int, seed: int = 0
 
 REF_BUDGET_S = 90.0  # the reference arm's timed steps, seconds
 
-# DRAM bytes (read + write) of the two attention kernels in one config-3 step (N = 1 packing), from
-# one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum; forward 68.1 + 15.6 MB, backward
-# 412.0 + 186.0 MB). Not measured by this run: the second field says which kernel build it describes.
-# the full step's attention pair, per step: 28 layers x (forward 81.2 + backward 370.4 MB), the
-# means of two layers each from one-pass ncu captures of a timed step at N = 1
+# DRAM bytes (read + write) of the two attention kernels per step, from one-pass ncu captures
+# (dram__bytes_read.sum + dram__bytes_write.sum). Not measured by this run: the second field says
+# which kernel build they describe. config3: one block step (N = 1 packing), forward 68.1 + 14.5 MB,
+# backward 432.4 + 181.3 MB. config5: 28 layers x the means of two layers of a timed step at N = 1.
 FULL_STEP_ATTN_DRAM_BYTES = {
-    "config5": (28 * (81.2e6 + 370.4e6),
-                "ncu captures (dram__bytes_read + write, one pass) of attn_fwd_sm100_kernel (83.3, 79.0 MB) and "
-                "attn_bwd_sm100_kernel (375.0, 365.9 MB) of two layers of a timed config-5 step at N=1, x 28 "
-                "layers; kernels as of commit c39bb33; not this run's")}
-ATTN_DRAM_BYTES = {"config3": (699.2e6, "ncu capture (dram__bytes_read + write) of attn_fwd_sm100_kernel "
-                                        "(83.4 MB) and attn_bwd_sm100_kernel (615.8 MB), one launch each, "
-                                        "kernels as of commit 4716b58; not this run's")}
+    "config5": (28 * (81.1e6 + 373.1e6),
+                "ncu captures (dram__bytes_read + write, one pass) of attn_fwd_sm100_kernel (83.0, 79.2 MB) and "
+                "attn_bwd_sm100_kernel (374.7, 371.5 MB) of two layers of a timed config-5 step at N=1, x 28 "
+                "layers; kernels as of commit 1f5d442; not this run's")}
+ATTN_DRAM_BYTES = {"config3": (696.3e6, "ncu capture (dram__bytes_read + write) of attn_fwd_sm100_kernel "
+                                        "(82.6 MB) and attn_bwd_sm100_kernel (613.7 MB), one launch each, "
+                                        "kernels as of commit 1f5d442; not this run's")}
 
 
 def run_reference(args, world, rank):
