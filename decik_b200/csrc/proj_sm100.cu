@@ -41,6 +41,7 @@
 #include "norm_math.cuh"
 #include "ptx.cuh"
 #include "sm100.cuh"
+#include "swiglu_math.cuh"
 
 namespace decik {
 namespace attn {
@@ -159,8 +160,8 @@ __device__ __forceinline__ float rnd(float x) {
   return Dt<T>::to_f(Dt<T>::from_f(x));
 }
 
-// the separate SwiGLU kernels' sigmoid (swiglu.cu): 1 / (1 + exp(-x)), IEEE division
-__device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
+// the separate SwiGLU kernels' sigmoid (swiglu.cu)
+using swiglu::sigmoid;
 
 // one row (this lane's) of 32 fp32 values (bit patterns in v) rounded to T into a [32 rows x 32]
 // 16-bit staging tile with the 64-byte swizzle (16-byte piece p of row r at p ^ ((r / 2) % 4))
@@ -435,7 +436,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float gf = __uint_as_float(g[e]), uf = __uint_as_float(u[e]);
-            g[e] = __float_as_uint(gf * sigmoid_ref(gf) * uf);
+            g[e] = __float_as_uint(gf * sigmoid(gf) * uf);
           }
           store_row32<T>(stg + base + 4096, lane, g);
           fence_proxy_async();
@@ -476,7 +477,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) proj_gemm_kernel(const __grid_con
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float grf = rnd<T>(__uint_as_float(gr[e]));  // grad_hidden as the 16-bit GEMM output
-            const float sg = sigmoid_ref(gv[e]);
+            const float sg = sigmoid(gv[e]);
             du[e] = __float_as_uint(grf * gv[e] * sg);
             dg[e] = __float_as_uint(grf * uv[e] * sg * (1.0f + gv[e] * (1.0f - sg)));
           }

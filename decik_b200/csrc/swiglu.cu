@@ -10,6 +10,7 @@
 // HBM-bound: 8 elements (16 bytes) per load, grid-stride over rows x 8-column groups (the forward
 // takes two groups per step so that four loads are in flight per thread).
 #include "common.cuh"
+#include "swiglu_math.cuh"
 
 namespace decik {
 namespace {
@@ -29,7 +30,7 @@ __device__ __forceinline__ void store8(T* p, const float (&f)[8]) {
   *reinterpret_cast<uint4*>(p) = make_uint4(Dt<T>::pack2(f[0], f[1]), Dt<T>::pack2(f[2], f[3]),
                                             Dt<T>::pack2(f[4], f[5]), Dt<T>::pack2(f[6], f[7]));
 }
-__device__ __forceinline__ float sigmoidf(float x) { return 1.0f / (1.0f + expf(-x)); }
+using swiglu::sigmoid;
 
 template <typename T>
 __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const T* __restrict__ gu, int64_t ld, T* __restrict__ out,
@@ -50,11 +51,11 @@ __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const T* __restrict__ g
     load8<T>(gu + row1 * ld + c1, g1);
     load8<T>(gu + row1 * ld + inter + c1, u1);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = g0[e] * sigmoidf(g0[e]) * u0[e];
+    for (int e = 0; e < 8; ++e) o[e] = g0[e] * sigmoid(g0[e]) * u0[e];
     store8<T>(out + row0 * ldo + c0, o);
     if (two) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = g1[e] * sigmoidf(g1[e]) * u1[e];
+      for (int e = 0; e < 8; ++e) o[e] = g1[e] * sigmoid(g1[e]) * u1[e];
       store8<T>(out + row1 * ldo + c1, o);
     }
   }
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const T* __restrict__ g
     load8<T>(gu + row * ld + inter + c, u);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float s = sigmoidf(g[e]);
+      const float s = sigmoid(g[e]);
       du[e] = gr[e] * g[e] * s;
       dg[e] = gr[e] * u[e] * s * (1.0f + g[e] * (1.0f - s));
     }
