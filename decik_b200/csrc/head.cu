@@ -9,16 +9,21 @@
 // n_vocab), 0 for an ignored one (target < 0), NaN for a target past the vocabulary; hit =
 // labelled and argmax == target. Pass 2, for labelled rows only, writes
 // softmax - onehot = exp(z - lse) - [col == target] over the logits in place, rounded to the
-// logits' type: the operand of the gradient matmul dX = G . W. The arithmetic is fp32.
-// HBM-bound: a labelled row moves 3 x n_vocab x 2 bytes (read, read, write).
+// logits' type: the operand of the gradient matmul dX = G . W. The arithmetic is fp32; the
+// per-logit exponentials of both passes are exp(z - c) = 2^(z log2 e - c log2 e), one FMA and the
+// hardware's ex2.approx (a relative error of a few 1e-7 for the logit ranges of a head; expf took
+// most of the kernel's issue slots). HBM-bound: a labelled row moves 3 x n_vocab x 2 bytes (read,
+// read, write).
 #include <cfloat>
 
 #include "common.cuh"
+#include "ptx.cuh"
 
 namespace decik {
 namespace {
 
 constexpr int kHeadThreads = 512;
+constexpr float kLog2eHead = 1.4426950408889634f;
 
 struct Stat {
   float m, s, w;  // max, sum exp(z - m), sum z exp(z - m)
@@ -67,15 +72,16 @@ head_stats_kernel(T* __restrict__ logits, int64_t ld, const int64_t* __restrict_
     for (int i = 1; i < 8; ++i)
       if (v[i] > mx) { mx = v[i]; at = i; }
     if (mx > st.m) {  // strictly larger: earlier columns keep the index on ties
-      const float f = st.m == -INFINITY ? 0.f : expf(st.m - mx);
+      const float f = st.m == -INFINITY ? 0.f : ptx::ex2((st.m - mx) * kLog2eHead);
       st.s *= f;
       st.w *= f;
       st.m = mx;
       st.idx = c + at;
     }
+    const float nm = -st.m * kLog2eHead;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float e = expf(v[i] - st.m);
+      const float e = ptx::ex2(fmaf(v[i], kLog2eHead, nm));
       st.s += e;
       st.w += v[i] * e;
     }
@@ -116,15 +122,15 @@ head_stats_kernel(T* __restrict__ logits, int64_t ld, const int64_t* __restrict_
   }
   __syncthreads();
   if (!labelled) return;
-  const float lse = s_lse;
+  const float nl = -s_lse * kLog2eHead;
   for (int c = threadIdx.x * 8; c < n_vocab; c += kHeadThreads * 8) {
     const uint4 u = *reinterpret_cast<const uint4*>(z + c);
     const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
     uint32_t o[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float a = expf(Dt<T>::lo_f(wd[i]) - lse);
-      float b = expf(Dt<T>::hi_f(wd[i]) - lse);
+      float a = ptx::ex2(fmaf(Dt<T>::lo_f(wd[i]), kLog2eHead, nl));
+      float b = ptx::ex2(fmaf(Dt<T>::hi_f(wd[i]), kLog2eHead, nl));
       if (c + 2 * i == tgt) a -= 1.f;
       if (c + 2 * i + 1 == tgt) b -= 1.f;
       o[i] = Dt<T>::pack2(a, b);
