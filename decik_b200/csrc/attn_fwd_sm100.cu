@@ -19,6 +19,8 @@
 // the first 64 columns of its S. The MMA thread ping-pongs the two tiles so the tensor core runs
 // one tile's QK^T / PV while the other tile's softmax runs:
 //   S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) | ...
+// and issues each PV in two halves of 64 keys, the first once the softmax has written that half of
+// P (it then computes the other half's exponentials while the first half runs).
 // Online softmax in the exp2 domain; O is rescaled in TMEM only when a row max grows by more than
 // 2^8 (the final O / l is exact for any reference max). Every mbarrier wait is bounded: a wait that
 // gives up records a code in the error word and the CTA winds down (waiting for its own MMAs and
@@ -60,7 +62,8 @@ constexpr int OFF_RING = OFF_STAGE + 8 * STAGE;                // int32 [2] tile
 constexpr int OFF_BAR = OFF_RING + 16;
 enum {
   B_Q = 0, B_QE, B_KF, B_KE = B_KF + 2, B_VF = B_KE + 2, B_VE = B_VF + 2, B_SF = B_VE + 2, B_PR = B_SF + 2,
-  B_OF = B_PR + 2, B_OE = B_OF + 2, B_TF = B_OE + 2, B_TE = B_TF + 2, B_DONE = B_TE + 2, N_BAR
+  B_OF = B_PR + 2, B_OE = B_OF + 2, B_TF = B_OE + 2, B_TE = B_TF + 2, B_DONE = B_TE + 2, B_PH = B_DONE + 1,
+  N_BAR = B_PH + 2
 };
 constexpr int OFF_TMEM = OFF_BAR + N_BAR * 8;
 constexpr int kSmem = OFF_TMEM + 16 + 1024;  // + slack for the 1024-byte alignment
@@ -135,10 +138,14 @@ __device__ __forceinline__ void issue_qk(uint32_t d, uint32_t q, uint32_t k, uin
   }
 }
 // O (+)= P V: P [128 x 128] 16-bit in TMEM (8 columns per K = 16 step), V MN-major in shared memory.
-__device__ __forceinline__ void issue_pv(uint32_t d, uint32_t p, uint32_t v, uint32_t idesc, bool acc) {
+// O += P V over keys [64 half, 64 half + 64) (k-steps 4 half .. 4 half + 3): P's columns
+// [32 half, 32 half + 32)
+__device__ __forceinline__ void issue_pv_half(uint32_t d, uint32_t p, uint32_t v, uint32_t idesc, bool acc, int half) {
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk)
+  for (int k4 = 0; k4 < 4; ++k4) {
+    const int kk = 4 * half + k4;
     umma_ts(d, p + kk * 8, smem_desc_sw128(v + kk * 2048, HALF, 1024), idesc, (acc || kk > 0) ? 1u : 0u);
+  }
 }
 
 template <typename T>
@@ -171,6 +178,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
       mbar_init(bar(B_VE + s), 1);
       mbar_init(bar(B_SF + s), 1);
       mbar_init(bar(B_PR + s), 128);
+      mbar_init(bar(B_PH + s), 128);
       mbar_init(bar(B_OF + s), 1);
       mbar_init(bar(B_OE + s), 128);
       mbar_init(bar(B_TF + s), 1);
@@ -292,10 +300,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
             const int s = g & 1;
             const uint32_t v = sb + OFF_V + s * TILE;
             const uint32_t kn = sb + OFF_K + ((g + 1) & 1) * TILE;
-            if (!mbar_wait(bar(B_VF + s), (g >> 1) & 1, p.err, 203) || !mbar_wait(bar(B_PR + 0), g0 & 1, p.err, 204))
+            // each PV in two halves: keys 0-63 once the softmax has written their P, while it
+            // computes the rest
+            if (!mbar_wait(bar(B_VF + s), (g >> 1) & 1, p.err, 203) || !mbar_wait(bar(B_PH + 0), g0 & 1, p.err, 211))
               return false;
             tc_fence_after();
-            issue_pv(tO0, tS0, v, id_pv, j > 0);
+            issue_pv_half(tO0, tS0, v, id_pv, j > 0, 0);
+            if (!mbar_wait(bar(B_PR + 0), g0 & 1, p.err, 204)) return false;
+            tc_fence_after();
+            issue_pv_half(tO0, tS0, v, id_pv, true, 1);
             ++g0;
             if (next) {
               if (!mbar_wait(bar(B_KF + ((g + 1) & 1)), ((g + 1) >> 1) & 1, p.err, 205)) return false;
@@ -304,9 +317,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
               umma_commit(bar(B_SF + 0));
             }
             if (w.has1) {
+              if (!mbar_wait(bar(B_PH + 1), g1 & 1, p.err, 212)) return false;
+              tc_fence_after();
+              issue_pv_half(tO1, tS1, v, id_pv, j > 0, 0);
               if (!mbar_wait(bar(B_PR + 1), g1 & 1, p.err, 206)) return false;
               tc_fence_after();
-              issue_pv(tO1, tS1, v, id_pv, j > 0);
+              issue_pv_half(tO1, tS1, v, id_pv, true, 1);
               ++g1;
             }
             umma_commit(bar(B_VE + s));
@@ -445,6 +461,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_fwd_sm100_kernel(const __gri
             pk[c] = pk2<T>(e0, e1);
           }
           tmem_st32(tS + 32 * h, pk);
+          if (h == 0) {  // keys 0-63 of P are in TMEM: the first half of PV may start
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(bar(B_PH + tile));
+          }
         }
         float s0, s1, s2, s3, s4, s5, s6, s7;
         f2split(acc[0], s0, s1);
