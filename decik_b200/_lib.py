@@ -75,6 +75,10 @@ SIGNATURES = {
                                       c_int64, c_int, c_float, c_void_p]),
     "decik_add_rmsnorm_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
                                       c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "decik_add_rmsnorm_fwd16": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                                        c_int64, c_int, c_float, c_void_p]),
+    "decik_add_rmsnorm_bwd16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
+                                        c_void_p, c_void_p, c_int64, c_int, c_void_p]),
     "decik_swiglu_fwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p]),
     "decik_swiglu_bwd": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_int,
                                  c_void_p]),

@@ -12,6 +12,8 @@
 // and its copy in delta's 16-bit type. The per-element and per-row arithmetic is the same source
 // as the plain kernels (sumsq4 / wdot4 / the output lines), so y and the norm gradient equal
 // rmsnorm_fwd / rmsnorm_bwd applied to the same h bit for bit.
+#include <type_traits>
+
 #include "common.cuh"
 #include "norm_math.cuh"
 
@@ -92,11 +94,12 @@ rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                                        __ldg(reinterpret_cast<const float4*>(xr + c)), w, c, rstd, k);
 }
 
-// h = residual + f32(delta); y = w * (h * rstd); rows contiguous ([n_rows, n_cols])
-template <typename W, typename D>
+// h = residual + f32(delta); y = w * (h * rstd) stored as Y (fp32, or delta's 16-bit type for a
+// consumer that computes in it: the same rounding as casting the fp32 y); rows contiguous
+template <typename W, typename D, typename Y>
 __global__ void __launch_bounds__(256)
 add_rmsnorm_fwd_kernel(const float* __restrict__ residual, const D* __restrict__ delta, const W* __restrict__ w,
-                       float* __restrict__ h, float* __restrict__ y, float* __restrict__ rstd_out, int64_t n_rows,
+                       float* __restrict__ h, Y* __restrict__ y, float* __restrict__ rstd_out, int64_t n_rows,
                        int n_cols, float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -111,16 +114,17 @@ add_rmsnorm_fwd_kernel(const float* __restrict__ residual, const D* __restrict__
   const float rstd = norm::row_rstd(acc, n_cols, eps);
   for (int c = lane * 4; c < n_cols; c += 128) {
     const float4 v = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
-    *reinterpret_cast<float4*>(y + off + c) = norm_out4<W>(v, w, c, rstd);
+    dstore4<Y>(y + off + c, norm_out4<W>(v, w, c, rstd));
   }
   if (rstd_out != nullptr && lane == 0) rstd_out[row] = rstd;
 }
 
 // total = grad_h + norm_bwd(dy, h) with h = residual + f32(delta) rebuilt; total in fp32 and,
-// when dx16 is set, in delta's type (the delta input's gradient)
-template <typename W, typename D>
+// when dx16 is set, in delta's type (the delta input's gradient); dy of type G (fp32, or the 16-bit
+// gradient of a 16-bit y)
+template <typename W, typename D, typename G>
 __global__ void __launch_bounds__(256)
-add_rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ grad_h,
+add_rmsnorm_bwd_kernel(const G* __restrict__ dy, const float* __restrict__ grad_h,
                        const float* __restrict__ residual, const D* __restrict__ delta, const W* __restrict__ w,
                        const float* __restrict__ rstd_in, float* __restrict__ dx, D* __restrict__ dx16,
                        int64_t n_rows, int n_cols) {
@@ -132,13 +136,13 @@ add_rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ g
   float acc = 0.f;
   for (int c = lane * 4; c < n_cols; c += 128) {
     const float4 v = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
-    acc += wdot4<W>(__ldg(reinterpret_cast<const float4*>(dy + off + c)), v, w, c);
+    acc += wdot4<W>(dload4<G>(dy + off + c), v, w, c);
   }
   const float dot = warp_sum(acc) / static_cast<float>(n_cols);
   const float k = rstd * rstd * dot;
   for (int c = lane * 4; c < n_cols; c += 128) {
     const float4 v = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
-    float4 o = norm_grad4<W>(__ldg(reinterpret_cast<const float4*>(dy + off + c)), v, w, c, rstd, k);
+    float4 o = norm_grad4<W>(dload4<G>(dy + off + c), v, w, c, rstd, k);
     if (grad_h != nullptr) o = add4(__ldg(reinterpret_cast<const float4*>(grad_h + off + c)), o);
     *reinterpret_cast<float4*>(dx + off + c) = o;
     if (dx16 != nullptr) dstore4<D>(dx16 + off + c, o);
@@ -200,10 +204,10 @@ rmsnorm_bwd_reg_kernel(const float* __restrict__ dy, const float* __restrict__ x
     *reinterpret_cast<float4*>(dx + off + lane * 4 + 128 * j) = norm_grad4<W>(g[j], v[j], w, lane * 4 + 128 * j, rstd, k);
 }
 
-template <typename W, typename D, int NC>
+template <typename W, typename D, typename Y, int NC>
 __global__ void __launch_bounds__(256)
 add_rmsnorm_fwd_reg_kernel(const float* __restrict__ residual, const D* __restrict__ delta, const W* __restrict__ w,
-                           float* __restrict__ h, float* __restrict__ y, float* __restrict__ rstd_out, int64_t n_rows,
+                           float* __restrict__ h, Y* __restrict__ y, float* __restrict__ rstd_out, int64_t n_rows,
                            float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -224,13 +228,13 @@ add_rmsnorm_fwd_reg_kernel(const float* __restrict__ residual, const D* __restri
   const float rstd = norm::row_rstd(acc, NC * 128, eps);
 #pragma unroll
   for (int j = 0; j < NC; ++j)
-    *reinterpret_cast<float4*>(y + off + lane * 4 + 128 * j) = norm_out4<W>(v[j], w, lane * 4 + 128 * j, rstd);
+    dstore4<Y>(y + off + lane * 4 + 128 * j, norm_out4<W>(v[j], w, lane * 4 + 128 * j, rstd));
   if (rstd_out != nullptr && lane == 0) rstd_out[row] = rstd;
 }
 
-template <typename W, typename D, int NC>
+template <typename W, typename D, typename G, int NC>
 __global__ void __launch_bounds__(256, 2)
-add_rmsnorm_bwd_reg_kernel(const float* __restrict__ dy, const float* __restrict__ grad_h,
+add_rmsnorm_bwd_reg_kernel(const G* __restrict__ dy, const float* __restrict__ grad_h,
                            const float* __restrict__ residual, const D* __restrict__ delta, const W* __restrict__ w,
                            const float* __restrict__ rstd_in, float* __restrict__ dx, D* __restrict__ dx16,
                            int64_t n_rows) {
@@ -244,7 +248,7 @@ add_rmsnorm_bwd_reg_kernel(const float* __restrict__ dy, const float* __restrict
   for (int j = 0; j < NC; ++j) {
     const int c = lane * 4 + 128 * j;
     v[j] = add4(__ldg(reinterpret_cast<const float4*>(residual + off + c)), dload4<D>(delta + off + c));
-    g[j] = __ldg(reinterpret_cast<const float4*>(dy + off + c));
+    g[j] = dload4<G>(dy + off + c);
   }
   float acc = 0.f;
 #pragma unroll
@@ -331,27 +335,90 @@ int add_rmsnorm_check(int64_t n_rows, int n_cols, const void* delta, int d_dtype
   return DECIK_OK;
 }
 
-template <typename W, typename D>
-void launch_add_fwd(const float* residual, const void* delta, const void* w, float* h, float* y, float* rstd,
+// Y / G: the type of y / dy, fp32 or (the 16-bit entry points) delta's type D
+template <typename W, typename D, bool Y16>
+void launch_add_fwd(const float* residual, const void* delta, const void* w, float* h, void* y, float* rstd,
                     int64_t n_rows, int n_cols, float eps, cudaStream_t st) {
+  using Y = typename std::conditional<Y16, D, float>::type;
   if (n_cols == 12 * 128)
-    add_rmsnorm_fwd_reg_kernel<W, D, 12><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
-        residual, static_cast<const D*>(delta), static_cast<const W*>(w), h, y, rstd, n_rows, eps);
+    add_rmsnorm_fwd_reg_kernel<W, D, Y, 12><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+        residual, static_cast<const D*>(delta), static_cast<const W*>(w), h, static_cast<Y*>(y), rstd, n_rows, eps);
   else
-    add_rmsnorm_fwd_kernel<W, D><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
-        residual, static_cast<const D*>(delta), static_cast<const W*>(w), h, y, rstd, n_rows, n_cols, eps);
+    add_rmsnorm_fwd_kernel<W, D, Y><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+        residual, static_cast<const D*>(delta), static_cast<const W*>(w), h, static_cast<Y*>(y), rstd, n_rows, n_cols,
+        eps);
 }
-template <typename W, typename D>
-void launch_add_bwd(const float* dy, const float* grad_h, const float* residual, const void* delta, const void* w,
+template <typename W, typename D, bool G16>
+void launch_add_bwd(const void* dy, const float* grad_h, const float* residual, const void* delta, const void* w,
                     const float* rstd, float* dx, void* dx16, int64_t n_rows, int n_cols, cudaStream_t st) {
+  using G = typename std::conditional<G16, D, float>::type;
   if (n_cols == 12 * 128)
-    add_rmsnorm_bwd_reg_kernel<W, D, 12><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
-        dy, grad_h, residual, static_cast<const D*>(delta), static_cast<const W*>(w), rstd, dx, static_cast<D*>(dx16),
-        n_rows);
+    add_rmsnorm_bwd_reg_kernel<W, D, G, 12><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+        static_cast<const G*>(dy), grad_h, residual, static_cast<const D*>(delta), static_cast<const W*>(w), rstd, dx,
+        static_cast<D*>(dx16), n_rows);
   else
-    add_rmsnorm_bwd_kernel<W, D><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
-        dy, grad_h, residual, static_cast<const D*>(delta), static_cast<const W*>(w), rstd, dx, static_cast<D*>(dx16),
-        n_rows, n_cols);
+    add_rmsnorm_bwd_kernel<W, D, G><<<static_cast<int>((n_rows + 7) / 8), 256, 0, st>>>(
+        static_cast<const G*>(dy), grad_h, residual, static_cast<const D*>(delta), static_cast<const W*>(w), rstd, dx,
+        static_cast<D*>(dx16), n_rows, n_cols);
+}
+
+}  // namespace
+}  // namespace decik
+
+namespace decik {
+namespace {
+
+template <bool Y16>
+int add_rmsnorm_fwd_impl(const float* residual, const void* delta, int delta_dtype, const void* w, int w_dtype,
+                         float* h, void* y, float* rstd, int64_t n_rows, int n_cols, float eps, void* stream,
+                         const char* what) {
+  if (n_rows == 0) return DECIK_OK;
+  if (!residual || !delta || !w || !h || !y) return set_error(DECIK_ERR_INVALID, "%s: null pointer", what);
+  if (int rc = add_rmsnorm_check(n_rows, n_cols, delta, delta_dtype, w_dtype, what)) return rc;
+  if (Y16 && delta_dtype == DECIK_F32) return set_error(DECIK_ERR_INVALID, "%s: delta must be F16 or BF16", what);
+  if (!aligned16(residual) || !aligned16(h) || (Y16 ? (reinterpret_cast<uintptr_t>(y) & 7u) != 0 : !aligned16(y)))
+    return set_error(DECIK_ERR_INVALID, "%s: residual, h (16 bytes) or y (16 / 8 bytes) misaligned", what);
+  const cudaStream_t st = as_stream(stream);
+  const bool wf = w_dtype == DECIK_F32;
+  if (delta_dtype == DECIK_F32) {
+    (wf ? launch_add_fwd<float, float, false> : launch_add_fwd<__half, float, false>)(residual, delta, w, h, y, rstd,
+                                                                                   n_rows, n_cols, eps, st);
+  } else if (delta_dtype == DECIK_F16) {
+    (wf ? launch_add_fwd<float, __half, Y16> : launch_add_fwd<__half, __half, Y16>)(residual, delta, w, h, y, rstd,
+                                                                                  n_rows, n_cols, eps, st);
+  } else {
+    (wf ? launch_add_fwd<float, __nv_bfloat16, Y16> : launch_add_fwd<__half, __nv_bfloat16, Y16>)(
+        residual, delta, w, h, y, rstd, n_rows, n_cols, eps, st);
+  }
+  return check_launch(what);
+}
+
+template <bool G16>
+int add_rmsnorm_bwd_impl(const void* dy, const float* grad_h, const float* residual, const void* delta,
+                         int delta_dtype, const void* w, int w_dtype, const float* rstd, float* dx, void* dx16,
+                         int64_t n_rows, int n_cols, void* stream, const char* what) {
+  if (n_rows == 0) return DECIK_OK;
+  if (!dy || !residual || !delta || !w || !rstd || !dx) return set_error(DECIK_ERR_INVALID, "%s: null pointer", what);
+  if (int rc = add_rmsnorm_check(n_rows, n_cols, delta, delta_dtype, w_dtype, what)) return rc;
+  if (G16 && delta_dtype == DECIK_F32) return set_error(DECIK_ERR_INVALID, "%s: delta must be F16 or BF16", what);
+  if ((G16 ? (reinterpret_cast<uintptr_t>(dy) & 7u) != 0 : !aligned16(dy)) || !aligned16(residual) || !aligned16(dx) ||
+      (grad_h && !aligned16(grad_h)))
+    return set_error(DECIK_ERR_INVALID, "%s: dy, grad_h, residual or dx misaligned", what);
+  if (dx16 && (reinterpret_cast<uintptr_t>(dx16) & (delta_dtype == DECIK_F32 ? 15u : 7u)))
+    return set_error(DECIK_ERR_INVALID, "%s: dx16 misaligned", what);
+  const cudaStream_t st = as_stream(stream);
+  const bool wf = w_dtype == DECIK_F32;
+  if (delta_dtype == DECIK_F32) {
+    (wf ? launch_add_bwd<float, float, false> : launch_add_bwd<__half, float, false>)(dy, grad_h, residual, delta, w,
+                                                                                   rstd, dx, dx16, n_rows, n_cols, st);
+  } else if (delta_dtype == DECIK_F16) {
+    (wf ? launch_add_bwd<float, __half, G16> : launch_add_bwd<__half, __half, G16>)(dy, grad_h, residual, delta, w,
+                                                                                  rstd, dx, dx16, n_rows, n_cols, st);
+  } else {
+    (wf ? launch_add_bwd<float, __nv_bfloat16, G16> : launch_add_bwd<__half, __nv_bfloat16, G16>)(
+        dy, grad_h, residual, delta, w, rstd, dx, dx16, n_rows, n_cols, st);
+  }
+  return check_launch(what);
 }
 
 }  // namespace
@@ -360,48 +427,28 @@ void launch_add_bwd(const float* dy, const float* grad_h, const float* residual,
 extern "C" int decik_add_rmsnorm_fwd(const float* residual, const void* delta, int delta_dtype, const void* w,
                                      int w_dtype, float* h, float* y, float* rstd, int64_t n_rows, int n_cols,
                                      float eps, void* stream) {
-  using namespace decik;
-  if (n_rows == 0) return DECIK_OK;
-  if (!residual || !delta || !w || !h || !y) return set_error(DECIK_ERR_INVALID, "add_rmsnorm_fwd: null pointer");
-  if (int rc = add_rmsnorm_check(n_rows, n_cols, delta, delta_dtype, w_dtype, "add_rmsnorm_fwd")) return rc;
-  if (!aligned16(residual) || !aligned16(h) || !aligned16(y))
-    return set_error(DECIK_ERR_INVALID, "add_rmsnorm_fwd: residual, h, y must be 16-byte aligned");
-  const cudaStream_t st = as_stream(stream);
-  const bool wf = w_dtype == DECIK_F32;
-  if (delta_dtype == DECIK_F32) {
-    (wf ? launch_add_fwd<float, float> : launch_add_fwd<__half, float>)(residual, delta, w, h, y, rstd, n_rows, n_cols, eps, st);
-  } else if (delta_dtype == DECIK_F16) {
-    (wf ? launch_add_fwd<float, __half> : launch_add_fwd<__half, __half>)(residual, delta, w, h, y, rstd, n_rows, n_cols, eps, st);
-  } else {
-    (wf ? launch_add_fwd<float, __nv_bfloat16> : launch_add_fwd<__half, __nv_bfloat16>)(residual, delta, w, h, y, rstd,
-                                                                                       n_rows, n_cols, eps, st);
-  }
-  return check_launch("add_rmsnorm_fwd");
+  return decik::add_rmsnorm_fwd_impl<false>(residual, delta, delta_dtype, w, w_dtype, h, y, rstd, n_rows, n_cols, eps,
+                                            stream, "add_rmsnorm_fwd");
+}
+
+extern "C" int decik_add_rmsnorm_fwd16(const float* residual, const void* delta, int delta_dtype, const void* w,
+                                       int w_dtype, float* h, void* y16, float* rstd, int64_t n_rows, int n_cols,
+                                       float eps, void* stream) {
+  return decik::add_rmsnorm_fwd_impl<true>(residual, delta, delta_dtype, w, w_dtype, h, y16, rstd, n_rows, n_cols, eps,
+                                           stream, "add_rmsnorm_fwd16");
 }
 
 extern "C" int decik_add_rmsnorm_bwd(const float* dy, const float* grad_h, const float* residual, const void* delta,
                                      int delta_dtype, const void* w, int w_dtype, const float* rstd, float* dx,
                                      void* dx16, int64_t n_rows, int n_cols, void* stream) {
-  using namespace decik;
-  if (n_rows == 0) return DECIK_OK;
-  if (!dy || !residual || !delta || !w || !rstd || !dx)
-    return set_error(DECIK_ERR_INVALID, "add_rmsnorm_bwd: null pointer");
-  if (int rc = add_rmsnorm_check(n_rows, n_cols, delta, delta_dtype, w_dtype, "add_rmsnorm_bwd")) return rc;
-  if (!aligned16(dy) || !aligned16(residual) || !aligned16(dx) || (grad_h && !aligned16(grad_h)))
-    return set_error(DECIK_ERR_INVALID, "add_rmsnorm_bwd: dy, grad_h, residual, dx must be 16-byte aligned");
-  if (dx16 && (reinterpret_cast<uintptr_t>(dx16) & (delta_dtype == DECIK_F32 ? 15u : 7u)))
-    return set_error(DECIK_ERR_INVALID, "add_rmsnorm_bwd: dx16 misaligned");
-  const cudaStream_t st = as_stream(stream);
-  const bool wf = w_dtype == DECIK_F32;
-  if (delta_dtype == DECIK_F32) {
-    (wf ? launch_add_bwd<float, float> : launch_add_bwd<__half, float>)(dy, grad_h, residual, delta, w, rstd, dx, dx16,
-                                                                      n_rows, n_cols, st);
-  } else if (delta_dtype == DECIK_F16) {
-    (wf ? launch_add_bwd<float, __half> : launch_add_bwd<__half, __half>)(dy, grad_h, residual, delta, w, rstd, dx, dx16,
-                                                                        n_rows, n_cols, st);
-  } else {
-    (wf ? launch_add_bwd<float, __nv_bfloat16> : launch_add_bwd<__half, __nv_bfloat16>)(dy, grad_h, residual, delta, w,
-                                                                                       rstd, dx, dx16, n_rows, n_cols, st);
-  }
-  return check_launch("add_rmsnorm_bwd");
+  return decik::add_rmsnorm_bwd_impl<false>(dy, grad_h, residual, delta, delta_dtype, w, w_dtype, rstd, dx, dx16, n_rows,
+                                            n_cols, stream, "add_rmsnorm_bwd");
+}
+
+extern "C" int decik_add_rmsnorm_bwd16(const void* dy16, const float* grad_h, const float* residual,
+                                       const void* delta, int delta_dtype, const void* w, int w_dtype,
+                                       const float* rstd, float* dx, void* dx16, int64_t n_rows, int n_cols,
+                                       void* stream) {
+  return decik::add_rmsnorm_bwd_impl<true>(dy16, grad_h, residual, delta, delta_dtype, w, w_dtype, rstd, dx, dx16,
+                                           n_rows, n_cols, stream, "add_rmsnorm_bwd16");
 }

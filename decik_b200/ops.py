@@ -255,39 +255,48 @@ def rmsnorm_bwd(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor, rstd: torc
     return dx
 
 
-def add_rmsnorm_fwd(residual: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float):
-    """h = residual + delta (fp32), y = RMSNorm(h) * w (fp32), rstd [rows]; residual fp32 and delta
-    fp32 / fp16 / bf16 of the same shape (last dim the normalised one)."""
+def add_rmsnorm_fwd(residual: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float, y16: bool = False):
+    """h = residual + delta (fp32), y = RMSNorm(h) * w, rstd [rows]; residual fp32 and delta
+    fp32 / fp16 / bf16 of the same shape (last dim the normalised one). y is fp32, or with ``y16``
+    in delta's 16-bit dtype (decik_add_rmsnorm_fwd16: the fp32 y rounded, never written)."""
     _cuda(residual, delta, w)
     if residual.dtype != torch.float32 or residual.shape != delta.shape:
         raise RuntimeError("decik_b200 add_rmsnorm_fwd: residual fp32 and delta of the same shape")
     n_cols = residual.shape[-1]
     r2 = residual.reshape(-1, n_cols).contiguous()
     d2 = delta.reshape(-1, n_cols).contiguous()
+    if y16 and d2.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("decik_b200 add_rmsnorm_fwd: a 16-bit y needs a 16-bit delta")
     h = torch.empty_like(r2)
-    y = torch.empty_like(r2)
+    y = torch.empty_like(d2) if y16 else torch.empty_like(r2)
     rstd = torch.empty(r2.shape[0], dtype=torch.float32, device=r2.device)
+    fn = _lib.lib().decik_add_rmsnorm_fwd16 if y16 else _lib.lib().decik_add_rmsnorm_fwd
     with _timed("add_rmsnorm_fwd", 1):
-        rc = _lib.lib().decik_add_rmsnorm_fwd(_p(r2), _p(d2), _dt(d2), _p(w.contiguous()), _dt(w), _p(h), _p(y),
-                                              _p(rstd), r2.shape[0], n_cols, float(eps), _stream(r2))
+        rc = fn(_p(r2), _p(d2), _dt(d2), _p(w.contiguous()), _dt(w), _p(h), _p(y), _p(rstd), r2.shape[0], n_cols,
+                float(eps), _stream(r2))
     _lib.check(rc, "add_rmsnorm_fwd")
     return h.view(residual.shape), y.view(residual.shape), rstd
 
 
 def add_rmsnorm_bwd(dy, grad_h, residual, delta, w, rstd, want_dx16: bool = True):
     """(dx fp32, dx in delta's dtype or None): dx = grad_h + RMSNorm backward of dy at
-    h = residual + delta (rebuilt, not stored); grad_h may be None."""
+    h = residual + delta (rebuilt, not stored); grad_h may be None. dy fp32, or in delta's 16-bit
+    dtype (the gradient of a 16-bit y: decik_add_rmsnorm_bwd16 reads it as it is)."""
     _cuda(dy, residual, delta, w, rstd)
     n_cols = residual.shape[-1]
     r2 = residual.reshape(-1, n_cols).contiguous()
     d2 = delta.reshape(-1, n_cols).contiguous()
-    g2 = dy.reshape(-1, n_cols).contiguous().float()
+    dy16 = dy.dtype == d2.dtype and dy.dtype in (torch.float16, torch.bfloat16)
+    g2 = dy.reshape(-1, n_cols).contiguous()
+    if not dy16:
+        g2 = g2.float()
     gh = None if grad_h is None else grad_h.reshape(-1, n_cols).contiguous().float()
     dx = torch.empty_like(r2)
     dx16 = torch.empty_like(d2) if want_dx16 else None
+    fn = _lib.lib().decik_add_rmsnorm_bwd16 if dy16 else _lib.lib().decik_add_rmsnorm_bwd
     with _timed("add_rmsnorm_bwd", 1):
-        rc = _lib.lib().decik_add_rmsnorm_bwd(_p(g2), _p(gh), _p(r2), _p(d2), _dt(d2), _p(w.contiguous()), _dt(w),
-                                              _p(rstd), _p(dx), _p(dx16), r2.shape[0], n_cols, _stream(r2))
+        rc = fn(_p(g2), _p(gh), _p(r2), _p(d2), _dt(d2), _p(w.contiguous()), _dt(w), _p(rstd), _p(dx), _p(dx16),
+                r2.shape[0], n_cols, _stream(r2))
     _lib.check(rc, "add_rmsnorm_bwd")
     return dx.view(residual.shape), None if dx16 is None else dx16.view(delta.shape)
 

@@ -64,7 +64,10 @@ class FusedMLP(torch.autograd.Function):
         gu, w_gu, w_down = ctx.saved_tensors
         g16 = grad_out.reshape(-1, grad_out.shape[-1]).to(w_down.dtype).contiguous()
         dgu = ops.mlp_down_grad(g16, w_down, gu)           # [T, 2 * inter] = [dgate | dup]
-        dx = torch.mm(dgu, w_gu, out_dtype=torch.float32)  # both input gradients summed in fp32
+        if ctx.in_dtype == torch.float32:
+            dx = torch.mm(dgu, w_gu, out_dtype=torch.float32)  # both input gradients summed in fp32
+        else:  # a 16-bit input: the fp32 sum rounded once to its dtype
+            dx = torch.mm(dgu, w_gu)
         return dx.to(ctx.in_dtype).view(ctx.shape), None, None, (grad_out if ctx.residual else None)
 
 
@@ -103,20 +106,27 @@ def patch(linear4bit_cls=None):
                 and not weight.requires_grad and bias is None
                 and supported(getattr(weight, "quant_state", None), n_in))
 
-    def forward(self, x, residual=None):
-        # ``residual``: the patched decoder layer's fp32 stream; the result is then residual + mlp(x)
+    def eligible(self, x):
+        """The node's compute dtype if it runs on x, else None."""
         config = getattr(self, "config", None)
         gate, up, down = (getattr(self, n, None) for n in ("gate_proj", "up_proj", "down_proj"))
         dtype = getattr(gate, "compute_dtype", None)
-        if not (isinstance(x, torch.Tensor) and on_gpu(x) and x.numel() > 0
-                and x.dtype in (torch.float32, torch.float16, torch.bfloat16)
-                and getattr(config, "hidden_act", None) == "silu" and dtype in (torch.float16, torch.bfloat16)
-                and nf4_projection(gate, x.shape[-1], dtype) and nf4_projection(up, x.shape[-1], dtype)
-                and gate.weight.quant_state.shape == up.weight.quant_state.shape
-                and nf4_projection(down, gate.weight.quant_state.shape[0], dtype)
-                and gate.weight.quant_state.shape[0] % 256 == 0 and x.shape[-1] % 8 == 0):
+        ok = (isinstance(x, torch.Tensor) and on_gpu(x) and x.numel() > 0
+              and x.dtype in (torch.float32, torch.float16, torch.bfloat16)
+              and getattr(config, "hidden_act", None) == "silu" and dtype in (torch.float16, torch.bfloat16)
+              and nf4_projection(gate, x.shape[-1], dtype) and nf4_projection(up, x.shape[-1], dtype)
+              and gate.weight.quant_state.shape == up.weight.quant_state.shape
+              and nf4_projection(down, gate.weight.quant_state.shape[0], dtype)
+              and gate.weight.quant_state.shape[0] % 256 == 0 and x.shape[-1] % 8 == 0)
+        return dtype if ok else None
+
+    def forward(self, x, residual=None):
+        # ``residual``: the patched decoder layer's fp32 stream; the result is then residual + mlp(x)
+        dtype = eligible(self, x)
+        if dtype is None:
             out = original(self, x)
             return out if residual is None else residual + out
+        gate, up, down = self.gate_proj, self.up_proj, self.down_proj
         w_gu, w_down = mlp_weights(gate, up, down, dtype)
         if residual is not None and not (residual.dtype == torch.float32 and residual.shape == x.shape
                                          and residual.is_contiguous()):
@@ -124,4 +134,5 @@ def patch(linear4bit_cls=None):
         return FusedMLP.apply(x, w_gu, w_down, residual)
 
     forward._skc = True
+    forward._skc_eligible = eligible  # the patched decoder layer asks before choosing its norm's dtype
     cls.forward = forward

@@ -55,11 +55,15 @@ class AddRMSNormFn(torch.autograd.Function):
     kept for backward: it is rebuilt from the residual (the layer input, kept by the input norm
     anyway) and delta (the 16-bit attention output). One sm_100a kernel each way
     (``decik_add_rmsnorm_fwd/bwd``); y equals RMSNormFn on the same h bit for bit, and the input
-    gradient is grad_h + the norm's gradient, returned to both inputs (fp32, and in delta's dtype)."""
+    gradient is grad_h + the norm's gradient, returned to both inputs (fp32, and in delta's dtype).
+
+    With ``y16`` y comes out in delta's 16-bit dtype, for a consumer that computes in it (the patched
+    MLP, whose first step is that cast): the fp32 y is never written, and y's gradient arrives in
+    the same dtype and is read as it is."""
 
     @staticmethod
-    def forward(ctx, residual, delta, weight, eps):
-        h, y, rstd = ops.add_rmsnorm_fwd(residual, delta, weight, eps)
+    def forward(ctx, residual, delta, weight, eps, y16=False):
+        h, y, rstd = ops.add_rmsnorm_fwd(residual, delta, weight, eps, y16=y16)
         ctx.save_for_backward(residual, delta, weight, rstd)
         ctx.eps = eps
         return h, y
@@ -69,10 +73,10 @@ class AddRMSNormFn(torch.autograd.Function):
         residual, delta, weight, rstd = ctx.saved_tensors
         if grad_y is None:
             if grad_h is None:
-                return None, None, None, None
-            return grad_h, grad_h.to(delta.dtype), None, None
+                return None, None, None, None, None
+            return grad_h, grad_h.to(delta.dtype), None, None, None
         total, total16 = ops.add_rmsnorm_bwd(grad_y, grad_h, residual, delta, weight, rstd)
-        return total, total16, None, None
+        return total, total16, None, None, None
 
 
 def fusable(module, x):

@@ -310,7 +310,11 @@ def _decoder_layer(original, fuse_residual, fuse_input_norm=True):
         if (isinstance(attn, torch.Tensor) and attn.is_cuda and attn.shape == layer_in.shape
                 and attn.dtype in (torch.float16, torch.bfloat16)):
             eps = float(post_norm.variance_epsilon)
-            mid, normed = rmsnorm.AddRMSNormFn.apply(layer_in, attn, post_norm.weight, eps)
+            # y in the attention output's 16-bit dtype when the patched MLP will compute in that
+            # dtype: its cast of an fp32 y (and the fp32 y itself) is then never made
+            eligible = getattr(type(self.mlp).forward, "_skc_eligible", None)
+            y16 = eligible is not None and eligible(self.mlp, attn) == attn.dtype
+            mid, normed = rmsnorm.AddRMSNormFn.apply(layer_in, attn, post_norm.weight, eps, y16)
             STATE.norm_link = (normed, (layer_in, attn), post_norm.weight, eps)
         else:
             mid = layer_in + attn

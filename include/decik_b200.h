@@ -262,6 +262,17 @@ DECIK_API int decik_add_rmsnorm_fwd(const float* residual, const void* delta, in
 DECIK_API int decik_add_rmsnorm_bwd(const float* dy, const float* grad_h, const float* residual,
                       const void* delta, int delta_dtype, const void* w, int w_dtype, const float* rstd,
                       float* dx, void* dx16, int64_t n_rows, int n_cols, void* stream);
+/* The same with y (forward) and dy (backward) in delta's 16-bit type (delta F16 or BF16; y, dy
+ * 8-byte aligned): for a consumer of y that computes in that type (the patched MLP), which would
+ * otherwise cast the fp32 y, and whose input gradient is then of that type. y equals
+ * decik_add_rmsnorm_fwd's y rounded to the type, and the backward equals decik_add_rmsnorm_bwd on
+ * the widened dy, bit for bit. */
+DECIK_API int decik_add_rmsnorm_fwd16(const float* residual, const void* delta, int delta_dtype, const void* w,
+                      int w_dtype, float* h, void* y16, float* rstd, int64_t n_rows, int n_cols, float eps,
+                      void* stream);
+DECIK_API int decik_add_rmsnorm_bwd16(const void* dy16, const float* grad_h, const float* residual,
+                      const void* delta, int delta_dtype, const void* w, int w_dtype, const float* rstd,
+                      float* dx, void* dx16, int64_t n_rows, int n_cols, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * SwiGLU of the Qwen2 MLP, for the fused MLP node.

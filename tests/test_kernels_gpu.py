@@ -272,6 +272,33 @@ def test_add_rmsnorm_equals_unfused_kernels(cuda_lib, rows, cols, dtype):
     np.testing.assert_allclose(dx.cpu().numpy(), tot, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("rows,cols", [(1, 256), (1000, 1536), (5, 8192)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("wdtype", [torch.float32, torch.float16])
+def test_add_rmsnorm_16bit_y_and_dy(cuda_lib, rows, cols, dtype, wdtype):
+    """The 16-bit variants (decik_add_rmsnorm_fwd16 / _bwd16) equal the fp32 ones bit for bit: y is
+    the fp32 y rounded to delta's dtype (h, rstd unchanged), and the backward of a 16-bit dy is the
+    backward of the same dy widened to fp32."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(rows + cols + 1)
+    r = (torch.randn(rows, cols, generator=g) * 3).to(DEV)
+    d = (torch.randn(rows, cols, generator=g) * 2).to(dtype).to(DEV)
+    w = (torch.rand(cols, generator=g) + 0.5).to(wdtype).to(DEV)
+    dy16 = torch.randn(rows, cols, generator=g).to(dtype).to(DEV)
+    gh = torch.randn(rows, cols, generator=g).to(DEV)
+    h, y, rstd = ops.add_rmsnorm_fwd(r, d, w, 1e-6)
+    h16, y16, rstd16 = ops.add_rmsnorm_fwd(r, d, w, 1e-6, y16=True)
+    assert y16.dtype == dtype and torch.equal(y16, y.to(dtype))
+    assert torch.equal(h16, h) and torch.equal(rstd16, rstd)
+    for grad_h in (gh, None):
+        dx, dx_16 = ops.add_rmsnorm_bwd(dy16, grad_h, r, d, w, rstd)
+        dx_ref, dx_16_ref = ops.add_rmsnorm_bwd(dy16.float(), grad_h, r, d, w, rstd)
+        assert torch.equal(dx, dx_ref) and torch.equal(dx_16, dx_16_ref)
+    assert cuda_lib.decik_kernel_error(1) == 0
+    with pytest.raises(RuntimeError, match="16-bit delta"):
+        ops.add_rmsnorm_fwd(r, r.clone(), w, 1e-6, y16=True)
+
+
 def test_add_rmsnorm_rejects_bad_arguments(cuda_lib):
     ops = _ops()
     r = torch.randn(4, 6, device=DEV)
