@@ -71,6 +71,8 @@ SIGNATURES = {
                                   c_int64, c_float, c_void_p]),
     "decik_rmsnorm_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int,
                                   c_void_p]),
+    "decik_rmsnorm_bwd_add": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64,
+                                      c_int, c_void_p]),
     "decik_add_rmsnorm_fwd": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
                                       c_int64, c_int, c_float, c_void_p]),
     "decik_add_rmsnorm_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,

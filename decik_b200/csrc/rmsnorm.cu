@@ -75,7 +75,7 @@ rmsnorm_fwd_kernel(const float* __restrict__ x, const W* __restrict__ w, float* 
 template <typename W>
 __global__ void __launch_bounds__(256)
 rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
-                   const W* __restrict__ w, const float* __restrict__ rstd_in,
+                   const W* __restrict__ w, const float* __restrict__ rstd_in, const float* __restrict__ addend,
                    float* __restrict__ dx, int64_t n_rows, int n_cols) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -89,9 +89,12 @@ rmsnorm_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
   const float dot = warp_sum(acc) / static_cast<float>(n_cols);
   const float k = rstd * rstd * dot;
   float* dr = dx + row * n_cols;
-  for (int c = lane * 4; c < n_cols; c += 128)
-    *reinterpret_cast<float4*>(dr + c) = norm_grad4<W>(__ldg(reinterpret_cast<const float4*>(gr + c)),
-                                                       __ldg(reinterpret_cast<const float4*>(xr + c)), w, c, rstd, k);
+  for (int c = lane * 4; c < n_cols; c += 128) {
+    float4 o = norm_grad4<W>(__ldg(reinterpret_cast<const float4*>(gr + c)), __ldg(reinterpret_cast<const float4*>(xr + c)),
+                             w, c, rstd, k);
+    if (addend != nullptr) o = add4(__ldg(reinterpret_cast<const float4*>(addend + row * n_cols + c)), o);
+    *reinterpret_cast<float4*>(dr + c) = o;
+  }
 }
 
 // h = residual + f32(delta); y = w * (h * rstd) stored as Y (fp32, or delta's 16-bit type for a
@@ -182,7 +185,8 @@ rmsnorm_fwd_reg_kernel(const float* __restrict__ x, const W* __restrict__ w, flo
 template <typename W, int NC>
 __global__ void __launch_bounds__(256, 2)
 rmsnorm_bwd_reg_kernel(const float* __restrict__ dy, const float* __restrict__ x, const W* __restrict__ w,
-                       const float* __restrict__ rstd_in, float* __restrict__ dx, int64_t n_rows) {
+                       const float* __restrict__ rstd_in, const float* __restrict__ addend, float* __restrict__ dx,
+                       int64_t n_rows) {
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= n_rows) return;
@@ -200,8 +204,12 @@ rmsnorm_bwd_reg_kernel(const float* __restrict__ dy, const float* __restrict__ x
   const float dot = warp_sum(acc) / static_cast<float>(NC * 128);
   const float k = rstd * rstd * dot;
 #pragma unroll
-  for (int j = 0; j < NC; ++j)
-    *reinterpret_cast<float4*>(dx + off + lane * 4 + 128 * j) = norm_grad4<W>(g[j], v[j], w, lane * 4 + 128 * j, rstd, k);
+  for (int j = 0; j < NC; ++j) {
+    const int c = lane * 4 + 128 * j;
+    float4 o = norm_grad4<W>(g[j], v[j], w, c, rstd, k);
+    if (addend != nullptr) o = add4(__ldg(reinterpret_cast<const float4*>(addend + off + c)), o);
+    *reinterpret_cast<float4*>(dx + off + c) = o;
+  }
 }
 
 template <typename W, typename D, typename Y, int NC>
@@ -292,30 +300,45 @@ extern "C" int decik_rmsnorm_fwd(const float* x, const void* w, int w_dtype, flo
   return check_launch("rmsnorm_fwd");
 }
 
-extern "C" int decik_rmsnorm_bwd(const float* dy, const float* x, const void* w, int w_dtype,
-                                 const float* rstd, float* dx, int64_t n_rows, int n_cols,
-                                 void* stream) {
-  using namespace decik;
+namespace decik {
+namespace {
+
+int rmsnorm_bwd_impl(const float* dy, const float* x, const void* w, int w_dtype, const float* rstd,
+                     const float* addend, float* dx, int64_t n_rows, int n_cols, void* stream, const char* what) {
   if (n_rows == 0) return DECIK_OK;
   if (n_rows < 0 || n_cols <= 0 || n_cols % 4 != 0 || n_cols > kMaxCols)
-    return set_error(DECIK_ERR_INVALID, "rmsnorm_bwd: n_cols %d", n_cols);
-  if (!dy || !x || !w || !rstd || !dx) return set_error(DECIK_ERR_INVALID, "rmsnorm_bwd: null pointer");
-  if (!aligned16(dy) || !aligned16(x) || !aligned16(dx))
-    return set_error(DECIK_ERR_INVALID, "rmsnorm_bwd: dy, x, dx must be 16-byte aligned");
+    return set_error(DECIK_ERR_INVALID, "%s: n_cols %d", what, n_cols);
+  if (!dy || !x || !w || !rstd || !dx) return set_error(DECIK_ERR_INVALID, "%s: null pointer", what);
+  if (!aligned16(dy) || !aligned16(x) || !aligned16(dx) || (addend && !aligned16(addend)))
+    return set_error(DECIK_ERR_INVALID, "%s: dy, x, addend, dx must be 16-byte aligned", what);
   const int grid = static_cast<int>((n_rows + 7) / 8);
   const cudaStream_t st = as_stream(stream);
   if (w_dtype != DECIK_F32 && w_dtype != DECIK_F16)
-    return set_error(DECIK_ERR_INVALID, "rmsnorm_bwd: w_dtype must be F32 or F16");
+    return set_error(DECIK_ERR_INVALID, "%s: w_dtype must be F32 or F16", what);
   const bool wf = w_dtype == DECIK_F32;
   if (n_cols == 12 * 128) {
-    if (wf) rmsnorm_bwd_reg_kernel<float, 12><<<grid, 256, 0, st>>>(dy, x, static_cast<const float*>(w), rstd, dx, n_rows);
-    else rmsnorm_bwd_reg_kernel<__half, 12><<<grid, 256, 0, st>>>(dy, x, static_cast<const __half*>(w), rstd, dx, n_rows);
+    if (wf) rmsnorm_bwd_reg_kernel<float, 12><<<grid, 256, 0, st>>>(dy, x, static_cast<const float*>(w), rstd, addend, dx, n_rows);
+    else rmsnorm_bwd_reg_kernel<__half, 12><<<grid, 256, 0, st>>>(dy, x, static_cast<const __half*>(w), rstd, addend, dx, n_rows);
   } else if (wf) {
-    rmsnorm_bwd_kernel<float><<<grid, 256, 0, st>>>(dy, x, static_cast<const float*>(w), rstd, dx, n_rows, n_cols);
+    rmsnorm_bwd_kernel<float><<<grid, 256, 0, st>>>(dy, x, static_cast<const float*>(w), rstd, addend, dx, n_rows, n_cols);
   } else {
-    rmsnorm_bwd_kernel<__half><<<grid, 256, 0, st>>>(dy, x, static_cast<const __half*>(w), rstd, dx, n_rows, n_cols);
+    rmsnorm_bwd_kernel<__half><<<grid, 256, 0, st>>>(dy, x, static_cast<const __half*>(w), rstd, addend, dx, n_rows, n_cols);
   }
-  return check_launch("rmsnorm_bwd");
+  return check_launch(what);
+}
+
+}  // namespace
+}  // namespace decik
+
+extern "C" int decik_rmsnorm_bwd(const float* dy, const float* x, const void* w, int w_dtype,
+                                 const float* rstd, float* dx, int64_t n_rows, int n_cols,
+                                 void* stream) {
+  return decik::rmsnorm_bwd_impl(dy, x, w, w_dtype, rstd, nullptr, dx, n_rows, n_cols, stream, "rmsnorm_bwd");
+}
+
+extern "C" int decik_rmsnorm_bwd_add(const float* dy, const float* x, const void* w, int w_dtype, const float* rstd,
+                                     const float* addend, float* dx, int64_t n_rows, int n_cols, void* stream) {
+  return decik::rmsnorm_bwd_impl(dy, x, w, w_dtype, rstd, addend, dx, n_rows, n_cols, stream, "rmsnorm_bwd_add");
 }
 
 namespace decik {

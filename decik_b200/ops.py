@@ -243,14 +243,22 @@ def rmsnorm_fwd(x2: torch.Tensor, w: torch.Tensor, eps: float, want_rstd: bool =
     return y, rstd
 
 
-def rmsnorm_bwd(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor, rstd: torch.Tensor):
-    _cuda(dy2, x2, w, rstd)
+def rmsnorm_bwd(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor, rstd: torch.Tensor,
+                addend: torch.Tensor | None = None):
+    """The RMSNorm input gradient [n, c] fp32; with ``addend`` (fp32 [n, c]) it is added in the same
+    pass (decik_rmsnorm_bwd_add): addend + norm_bwd, one rounding, as autograd's sum."""
+    _cuda(dy2, x2, w, rstd, addend)
     n, c = x2.shape
     dy2 = dy2.contiguous()
     x2 = x2.contiguous()
     dx = torch.empty((n, c), dtype=torch.float32, device=x2.device)
-    rc = _lib.lib().decik_rmsnorm_bwd(_p(dy2), _p(x2), _p(w.contiguous()), _dt(w), _p(rstd), _p(dx), n, c,
-                                      _stream(x2))
+    if addend is None:
+        rc = _lib.lib().decik_rmsnorm_bwd(_p(dy2), _p(x2), _p(w.contiguous()), _dt(w), _p(rstd), _p(dx), n, c,
+                                          _stream(x2))
+    else:
+        a2 = addend.reshape(n, c).contiguous().float()
+        rc = _lib.lib().decik_rmsnorm_bwd_add(_p(dy2), _p(x2), _p(w.contiguous()), _dt(w), _p(rstd), _p(a2), _p(dx),
+                                              n, c, _stream(x2))
     _lib.check(rc, "rmsnorm_bwd")
     return dx
 

@@ -21,6 +21,7 @@ from ._state import STATE, on_gpu
 
 # keyword under which the patched decoder layer hands its input RMSNorm to the patched attention
 INPUT_NORM_KW = "decik_input_norm"
+RESIDUAL_LINK_KW = "decik_residual_link"
 
 
 class FusedQKRope(torch.autograd.Function):
@@ -67,12 +68,17 @@ class FusedAttentionBlock(torch.autograd.Function):
     the layer input h and the norm runs inside the forward's first kernel
     (decik_qkv_proj_norm_fwd: the norm's fp32 output is never written); the backward applies the
     norm's backward (decik_rmsnorm_bwd, from the kept rstd) to dX and returns the gradient for h.
-    The LoRA gradients use the kept x16, so there is no norm recompute (solution/attn.py:238)."""
+    The LoRA gradients use the kept x16, so there is no norm recompute (solution/attn.py:238).
+    With ``residual_link`` (rmsnorm.ResidualGradLink, armed here) h's gradient from the residual
+    stream, left there by the layer's AddRMSNormFn, is added in the same pass."""
 
     @staticmethod
     def forward(ctx, x, a_q, b_q, a_v, b_v, w_cat, bias_cat, cos, sin, cu_seqlens, max_len, n_heads,
-                n_kv, scaling, scale, w_o=None, b_o=None, norm_w=None, norm_eps=0.0):
+                n_kv, scaling, scale, w_o=None, b_o=None, norm_w=None, norm_eps=0.0, residual_link=None):
         dt = w_cat.dtype
+        ctx.link = residual_link if norm_w is not None else None
+        if ctx.link is not None:
+            ctx.link.armed = True
         D = cos.shape[-1]
         r = a_q.shape[0]
         n_proj = (n_heads + 2 * n_kv) * D
@@ -112,8 +118,8 @@ class FusedAttentionBlock(torch.autograd.Function):
         dx = ops.proj_dx(dy, ops.transpose16(w_cat))
         da, db = ops.lora_grads(dy, x16, u, scaling, n_heads, n_kv)
         if norm_w is not None:  # through the input norm: the gradient for the layer input h
-            dx = ops.rmsnorm_bwd(dx, h, norm_w, rstd)
-        return (dx, da[:r], db[:n_q], da[r:], db[n_q:]) + (None,) * 14
+            dx = ops.rmsnorm_bwd(dx, h, norm_w, rstd, addend=None if ctx.link is None else ctx.link.take())
+        return (dx, da[:r], db[:n_q], da[r:], db[n_q:]) + (None,) * 15
 
 
 def pack_keep(keep_q, keep_v):
@@ -277,7 +283,7 @@ def _nf4_parts(module, n_in, dtype):
 
 
 def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim, o_nf4=False,
-                 input_norm=None):
+                 input_norm=None, residual_link=None):
     """(output, o_proj applied) through FusedAttentionBlock, or None when this layer does not
     qualify: both LoRA branches without dropout, rank 16 and one scaling; q, k, v NF4 linears of the
     compute dtype; the varlen attention switched on; head_dim 128. With ``o_nf4`` (o_proj is a plain
@@ -319,7 +325,8 @@ def _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_k
                                     packing.cu_seqlens(x.device), packing.max_len, n_heads, n_kv, pq[2],
                                     self.scaling, w_o, b_o,
                                     None if input_norm is None else input_norm.weight,
-                                    0.0 if input_norm is None else float(input_norm.variance_epsilon))
+                                    0.0 if input_norm is None else float(input_norm.variance_epsilon),
+                                    residual_link)
     return out.reshape(1, n_tok, -1), w_o is not None
 
 
@@ -352,6 +359,7 @@ def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None, fused_blo
         # the norm's output) so that the fused block runs the norm in its first kernel; any other
         # path applies the norm here first
         input_norm = kwargs.pop(INPUT_NORM_KW, None)
+        residual_link = kwargs.pop(RESIDUAL_LINK_KW, None)
         packing = STATE.packing
         q_name = _single_lora(getattr(self, "q_proj", None), lora_classes)
         v_name = _single_lora(getattr(self, "v_proj", None), lora_classes)
@@ -380,7 +388,8 @@ def patch(recompute_lora=True, linear4bit_cls=None, lora_classes=None, fused_blo
         x = hidden_states
         if fused_block:
             res = _fused_block(self, x, q_name, v_name, cos, sin, packing, dtype, n_heads, n_kv, head_dim,
-                               o_nf4=nf4_linear(getattr(self, "o_proj", None)), input_norm=input_norm)
+                               o_nf4=nf4_linear(getattr(self, "o_proj", None)), input_norm=input_norm,
+                               residual_link=residual_link)
             if res is not None:
                 out, o_done = res
                 return (out if o_done else self.o_proj(out)), None

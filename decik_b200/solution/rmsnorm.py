@@ -50,6 +50,22 @@ class RMSNormFn(torch.autograd.Function):
         return dx.view(ctx.shape), None, None
 
 
+class ResidualGradLink:
+    """Hands the residual path's gradient of a decoder layer's input to the fused attention block
+    of the same layer, which adds it inside its input norm's backward (decik_rmsnorm_bwd_add)
+    instead of autograd summing the two in a separate pass. The block arms the link in its forward
+    (so only a block that will consume it gets one); AddRMSNormFn's backward, which runs before the
+    block's, leaves the gradient here and returns none for its residual input."""
+
+    def __init__(self):
+        self.armed = False
+        self.grad = None
+
+    def take(self):
+        g, self.grad = self.grad, None
+        return g
+
+
 class AddRMSNormFn(torch.autograd.Function):
     """``h = residual + delta; y = norm(h)``, both returned (solution/rmsnorm.py:108-144). h is not
     kept for backward: it is rebuilt from the residual (the layer input, kept by the input norm
@@ -59,13 +75,15 @@ class AddRMSNormFn(torch.autograd.Function):
 
     With ``y16`` y comes out in delta's 16-bit dtype, for a consumer that computes in it (the patched
     MLP, whose first step is that cast): the fp32 y is never written, and y's gradient arrives in
-    the same dtype and is read as it is."""
+    the same dtype and is read as it is. With an armed ``link`` (ResidualGradLink) the residual
+    input's gradient goes to the link rather than to autograd."""
 
     @staticmethod
-    def forward(ctx, residual, delta, weight, eps, y16=False):
+    def forward(ctx, residual, delta, weight, eps, y16=False, link=None):
         h, y, rstd = ops.add_rmsnorm_fwd(residual, delta, weight, eps, y16=y16)
         ctx.save_for_backward(residual, delta, weight, rstd)
         ctx.eps = eps
+        ctx.link = link if (link is not None and link.armed) else None
         return h, y
 
     @staticmethod
@@ -73,10 +91,14 @@ class AddRMSNormFn(torch.autograd.Function):
         residual, delta, weight, rstd = ctx.saved_tensors
         if grad_y is None:
             if grad_h is None:
-                return None, None, None, None, None
-            return grad_h, grad_h.to(delta.dtype), None, None, None
-        total, total16 = ops.add_rmsnorm_bwd(grad_y, grad_h, residual, delta, weight, rstd)
-        return total, total16, None, None, None
+                return None, None, None, None, None, None
+            total, total16 = grad_h, grad_h.to(delta.dtype)
+        else:
+            total, total16 = ops.add_rmsnorm_bwd(grad_y, grad_h, residual, delta, weight, rstd)
+        if ctx.link is not None:
+            ctx.link.grad = total
+            total = None
+        return total, total16, None, None, None, None
 
 
 def fusable(module, x):

@@ -281,7 +281,7 @@ def _packed_sdpa(original, varlen_attention):
 
 def _decoder_layer(original, fuse_residual, fuse_input_norm=True):
     from . import rmsnorm
-    from .attn import INPUT_NORM_KW
+    from .attn import INPUT_NORM_KW, RESIDUAL_LINK_KW
 
     def forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
                 use_cache=False, position_embeddings=None, **kwargs):
@@ -300,10 +300,14 @@ def _decoder_layer(original, fuse_residual, fuse_input_norm=True):
                 and rmsnorm.fusable(norm_in, layer_in)):
             # the patched attention takes the layer input and its norm: the fused block then runs
             # the norm inside its first kernel (any other path applies it first)
+            # the link carries layer_in's residual gradient into the block's norm backward (armed
+            # only if the fused block ran)
+            link = rmsnorm.ResidualGradLink()
             attn, _ = self.self_attn(hidden_states=layer_in, attention_mask=None, position_ids=position_ids,
-                                     past_key_values=None, use_cache=False,
-                                     position_embeddings=position_embeddings, **{INPUT_NORM_KW: norm_in}, **kwargs)
+                                     past_key_values=None, use_cache=False, position_embeddings=position_embeddings,
+                                     **{INPUT_NORM_KW: norm_in, RESIDUAL_LINK_KW: link}, **kwargs)
         else:
+            link = None
             attn, _ = self.self_attn(hidden_states=norm_in(layer_in), attention_mask=None,
                                      position_ids=position_ids, past_key_values=None, use_cache=False,
                                      position_embeddings=position_embeddings, **kwargs)
@@ -314,7 +318,7 @@ def _decoder_layer(original, fuse_residual, fuse_input_norm=True):
             # dtype: its cast of an fp32 y (and the fp32 y itself) is then never made
             eligible = getattr(type(self.mlp).forward, "_skc_eligible", None)
             y16 = eligible is not None and eligible(self.mlp, attn) == attn.dtype
-            mid, normed = rmsnorm.AddRMSNormFn.apply(layer_in, attn, post_norm.weight, eps, y16)
+            mid, normed = rmsnorm.AddRMSNormFn.apply(layer_in, attn, post_norm.weight, eps, y16, link)
             STATE.norm_link = (normed, (layer_in, attn), post_norm.weight, eps)
         else:
             mid = layer_in + attn

@@ -242,6 +242,12 @@ DECIK_API int decik_rmsnorm_fwd(const float* x, const void* w, int w_dtype, floa
                       void* stream);
 DECIK_API int decik_rmsnorm_bwd(const float* dy, const float* x, const void* w, int w_dtype,
                       const float* rstd, float* dx, int64_t n_rows, int n_cols, void* stream);
+/* decik_rmsnorm_bwd plus an fp32 addend [n_rows, n_cols] (16-byte aligned): dx = addend +
+ * norm_bwd(dy, x), the one fp32 rounding of the sum autograd forms when x also reaches the loss by
+ * another path (the decoder layer's residual stream: the input norm's gradient plus the residual
+ * gradient of the layer input, in one pass instead of a separate add). */
+DECIK_API int decik_rmsnorm_bwd_add(const float* dy, const float* x, const void* w, int w_dtype, const float* rstd,
+                      const float* addend, float* dx, int64_t n_rows, int n_cols, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * The decoder's residual add + post-attention RMSNorm, one pass each way.

@@ -273,6 +273,22 @@ def test_add_rmsnorm_equals_unfused_kernels(cuda_lib, rows, cols, dtype):
 
 
 @pytest.mark.parametrize("rows,cols", [(1, 256), (1000, 1536), (5, 8192)])
+@pytest.mark.parametrize("wdtype", [torch.float32, torch.float16])
+def test_rmsnorm_bwd_with_addend(cuda_lib, rows, cols, wdtype):
+    """decik_rmsnorm_bwd_add equals the separate norm backward plus the addend (one fp32 add per
+    element, as autograd's sum of the two gradients), bit for bit."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(rows * 7 + cols)
+    x = (torch.randn(rows, cols, generator=g) * 2).to(DEV)
+    w = (torch.rand(cols, generator=g) + 0.5).to(wdtype).to(DEV)
+    dy = torch.randn(rows, cols, generator=g).to(DEV)
+    add = torch.randn(rows, cols, generator=g).to(DEV)
+    _, rstd = ops.rmsnorm_fwd(x, w, 1e-6)
+    assert torch.equal(ops.rmsnorm_bwd(dy, x, w, rstd, addend=add), add + ops.rmsnorm_bwd(dy, x, w, rstd))
+    assert cuda_lib.decik_kernel_error(1) == 0
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 256), (1000, 1536), (5, 8192)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("wdtype", [torch.float32, torch.float16])
 def test_add_rmsnorm_16bit_y_and_dy(cuda_lib, rows, cols, dtype, wdtype):

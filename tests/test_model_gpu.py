@@ -130,13 +130,24 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
             return orig[name](ctx, *a)
         return staticmethod(fwd)
 
+    # the fused layers' input-norm backward takes the residual stream's gradient of the layer input
+    # as its addend (rmsnorm.ResidualGradLink) instead of autograd summing the two
+    from decik_b200 import ops
+    orig_bwd, added = ops.rmsnorm_bwd, []
+
+    def counting_bwd(*a, **kw):
+        added.append(kw.get("addend") is not None)
+        return orig_bwd(*a, **kw)
+
     try:
         for n, c in fns:
             c.forward = counting(n)
+        ops.rmsnorm_bwd = counting_bwd
         l1, g1, packed1 = _step(model, batch, _state.STATE, dtype)
     finally:
         for n, c in fns:
             c.forward = orig[n]
+        ops.rmsnorm_bwd = orig_bwd
     assert packed1
     n_layers = len(model.model.layers)
     # without LoRA dropout every layer runs as one fused node (o_proj and the input norm included);
@@ -146,6 +157,7 @@ def test_patched_qwen2_matches_original(cuda_lib, patched_classes, lengths, lora
     assert calls == {"rope": chain, "varlen": chain, "pair": chain, "fused": n_layers - chain,
                      "addnorm": n_layers, "mlp": n_layers, "nf4linear": 4 * chain,
                      "rmsnorm": chain + 1}, calls
+    assert sum(added) == n_layers - chain, added
     print(f"loss {l0.item():.6f} -> {l1.item():.6f}")
     assert abs(l1.item() - l0.item()) / abs(l0.item()) < 2e-3, (l1.item(), l0.item())
     assert set(g1) == set(g0)
