@@ -12,28 +12,46 @@ namespace {
 // backward
 // ------------------------------------------------------------------------------------------------
 // delta[h, t] = sum_d dO * O (fp32), dq_acc = 0 and, when dK / dV are reduced in fp32, their
-// accumulators = 0. One warp per (token, head), 4 dims per lane.
+// accumulators = 0. kPrepItems (token, head) rows per warp, 4 dims per lane.
+constexpr int kPrepItems = 4;  // (token, head) rows per warp in the prep kernel
+
 template <typename T>
 __global__ void __launch_bounds__(256)
 attn_bwd_prep_kernel(Tensor3 dout, Tensor3 out, float* __restrict__ delta, float* __restrict__ dq_acc,
                      float* __restrict__ dk_acc, float* __restrict__ dv_acc, int64_t n_tok, int n_heads, int n_kv) {
+  // kPrepItems (token, head) rows per warp, all their loads issued before any arithmetic (one row
+  // per warp left too few bytes in flight: ~0.68 of HBM); lane l holds dims 4l .. 4l + 3 of a row
   const int lane = threadIdx.x & 31;
-  const int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (item >= n_tok * n_heads) return;
-  const int64_t tok = item / n_heads;
-  const int h = static_cast<int>(item % n_heads);
-  const uint2 a = *reinterpret_cast<const uint2*>(static_cast<const T*>(dout.ptr) + tok * dout.tok + h * dout.head + lane * 4);
-  const uint2 b = *reinterpret_cast<const uint2*>(static_cast<const T*>(out.ptr) + tok * out.tok + h * out.head + lane * 4);
-  float acc = Dt<T>::lo_f(a.x) * Dt<T>::lo_f(b.x) + Dt<T>::hi_f(a.x) * Dt<T>::hi_f(b.x) +
-              Dt<T>::lo_f(a.y) * Dt<T>::lo_f(b.y) + Dt<T>::hi_f(a.y) * Dt<T>::hi_f(b.y);
+  const int64_t first = (static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * kPrepItems;
+  const int64_t n_items = n_tok * n_heads;
+  uint2 a[kPrepItems], b[kPrepItems];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) delta[static_cast<int64_t>(h) * n_tok + tok] = acc;
-  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-  reinterpret_cast<float4*>(dq_acc + (tok * n_heads + h) * D)[lane] = z;
-  if (dk_acc != nullptr && h < n_kv) {
-    reinterpret_cast<float4*>(dk_acc + (tok * n_kv + h) * D)[lane] = z;
-    reinterpret_cast<float4*>(dv_acc + (tok * n_kv + h) * D)[lane] = z;
+  for (int i = 0; i < kPrepItems; ++i) {
+    const int64_t item = first + i;
+    if (item < n_items) {
+      const int64_t tok = item / n_heads;
+      const int h = static_cast<int>(item % n_heads);
+      a[i] = *reinterpret_cast<const uint2*>(static_cast<const T*>(dout.ptr) + tok * dout.tok + h * dout.head + lane * 4);
+      b[i] = *reinterpret_cast<const uint2*>(static_cast<const T*>(out.ptr) + tok * out.tok + h * out.head + lane * 4);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPrepItems; ++i) {
+    const int64_t item = first + i;
+    if (item >= n_items) break;  // uniform across the warp
+    const int64_t tok = item / n_heads;
+    const int h = static_cast<int>(item % n_heads);
+    float acc = Dt<T>::lo_f(a[i].x) * Dt<T>::lo_f(b[i].x) + Dt<T>::hi_f(a[i].x) * Dt<T>::hi_f(b[i].x) +
+                Dt<T>::lo_f(a[i].y) * Dt<T>::lo_f(b[i].y) + Dt<T>::hi_f(a[i].y) * Dt<T>::hi_f(b[i].y);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) delta[static_cast<int64_t>(h) * n_tok + tok] = acc;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    reinterpret_cast<float4*>(dq_acc + (tok * n_heads + h) * D)[lane] = z;
+    if (dk_acc != nullptr && h < n_kv) {
+      reinterpret_cast<float4*>(dk_acc + (tok * n_kv + h) * D)[lane] = z;
+      reinterpret_cast<float4*>(dv_acc + (tok * n_kv + h) * D)[lane] = z;
+    }
   }
 }
 
@@ -170,7 +188,7 @@ int varlen_attn_bwd_core(const decik_tensor3& dout, const decik_tensor3& q, cons
   *acc_out = BwdAcc{dq_acc, dk_acc, dv_acc, n_split};
   return DECIK_DISPATCH_16(dtype, [&] {
     const int64_t items = n_tok * n_heads;
-    attn_bwd_prep_kernel<T><<<static_cast<unsigned>((items + 7) / 8), 256, 0, s>>>(
+    attn_bwd_prep_kernel<T><<<static_cast<unsigned>((items + 8 * kPrepItems - 1) / (8 * kPrepItems)), 256, 0, s>>>(
         Tensor3{dout.ptr, dout.tok_stride, dout.head_stride}, Tensor3{out.ptr, out.tok_stride, out.head_stride},
         delta, dq_acc, dk_acc, dv_acc, n_tok, n_heads, n_kv);
     int rc = check_launch("varlen_attn_bwd prep");
