@@ -275,15 +275,16 @@ def add_rmsnorm_fwd(residual: torch.Tensor, delta: torch.Tensor, w: torch.Tensor
     d2 = delta.reshape(-1, n_cols).contiguous()
     if y16 and d2.dtype not in (torch.float16, torch.bfloat16):
         raise RuntimeError("decik_b200 add_rmsnorm_fwd: a 16-bit y needs a 16-bit delta")
-    h = torch.empty_like(r2)
-    y = torch.empty_like(d2) if y16 else torch.empty_like(r2)
+    # h and y in the caller's shape (not views: the decoder layer's stream h may be updated in place)
+    h = torch.empty(residual.shape, dtype=torch.float32, device=r2.device)
+    y = torch.empty(residual.shape, dtype=d2.dtype if y16 else torch.float32, device=r2.device)
     rstd = torch.empty(r2.shape[0], dtype=torch.float32, device=r2.device)
     fn = _lib.lib().decik_add_rmsnorm_fwd16 if y16 else _lib.lib().decik_add_rmsnorm_fwd
     with _timed("add_rmsnorm_fwd", 1):
         rc = fn(_p(r2), _p(d2), _dt(d2), _p(w.contiguous()), _dt(w), _p(h), _p(y), _p(rstd), r2.shape[0], n_cols,
                 float(eps), _stream(r2))
     _lib.check(rc, "add_rmsnorm_fwd")
-    return h.view(residual.shape), y.view(residual.shape), rstd
+    return h, y, rstd
 
 
 def add_rmsnorm_bwd(dy, grad_h, residual, delta, w, rstd, want_dx16: bool = True):

@@ -42,7 +42,9 @@ class FusedMLP(torch.autograd.Function):
     With ``residual`` (the decoder layer's fp32 stream, x's shape) the node returns
     residual + mlp(x) in fp32 from the down projection's GEMM (beta = 1, fp32 output): the layer's
     residual add (solution/varlen.py:343) needs no pass of its own, and the MLP output is added
-    before any 16-bit rounding. The residual's gradient is the output's."""
+    before any 16-bit rounding. The residual's gradient is the output's. A contiguous residual that
+    is not a leaf requiring grad is updated in place and returned (marked dirty): the patched
+    decoder layer's stream, which no node keeps for backward."""
 
     @staticmethod
     def forward(ctx, x, w_gu, w_down, residual=None):
@@ -50,13 +52,20 @@ class FusedMLP(torch.autograd.Function):
         shape = x.shape
         x16 = x.reshape(-1, shape[-1]).to(w_gu.dtype).contiguous()
         gu, hidden = ops.mlp_gate_up(x16, w_gu)            # [T, 2 * inter], [T, inter]
-        if residual is None:
-            out = torch.mm(hidden, w_down.t())             # [T, hidden], plain GEMM
-        else:
-            out = torch.addmm(residual.reshape(-1, residual.shape[-1]), hidden, w_down.t(), out_dtype=torch.float32)
         ctx.save_for_backward(gu, w_gu, w_down)
         ctx.in_dtype, ctx.shape, ctx.inter = x.dtype, shape, inter
         ctx.residual = residual is not None
+        if residual is None:
+            out = torch.mm(hidden, w_down.t())             # [T, hidden], plain GEMM
+            return out.view(*shape[:-1], out.shape[-1])
+        r2 = residual.reshape(-1, residual.shape[-1])
+        if residual.is_contiguous() and not (residual.is_leaf and residual.requires_grad):
+            # into the residual itself (no node keeps it): addmm into a new tensor first copies the
+            # residual there (330.7 -> 293.9 us at 16,384 tokens, same bits)
+            torch.addmm(r2, hidden, w_down.t(), out_dtype=torch.float32, out=r2)
+            ctx.mark_dirty(residual)
+            return residual
+        out = torch.addmm(r2, hidden, w_down.t(), out_dtype=torch.float32)
         return out.view(*shape[:-1], out.shape[-1])
 
     @staticmethod

@@ -154,4 +154,14 @@ def test_fused_mlp_with_residual(cuda_lib):
     assert torch.equal(ra.grad, grad)
     rel = ((xa.grad - xb.grad).norm() / xb.grad.norm()).item()
     assert rel < 1e-5, rel  # the same kernels on the same 16-bit gradient
+    # a residual that is not a leaf (the decoder layer's stream) is updated in place: the same
+    # values as into a new tensor, and the same gradients
+    rl = res.clone().requires_grad_(True)
+    rc = rl * 1.0
+    xc = x.clone().requires_grad_(True)
+    out_c = FusedMLP.apply(xc, w_gu, w_down, rc)
+    assert out_c.data_ptr() == rc.data_ptr() and torch.equal(out_c, out)
+    out_c.backward(grad)
+    assert torch.equal(rl.grad, grad)
+    assert ((xc.grad - xa.grad).norm() / xa.grad.norm()).item() < 1e-6
     assert cuda_lib.decik_kernel_error(1) == 0
